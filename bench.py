@@ -1,0 +1,389 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 INT8 hot path (BASELINE metric: INT8 TOPS of the W8A8 GEMM and the INT8
+attention vs the B200 dense INT8 peak).
+
+Headline workload: INT8 flash attention, B=1, H=24, S=4608, D=128, bf16,
+non-causal, Q and K quantized per 64-token block (mode "block64"), softmax scale 1/sqrt(128).
+One step = the whole attention call (Q/K quantization + the tcgen05 kernel) on one batch.
+value = whole-job INT8 TOPS = 4*B*H*S^2*D ops per step * steps * N / max-over-ranks time.
+The same line carries the W8A8 GEMM of config 1 (M=4096, K=N=3072, bf16 out with bias), the
+activation quantizer's GB/s, the reference-mode attention, the roofline of the dominant kernel,
+the CPU baseline (the oracle port timed on this host), clocks and the end-to-end number through
+the public API with host buffers.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs under torch.distributed.run, one rank per GPU, each rank its own batch (weak scaling,
+no data-path collective: attention batches are independent).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+B, H, S, D = 1, 24, 4608, 128
+ATTN_OPS = 4 * B * H * S * S * D                     # QK^T (int8) + PV (bf16), 2 ops per MAC
+GEMM_M, GEMM_N, GEMM_K = 4096, 3072, 3072
+GEMM_OPS = 2 * GEMM_M * GEMM_N * GEMM_K
+METRIC = "INT8 TOPS, INT8 flash attention (BASELINE config 2: B=1, H=24, S=4608, D=128, bf16)"
+CONFIG = {"workload": "int8_flash_attention_config2", "batch": B, "heads": H, "seq_len": S, "head_dim": D,
+          "quant": "per-64-token-block Q and K (block64)", "causal": False,
+          "l2": "4 rotating input sets (4 x 85 MB > 126 MB L2)", "parallelism": "replicas (weak scaling)"}
+
+
+def _peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        p = json.loads(path.read_text())
+        return {"bf16_tflops": float(p["bf16_tflops"]), "hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+    return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def _int8_peak_tops(peaks: dict) -> float:
+    # B200 dense INT8 runs at twice the dense BF16 rate (4.5 vs 2.25 P nominal).
+    return 2.0 * peaks["bf16_tflops"]
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling while the GPU is under load."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, out_path: Path | None = None):
+        self.gpu_index, self.proc, self.out_path = gpu_index, None, out_path
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if self.out_path is not None:
+            self.out_path.write_text(out)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        smax = float(rows[0][2])
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows)}
+
+
+def _dist():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ─── CPU side: the oracle port of the reference's path ──────────────────────────────────
+
+def _cpu_attention_sample(rows: int, threads: int, mode: str = "block64") -> tuple[float, int]:
+    """Seconds for the oracle's int8 attention over ``rows`` query rows of one head against all S
+    keys (same shapes / distributions as config 2). Returns (seconds, ops)."""
+    import numpy as np
+    import oracle
+    oracle.set_threads(threads)
+    rng = np.random.default_rng(0)
+    q = oracle.to_bits(rng.standard_normal((1, rows, 1, D), dtype=np.float32), "bf16")
+    k = oracle.to_bits(rng.standard_normal((1, S, 1, D), dtype=np.float32), "bf16")
+    v = oracle.to_bits(rng.standard_normal((1, S, 1, D), dtype=np.float32), "bf16")
+    t0 = time.perf_counter()
+    oracle.attn_int8(q, k, v, "bf16", D ** -0.5, mode)
+    return time.perf_counter() - t0, 4 * rows * S * D
+
+
+def _cpu_baseline(budget_s: float = 15.0) -> dict:
+    threads = os.cpu_count() or 1
+    rows = 64
+    t, ops = _cpu_attention_sample(rows, threads)
+    # grow the sample to roughly the time budget (bounded)
+    rows = int(max(64, min(S, rows * budget_s / max(t, 1e-3) / 4)) // 64 * 64)
+    t, ops = _cpu_attention_sample(rows, threads)
+    return {"value": ops / t / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"oracle int8 attention (block64), 1 head x {rows} query rows x {S} keys, D={D}, "
+                      f"{t:.2f} s", "cpu": _cpu_model()}
+
+
+def _cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args) -> int:
+    """The reference arm: the oracle port of the reference's CPU path on this host's cores,
+    rank 0 only, each step a bounded sample of config 2."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    t1, _ = _cpu_attention_sample(64, threads)
+    total_budget = 150.0
+    per_step = max(0.05, min(2.0, total_budget / max(1, args.steps + args.warmup)))
+    rows = int(max(64, min(S, 64 * per_step / max(t1, 1e-4))) // 64 * 64)
+    for _ in range(args.warmup):
+        _cpu_attention_sample(rows, threads)
+    secs, ops = 0.0, 0
+    for _ in range(args.steps):
+        t, o = _cpu_attention_sample(rows, threads)
+        secs += t
+        ops += o
+    value = ops / secs / 1e12
+    sample = f"oracle int8 attention (block64), 1 head x {rows} query rows x {S} keys, D={D} per step"
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/bf16",
+            "data": "synthetic N(0,1), seeded", "config": CONFIG,
+            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample,
+                             "cpu": _cpu_model()},
+            "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ─── GPU side ───────────────────────────────────────────────────────────────────────────
+
+def _events(n):
+    import torch
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+
+def bench_attention(args, world, mode_code, sets, plan, out, sampler=None):
+    """Times K steps of prep + main over rotating input sets. Returns dict of timings (ms)."""
+    import torch
+    scale = D ** -0.5
+    for i in range(args.warmup):
+        q, k, v = sets[i % len(sets)]
+        plan(q, k, v, out, scale)
+    torch.cuda.synchronize()
+    if sampler is not None:
+        # clock soak: the same step for ~1 s right before the timed region, sampled with it
+        sampler.start()
+        t_end = time.perf_counter() + 1.0
+        i = 0
+        while time.perf_counter() < t_end:
+            q, k, v = sets[i % len(sets)]
+            plan(q, k, v, out, scale)
+            i += 1
+            if i % 50 == 0:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+    ev = _events(3 * args.steps)
+    start, end = _events(2)
+    _barrier(world)
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(args.steps):
+        q, k, v = sets[i % len(sets)]
+        ev[3 * i].record()
+        plan.prep(q, k)
+        ev[3 * i + 1].record()
+        plan.main(v, out, scale)
+        ev[3 * i + 2].record()
+    end.record()
+    torch.cuda.synchronize()
+    _barrier(world)
+    clocks = sampler.stop() if sampler is not None else None
+    total = start.elapsed_time(end)
+    prep = sum(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(args.steps))
+    main = sum(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(args.steps))
+    return {"total_ms": total, "prep_ms": prep / args.steps, "main_ms": main / args.steps, "clocks": clocks}
+
+
+def bench_e2e(args, dev):
+    """The same metric through the public API (attention_bhld) with pinned host inputs copied in
+    and the output copied back inside the timed region."""
+    import torch
+    from diffucore_b200 import _attention
+    g = torch.Generator().manual_seed(1)
+    host = [torch.randn(B, H, S, D, generator=g).to(torch.bfloat16).pin_memory() for _ in range(3)]
+    host_out = torch.empty(B, S, H * D, dtype=torch.bfloat16).pin_memory()
+
+    def step():
+        q, k, v = (t.to(dev, non_blocking=True) for t in host)
+        o = _attention.attention_bhld(q, k, v, "int8_turing", quant_mode="block64")
+        host_out.copy_(o, non_blocking=True)
+
+    for _ in range(max(3, args.warmup // 4)):
+        step()
+    torch.cuda.synchronize()
+    n = max(3, min(args.steps, 50))
+    s, e = _events(2)
+    s.record()
+    for _ in range(n):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / n
+    return {"value": ATTN_OPS / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": ms,
+            "h2d_bytes_per_step": 3 * B * H * S * D * 2, "d2h_bytes_per_step": B * S * H * D * 2, "steps": n}
+
+
+def bench_gemm(args, dev, peaks):
+    """Config 1: W8A8 linear (quantize + tcgen05 GEMM with rescale/bias epilogue)."""
+    import torch
+    from diffucore_b200 import _int8, kernels
+    g = torch.Generator().manual_seed(0)
+    lin = torch.nn.Linear(GEMM_K, GEMM_N, bias=True).to(torch.bfloat16)
+    with torch.no_grad():
+        lin.weight.copy_((torch.randn(GEMM_N, GEMM_K, generator=g) * 0.02).to(torch.bfloat16))
+        lin.bias.copy_((torch.randn(GEMM_N, generator=g) * 0.01).to(torch.bfloat16))
+    layer = _int8.Int8Linear.from_linear(lin.to(dev), group=0)
+    nsets = 6                                               # 6 x (25 MB x + 13 MB q + 25 MB y) > L2
+    xs = [torch.randn(GEMM_M, GEMM_K, generator=g).to(torch.bfloat16).to(dev) for _ in range(nsets)]
+    qs = [kernels.quant_rows(x, 0) for x in xs]
+    steps = max(10, args.steps)
+    for i in range(max(3, args.warmup)):
+        q, s = qs[i % nsets]
+        layer.matmul_quantized(q, s, torch.bfloat16)
+        kernels.quant_rows(xs[i % nsets], 0)
+    torch.cuda.synchronize()
+    ev = _events(3 * steps)
+    for i in range(steps):
+        x = xs[i % nsets]
+        ev[3 * i].record()
+        q, s = kernels.quant_rows(x, 0)
+        ev[3 * i + 1].record()
+        layer.matmul_quantized(q, s, torch.bfloat16)
+        ev[3 * i + 2].record()
+    torch.cuda.synchronize()
+    quant_ms = sum(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(steps)) / steps
+    gemm_ms = sum(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(steps)) / steps
+    tops = GEMM_OPS / (gemm_ms * 1e-3) / 1e12
+    peak = _int8_peak_tops(peaks)
+    qbytes = GEMM_M * GEMM_K * 2 + GEMM_M * GEMM_K + GEMM_M * 4
+    qgbs = qbytes / (quant_ms * 1e-3) / 1e9
+    return {
+        "workload": "W8A8 linear, BASELINE config 1: M=4096, K=N=3072, bf16 in/out, bias, group 0",
+        "value": GEMM_OPS / ((quant_ms + gemm_ms) * 1e-3) / 1e12, "unit": "TOPS",
+        "ms_per_call": quant_ms + gemm_ms,
+        "gemm": {"ms": gemm_ms, "roofline": {"bound": "tensor", "achieved": tops, "peak": peak, "unit": "TOPS",
+                                             "frac": tops / peak, "traffic": None,
+                                             "peak_source": f"2 x bf16_tflops ({peaks['source']})"}},
+        "quantizer": {"ms": quant_ms, "roofline": {"bound": "hbm", "achieved": qgbs, "peak": peaks["hbm_gbs"],
+                                                   "unit": "GB/s", "frac": qgbs / peaks["hbm_gbs"],
+                                                   "traffic": None, "peak_source": f"hbm_gbs ({peaks['source']})"}},
+        "gpu_launches_per_call": 2,
+    }
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--no-extras", action="store_true", help="headline attention only (for profiling)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    from diffucore_b200 import _lib, kernels
+    world, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peaks = _peaks()
+
+    g = torch.Generator().manual_seed(0)
+    sets = []
+    for _ in range(4):
+        q, k, v = (torch.randn(B, H, S, D, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+        sets.append((q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)))   # (B, L, H, D) views of bhld
+    out = torch.empty(B, S, H, D, device=dev, dtype=torch.bfloat16)
+    plan = kernels.AttnPlan(B, H, S, S, D, torch.bfloat16, _lib.MODE_BLOCK64, dev)
+    sampler = ClockSampler(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv"
+                           if (ROOT / "gpurun_out").is_dir() else None)
+    t = bench_attention(args, world, _lib.MODE_BLOCK64, sets, plan, out, sampler)
+    total_s = _max_over_ranks(t["total_ms"] * 1e-3, world)
+    value = world * ATTN_OPS * args.steps / total_s / 1e12
+    main_tops = ATTN_OPS / (t["main_ms"] * 1e-3) / 1e12
+    peak = _int8_peak_tops(peaks)
+    line = {
+        "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_s * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 QK^T / bf16 PV",
+        "data": "synthetic N(0,1) bf16, seeded", "config": CONFIG,
+        "prep_ms": t["prep_ms"], "attn_kernel_ms": t["main_ms"],
+        "roofline": {"bound": "tensor", "achieved": main_tops, "peak": peak, "unit": "TOPS",
+                     "frac": main_tops / peak, "traffic": None,
+                     "peak_source": f"2 x bf16_tflops ({peaks['source']}); nominal dense INT8 4500 TOPS",
+                     "kernel": "attn_int8_kernel<128, bf16>"},
+        "clocks": t["clocks"],
+        "gpu_launches": 3 * args.steps,
+    }
+    if not args.no_extras:
+        ref_plan = kernels.AttnPlan(B, H, S, S, D, torch.bfloat16, _lib.MODE_REF, dev)
+        r = bench_attention(args, world, _lib.MODE_REF, sets, ref_plan, out)
+        line["ref_mode"] = {"value": ATTN_OPS / (r["total_ms"] / args.steps * 1e-3) / 1e12, "unit": "TOPS",
+                            "ms_per_step": r["total_ms"] / args.steps, "prep_ms": r["prep_ms"],
+                            "attn_kernel_ms": r["main_ms"]}
+        del ref_plan
+        line["w8a8_linear"] = bench_gemm(args, dev, peaks)
+        line["e2e"] = bench_e2e(args, dev)
+        if rank == 0 and world == 1:
+            line["cpu_baseline"] = _cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

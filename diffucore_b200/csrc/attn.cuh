@@ -1,0 +1,480 @@
+// INT8 flash attention for sm_100a: int8 Q.K^T on tcgen05 (kind::i8, int32 S in TMEM), fp32
+// online softmax (one thread owns one query row, so row max and row sum are thread-local),
+// bf16/fp16 P written back to TMEM, and P.V on tcgen05 (kind::f16, fp32 O in TMEM).
+//
+// Two quantization modes share the main kernel:
+//   kModeRef      the reference's scheme (src/diffucore/kernels/int8_attn_sm80.cu):
+//                 Q per token, K per 64-key block after subtracting K's per-channel mean.
+//   kModeBlock64  Q and K both per 64-token block, no mean (symmetric abs-max).
+// The prep kernels write contiguous int8 codes + fp32 scales into the caller's workspace; the
+// main kernel TMA-loads them. V is read in place from the caller's (B, L, H, D) strides.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+#include "sm100.cuh"
+#include "quant.cuh"
+
+namespace dc {
+
+enum AttnMode : int { kModeRef = 0, kModeBlock64 = 1 };
+
+constexpr int kAttnBM = 128;        // query rows per Q tile (one softmax warpgroup)
+constexpr int kAttnBN = 128;        // keys per K/V tile
+constexpr int kAttnKBlk = 64;       // keys per K scale block
+constexpr int kAttnRows = 256;      // query rows per CTA (two Q tiles)
+constexpr int kAttnThreads = 320;   // warps 0-7 softmax (2 x 4), warp 8 TMA, warp 9 MMA
+constexpr int kAttnStages = 3;
+constexpr int kStatWin = 128;       // rows per K-sum window (the reference's FLUSH_EVERY * BC)
+
+// ----------------------------------------------------------------------------- prep
+
+// Per-(b, h, window) partial K column sums in the reference's fixed order
+// (int8_attn_sm80.cu:92-135): thread (rg, ch) adds rows r0+rg, r0+rg+16, ... of its 8 channels;
+// the 16 row-group partials are then added in order rg = 0..15.
+template <typename T, int D>
+__global__ void __launch_bounds__(16 * (D / 8))
+k_stats_kernel(const T* __restrict__ k, float* __restrict__ kpart, int L, int H, int64_t sb, int64_t sl,
+               int64_t sh) {
+  constexpr int NCH = D / 8;
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int ch = threadIdx.x % NCH, rg = threadIdx.x / NCH;
+  const T* kb = k + b * sb + h * sh + ch * 8;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const int r0 = blockIdx.x * kStatWin, r1 = min(L, r0 + kStatWin);
+  for (int r = r0 + rg; r < r1; r += 16) {
+    float f[8];
+    Vec8<T>::load(kb + r * sl, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], f[i]);
+  }
+  __shared__ float red[16][D + 1];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[rg][ch * 8 + i] = acc[i];
+  __syncthreads();
+  if (threadIdx.x < D) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) s = __fadd_rn(s, red[i][threadIdx.x]);
+    kpart[(static_cast<int64_t>(b * H + h) * gridDim.x + blockIdx.x) * D + threadIdx.x] = s;
+  }
+}
+
+// ksum[bh, d] = sum over windows in order (int8_attn_sm80.cu:137-142).
+template <int D>
+__global__ void k_sum_kernel(const float* __restrict__ kpart, float* __restrict__ ksum, int nwin) {
+  const float* src = kpart + static_cast<int64_t>(blockIdx.x) * nwin * D + threadIdx.x;
+  float s = 0.f;
+  for (int w = 0; w < nwin; ++w) s = __fadd_rn(s, src[w * D]);
+  ksum[blockIdx.x * D + threadIdx.x] = s;
+}
+
+// Per-64-row block int8 codes: x' = x - ksum * (1/L) (as one fused multiply-add, the form the
+// reference's `f.x - ksum[..] * inv_l` takes under nvcc's default contraction,
+// int8_attn_sm80.cu:57-58) when `ksum` is given, else x' = x; amax over the 64 x D block;
+// scale = amax / 127; code = rn(x' * (127 / amax)), 0 when amax == 0 (:65-89).
+// Rows past L are zero. Grid (Lpad / 64, H, B), 256 threads. Writes codes to
+// codes[(bh * Lpad + row) * D], one scale per block to scales[bh * (Lpad / 64) + blk] and,
+// when row_scales != null, the block scale to every row: row_scales[bh * Lpad + row].
+template <typename T, int D>
+__global__ void __launch_bounds__(256)
+block_quant_kernel(const T* __restrict__ x, const float* __restrict__ ksum, int8_t* __restrict__ codes,
+                   float* __restrict__ scales, float* __restrict__ row_scales, int L, int H, int Lpad,
+                   int64_t sb, int64_t sl, int64_t sh) {
+  constexpr int NCH = D / 8;                        // 16-byte chunks per row
+  constexpr int PER = kAttnKBlk * NCH / 256;        // chunks per thread (4 or 2)
+  const int b = blockIdx.z, h = blockIdx.y, blk = blockIdx.x;
+  const int bh = b * H + h;
+  const float inv_l = __fdiv_rn(1.0f, static_cast<float>(L));
+  float vals[PER][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int ci = threadIdx.x + u * 256;
+    const int r = ci / NCH, c = ci % NCH;
+    const int row = blk * kAttnKBlk + r;
+    if (row < L) {
+      float f[8];
+      Vec8<T>::load(x + b * sb + row * sl + h * sh + c * 8, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        vals[u][i] = ksum != nullptr ? __fmaf_rn(-ksum[bh * D + c * 8 + i], inv_l, f[i]) : f[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) vals[u][i] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(vals[u][i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  __shared__ float wmax[8];
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = wmax[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) amax = fmaxf(amax, wmax[i]);
+  const float inv = amax > 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+  const float scale = __fdiv_rn(amax, 127.f);
+  if (threadIdx.x == 0 && scales != nullptr) scales[bh * (Lpad / kAttnKBlk) + blk] = scale;
+  if (row_scales != nullptr && threadIdx.x < kAttnKBlk)
+    row_scales[static_cast<int64_t>(bh) * Lpad + blk * kAttnKBlk + threadIdx.x] = scale;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int ci = threadIdx.x + u * 256;
+    const int r = ci / NCH, c = ci % NCH;
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      w0 |= static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(__fmul_rn(vals[u][i], inv))))) << (8 * i);
+      w1 |= static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(__fmul_rn(vals[u][i + 4], inv))))) << (8 * i);
+    }
+    int8_t* dst = codes + (static_cast<int64_t>(bh) * Lpad + blk * kAttnKBlk + r) * D + c * 8;
+    *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
+  }
+}
+
+// Per-token Q codes (int8_attn_sm80.cu:341-388): amax over the D channels of the row;
+// inv = amax > 0 ? 127 / amax : 0; code = rn(x * inv); row scale = amax / 127 (the softmax scale
+// is applied by the main kernel). NCH = D / 8 lanes per row; rows in [L, Lpad) are zero.
+template <typename T, int D>
+__global__ void __launch_bounds__(256)
+q_token_quant_kernel(const T* __restrict__ q, int8_t* __restrict__ codes, float* __restrict__ row_scales, int L,
+                     int H, int Lpad, int64_t total_rows, int64_t sb, int64_t sl, int64_t sh) {
+  constexpr int NCH = D / 8;
+  constexpr int ROWS_PER_CTA = 256 / NCH;
+  const int sub = threadIdx.x / NCH, c = threadIdx.x % NCH;
+  const int64_t grow = static_cast<int64_t>(blockIdx.x) * ROWS_PER_CTA + sub;   // (bh, row) flattened
+  const bool live = grow < total_rows;
+  const int bh = live ? static_cast<int>(grow / Lpad) : 0;
+  const int row = live ? static_cast<int>(grow % Lpad) : 0;
+  const int b = bh / H, h = bh % H;
+  float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (live && row < L) Vec8<T>::load(q + b * sb + row * sl + h * sh + c * 8, f);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+#pragma unroll
+  for (int o = NCH / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float inv = amax > 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+  uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    w0 |= static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(__fmul_rn(f[i], inv))))) << (8 * i);
+    w1 |= static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(__fmul_rn(f[i + 4], inv))))) << (8 * i);
+  }
+  if (live) {
+    *reinterpret_cast<uint2*>(codes + grow * D + c * 8) = make_uint2(w0, w1);
+    if (c == 0) row_scales[grow] = __fdiv_rn(amax, 127.f);
+  }
+}
+
+// ----------------------------------------------------------------------------- main kernel
+
+struct AttnParams {
+  int H, Lq, Lk, Lq_pad, Lk_pad, n_ktiles;
+  float scale_log2;            // softmax scale * log2(e)
+  const float* q_scale;        // [B*H, Lq_pad] per-row Q scale
+  const float* k_scale;        // [B*H, Lk_pad / 64] per-block K scale
+  void* o;                     // output, (B, Lq, H, D) with the strides below (elements)
+  int64_t o_sb, o_sl, o_sh;
+};
+
+template <int D>
+struct AttnSmem {
+  static constexpr int kQTile = kAttnBM * D;            // int8
+  static constexpr int kKTile = kAttnBN * D;            // int8
+  static constexpr int kVTile = kAttnBN * D * 2;        // 16-bit
+  static constexpr int kVHalf = kAttnBN * 64 * 2;       // one 64-column TMA box of V
+  static constexpr int kStage = kKTile + kVTile;
+  static constexpr int kBytes = 2 * kQTile + kAttnStages * kStage;
+  static constexpr int kDynamic = kBytes + 1024;
+  // Q/K rows are D bytes: 128-byte swizzle for D = 128, 64-byte swizzle for D = 64.
+  static constexpr uint32_t kQKSwizzle = D == 128 ? 2u : 4u;   // descriptor layout type
+  static constexpr uint32_t kQKAtom = D == 128 ? 1024u : 512u; // 8 rows
+};
+
+__device__ __forceinline__ uint64_t smem_desc_sw(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                                 uint32_t layout) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
+  return d;
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack_p(float a, float b) {
+  if (BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+constexpr int kMagicI = 0x4B400000;         // bits of 1.5 * 2^23
+constexpr float kMagicF = 12582912.0f;      // int32 s -> float(s) + 1.5 * 2^23 by an integer add
+constexpr float kLazyRescale = 8.0f;        // log2 headroom before O is rescaled
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
+                 const __grid_constant__ CUtensorMap tma_v, const AttnParams p) {
+  using SM = AttnSmem<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = smem;                                  // 2 Q tiles
+  uint8_t* sstage = smem + 2 * SM::kQTile;             // stages: K tile, then V (D / 64 boxes)
+
+  __shared__ __align__(8) uint64_t q_full;
+  __shared__ __align__(8) uint64_t k_full[kAttnStages];
+  __shared__ __align__(8) uint64_t v_full[kAttnStages];
+  __shared__ __align__(8) uint64_t kv_empty[kAttnStages];
+  __shared__ __align__(8) uint64_t s_ready[2];
+  __shared__ __align__(8) uint64_t p_ready[2];
+  __shared__ __align__(8) uint64_t pv_done[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = warp_id(), lane = lane_id();
+  const int qpair = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int bh = b * p.H + h;
+  const int n = p.n_ktiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < kAttnStages; ++s) {
+      mbar_init(&k_full[s], 1); mbar_init(&v_full[s], 1); mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) { mbar_init(&s_ready[i], 1); mbar_init(&p_ready[i], 128); mbar_init(&pv_done[i], 1); }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8 && lane == 0) { tma_prefetch_desc(&tma_q); tma_prefetch_desc(&tma_k); tma_prefetch_desc(&tma_v); }
+  if (warp == 9) { tmem_alloc(&tmem_slot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+  // TMEM columns: S0 [0,128), S1 [128,256) (P_i aliases the first 64 columns of S_i),
+  // O0 [256, 256 + D), O1 [256 + D, 256 + 2D).
+  constexpr uint32_t kOCol = 256;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      const int qrow0 = bh * p.Lq_pad + qpair * kAttnRows;
+      mbar_arrive_expect_tx(&q_full, 2 * SM::kQTile);
+      tma_load_2d(sq, &tma_q, &q_full, 0, qrow0);
+      tma_load_2d(sq + SM::kQTile, &tma_q, &q_full, 0, qrow0 + kAttnBM);
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j % kAttnStages;
+        const uint32_t ph = (j / kAttnStages) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort)) { ok = false; break; }
+        uint8_t* sk = sstage + st * SM::kStage;
+        uint8_t* sv = sk + SM::kKTile;
+        mbar_arrive_expect_tx(&k_full[st], SM::kKTile);
+        tma_load_2d(sk, &tma_k, &k_full[st], 0, bh * p.Lk_pad + j * kAttnBN);
+        mbar_arrive_expect_tx(&v_full[st], SM::kVTile);
+#pragma unroll
+        for (int dh = 0; dh < D / 64; ++dh)
+          tma_load_4d(sv + dh * SM::kVHalf, &tma_v, &v_full[st], dh * 64, j * kAttnBN, h, b);
+      }
+      if (!ok) for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMA issuer (lane 0)
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_i8(kAttnBM, kAttnBN);
+      constexpr uint32_t idesc_o = idesc_f16(kAttnBM, D, BF16, true);
+      const uint32_t sq_addr = smem_u32(sq);
+      auto issue_s = [&](int i, int st) {
+        const uint32_t sk_addr = smem_u32(sstage + st * SM::kStage);
+        const uint32_t qa = sq_addr + i * SM::kQTile;
+#pragma unroll
+        for (int kk = 0; kk < D / 32; ++kk) {
+          const uint64_t ad = smem_desc_sw(qa + kk * 32, 16, SM::kQKAtom, SM::kQKSwizzle);
+          const uint64_t bd = smem_desc_sw(sk_addr + kk * 32, 16, SM::kQKAtom, SM::kQKSwizzle);
+          mma_i8_ss(tmem + i * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int i, int st, bool acc) {
+        const uint32_t sv_addr = smem_u32(sstage + st * SM::kStage + SM::kKTile);
+#pragma unroll
+        for (int kk = 0; kk < kAttnBN / 16; ++kk) {
+          // B = V[16 keys x D], MN-major, 128B swizzle: 8-key groups 1024 B apart, 64-column
+          // boxes kVHalf apart.
+          const uint64_t bd = smem_desc_sw(sv_addr + kk * 16 * 128, SM::kVHalf, 1024, 2);
+          mma_f16_ts(tmem + kOCol + i * D, tmem + i * 128 + kk * 8, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(&q_full, 0, abort) && mbar_wait(&k_full[0], 0, abort);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0); mma_commit(&s_ready[0]);
+        issue_s(1, 0); mma_commit(&s_ready[1]);
+      }
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j % kAttnStages;
+        const uint32_t ph = (j / kAttnStages) & 1;
+        const int st1 = (j + 1) % kAttnStages;
+        const uint32_t ph1 = ((j + 1) / kAttnStages) & 1;
+        const bool more = j + 1 < n;
+        if (!mbar_wait(&v_full[st], ph, abort)) { ok = false; break; }
+        if (!mbar_wait(&p_ready[0], j & 1, abort)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(0, st, j > 0); mma_commit(&pv_done[0]);
+        if (more) {
+          if (!mbar_wait(&k_full[st1], ph1, abort)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(0, st1); mma_commit(&s_ready[0]);
+        }
+        if (!mbar_wait(&p_ready[1], j & 1, abort)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(1, st, j > 0); mma_commit(&pv_done[1]);
+        mma_commit(&kv_empty[st]);
+        if (more) { issue_s(1, st1); mma_commit(&s_ready[1]); }
+      }
+      mma_commit(&drain_bar);
+      mbar_wait(&drain_bar, 0, nullptr, 1000000);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax warpgroups
+    const int wg = warp >> 2;                 // Q tile 0 or 1
+    const int quarter = warp & 3;             // TMEM lane quarter
+    const int r_local = quarter * 32 + lane;
+    const int qrow = qpair * kAttnRows + wg * kAttnBM + r_local;    // row in [0, Lq_pad)
+    const float cq = __fmul_rn(p.q_scale[static_cast<int64_t>(bh) * p.Lq_pad + qrow], p.scale_log2);
+    const float* ksc = p.k_scale + static_cast<int64_t>(bh) * (p.Lk_pad / kAttnKBlk);
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_addr = tmem + lane_off + wg * 128;
+    const uint32_t o_addr = tmem + lane_off + kOCol + wg * D;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      ok = mbar_wait(&s_ready[wg], j & 1, abort);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t r[128];
+      tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+      tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+      tmem_wait_ld();
+      const int valid = p.Lk - j * kAttnBN;     // keys of this tile that exist
+      if (valid < kAttnBN) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) if (c >= valid) r[c] = static_cast<uint32_t>(INT_MIN);
+      }
+      int mx0 = static_cast<int>(r[0]), mx1 = static_cast<int>(r[64]);
+#pragma unroll
+      for (int c = 1; c < 64; ++c) {
+        mx0 = max(mx0, static_cast<int>(r[c]));
+        mx1 = max(mx1, static_cast<int>(r[64 + c]));
+      }
+      const float c0 = __fmul_rn(cq, ksc[2 * j]);
+      const float c1 = __fmul_rn(cq, ksc[2 * j + 1]);
+      const float mt0 = mx0 == INT_MIN ? -INFINITY : __fmul_rn(static_cast<float>(mx0), c0);
+      const float mt1 = mx1 == INT_MIN ? -INFINITY : __fmul_rn(static_cast<float>(mx1), c1);
+      const float mt = fmaxf(mt0, mt1);
+      const bool need = mt > m + kLazyRescale;
+      if (__any_sync(0xffffffffu, need)) {
+        // Move this row's max up (every lane whose tile max exceeds its running max) and
+        // rescale its O row once the previous P.V has landed.
+        const float mnew = fmaxf(m, mt);
+        const float alpha = ex2_approx(m - mnew);      // 0 when m = -inf
+        l = __fmul_rn(l, alpha);
+        m = mnew;
+        if (j > 0) {
+          ok = mbar_wait(&pv_done[wg], (j - 1) & 1, abort);
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < D; c += 32) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__fmul_rn(__uint_as_float(o[e]), alpha));
+            tmem_st32(o_addr + c, o);
+          }
+        }
+      }
+      const float nb0 = -__fmaf_rn(kMagicF, c0, m);
+      const float nb1 = -__fmaf_rn(kMagicF, c1, m);
+      float lsum = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const float c = cc < 2 ? c0 : c1;
+        const float nb = cc < 2 ? nb0 : nb1;
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int col = cc * 32 + 2 * e;
+          float p0 = ex2_approx(__fmaf_rn(__int_as_float(static_cast<int>(r[col]) + kMagicI), c, nb));
+          float p1 = ex2_approx(__fmaf_rn(__int_as_float(static_cast<int>(r[col + 1]) + kMagicI), c, nb));
+          if (valid < kAttnBN) {
+            if (col >= valid) p0 = 0.f;
+            if (col + 1 >= valid) p1 = 0.f;
+          }
+          lsum = __fadd_rn(lsum, __fadd_rn(p0, p1));
+          pk[e] = pack_p<BF16>(p0, p1);
+        }
+        tmem_st16(s_addr + cc * 16, pk);
+      }
+      l = __fadd_rn(l, lsum);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_ready[wg]);
+    }
+    if (ok) {
+      ok = mbar_wait(&pv_done[wg], (n - 1) & 1, abort);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv = __fdiv_rn(1.0f, l);
+      const bool row_ok = qrow < p.Lq;
+      uint16_t* dst = reinterpret_cast<uint16_t*>(p.o) + b * p.o_sb + static_cast<int64_t>(qrow) * p.o_sl + h * p.o_sh;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + c, o);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 w;
+            w.x = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e]), inv), __fmul_rn(__uint_as_float(o[e + 1]), inv));
+            w.y = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e + 2]), inv), __fmul_rn(__uint_as_float(o[e + 3]), inv));
+            w.z = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e + 4]), inv), __fmul_rn(__uint_as_float(o[e + 5]), inv));
+            w.w = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e + 6]), inv), __fmul_rn(__uint_as_float(o[e + 7]), inv));
+            *reinterpret_cast<uint4*>(dst + c + e) = w;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace dc

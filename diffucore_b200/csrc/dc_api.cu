@@ -1,0 +1,491 @@
+// C-ABI of the B200 hot path. Plain pointers and sizes in, an int status out (0 = ok);
+// dc_last_error() returns the reason of the last non-zero status on the calling thread.
+// The library never allocates or frees device memory: callers pass outputs and workspaces.
+// Every launch goes on the stream the caller passes; nothing here synchronizes.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/diffucore_b200.h"
+#include "sm100.cuh"
+#include "quant.cuh"
+#include "gemm.cuh"
+#include "attn.cuh"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return DC_ERR_INVALID;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  snprintf(g_err, sizeof(g_err), "%s: %s", what, cudaGetErrorString(e));
+  return DC_ERR_CUDA;
+}
+
+#define DC_CHECK_LAUNCH(what)                          \
+  do {                                                 \
+    cudaError_t e_ = cudaGetLastError();               \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// rank-N tiled map; dims/strides innermost first, strides in bytes for dims 1..N-1.
+int make_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+             const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail("cuTensorMapEncodeTiled is not available from the CUDA driver");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail("TMA base address is not 16-byte aligned");
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) { d[i] = dims[i]; b[i] = box[i]; e[i] = 1; }
+  for (int i = 0; i + 1 < rank; ++i) {
+    if (strides_bytes[i] % 16 != 0) return fail("TMA stride %llu bytes is not a multiple of 16",
+                                                (unsigned long long)strides_bytes[i]);
+    s[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, dt, rank, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return DC_OK;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+int check_sm100() {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail("no CUDA device");
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0) return fail("device is sm_%d%d; this library is built for sm_100a only", major, minor);
+  return DC_OK;
+}
+
+template <typename K>
+int set_smem(K kernel, int bytes) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  return DC_OK;
+}
+
+inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+// ------------------------------------------------------------------------------ quantizer
+
+template <typename T>
+int launch_quant(const void* x, int64_t M, int64_t K, int64_t ldx, int group, int gelu, int8_t* q, float* s,
+                 cudaStream_t st) {
+  const int64_t grid64 = M < static_cast<int64_t>(sm_count()) * 16 ? M : static_cast<int64_t>(sm_count()) * 16;
+  const int grid = static_cast<int>(grid64);
+  const T* xp = static_cast<const T*>(x);
+  const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(q) % 8 == 0) && K <= 16384;
+  if (group != 0 && !vec) return fail("rotated quantization needs K %% 256 == 0, ldx %% 8 == 0, 16-byte aligned rows");
+  if (vec) {
+    const int vpt = static_cast<int>((K / 8 + dc::kQuantThreads - 1) / dc::kQuantThreads);
+    if (vpt <= 2)
+      dc::quant_rows_kernel<T, 2><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, static_cast<int>(K), ldx, group, gelu, q, s);
+    else if (vpt <= 4)
+      dc::quant_rows_kernel<T, 4><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, static_cast<int>(K), ldx, group, gelu, q, s);
+    else if (vpt <= 8)
+      dc::quant_rows_kernel<T, 8><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, static_cast<int>(K), ldx, group, gelu, q, s);
+    else
+      dc::quant_rows_kernel<T, 16><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, static_cast<int>(K), ldx, group, gelu, q, s);
+  } else {
+    dc::quant_rows_scalar_kernel<T><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, static_cast<int>(K), ldx, gelu, q, s);
+  }
+  DC_CHECK_LAUNCH("quant_rows launch");
+  return DC_OK;
+}
+
+// ------------------------------------------------------------------------------ GEMM
+
+template <int BN, int OUT>
+int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
+                const void* bias, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K, int gelu,
+                cudaStream_t st) {
+  constexpr int STAGES = BN == 256 ? 4 : 6;
+  using S = dc::GemmSmem<BN, STAGES>;
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldq)};
+    const uint32_t box[2] = {dc::kGemmBK, dc::kGemmBM};
+    int r = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (r) return r;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldw)};
+    const uint32_t box[2] = {dc::kGemmBK, static_cast<uint32_t>(BN)};
+    int r = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (r) return r;
+  }
+  dc::GemmParams p;
+  p.M = static_cast<int>(M); p.N = static_cast<int>(N); p.K = static_cast<int>(K);
+  p.tiles_m = static_cast<int>((M + dc::kGemmBM - 1) / dc::kGemmBM);
+  p.tiles_n = static_cast<int>((N + BN - 1) / BN);
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.num_kb = static_cast<int>((K + dc::kGemmBK - 1) / dc::kGemmBK);
+  p.sx = sx; p.sw = sw; p.bias = bias; p.out = out; p.ldo = ldo; p.gelu = gelu;
+  auto kernel = dc::gemm_w8a8_kernel<BN, STAGES, OUT>;
+  int r = set_smem(kernel, S::kDynamic);
+  if (r) return r;
+  const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
+  kernel<<<grid, dc::kGemmThreads, S::kDynamic, st>>>(ta, tb, p);
+  DC_CHECK_LAUNCH("gemm_w8a8 launch");
+  return DC_OK;
+}
+
+// ------------------------------------------------------------------------------ attention
+
+struct AttnLayout {
+  int64_t Lq_pad, Lk_pad, nwin;
+  size_t q_codes, k_codes, q_scale, k_scale, kpart, ksum, total;
+};
+
+AttnLayout attn_layout(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D, int mode) {
+  AttnLayout a;
+  a.Lq_pad = round_up(Lq, dc::kAttnRows);
+  a.Lk_pad = round_up(Lk, dc::kAttnBN);
+  a.nwin = (Lk + dc::kStatWin - 1) / dc::kStatWin;
+  const int64_t BH = B * H;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += static_cast<size_t>(round_up(static_cast<int64_t>(bytes), 256)); return o; };
+  a.q_codes = take(static_cast<size_t>(BH * a.Lq_pad * D));
+  a.k_codes = take(static_cast<size_t>(BH * a.Lk_pad * D));
+  a.q_scale = take(static_cast<size_t>(BH * a.Lq_pad) * 4);
+  a.k_scale = take(static_cast<size_t>(BH * (a.Lk_pad / dc::kAttnKBlk)) * 4);
+  if (mode == dc::kModeRef) {
+    a.kpart = take(static_cast<size_t>(BH * a.nwin * D) * 4);
+    a.ksum = take(static_cast<size_t>(BH * D) * 4);
+  } else {
+    a.kpart = a.ksum = 0;
+  }
+  a.total = off;
+  return a;
+}
+
+int check_attn_args(int dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D, int mode) {
+  if (dtype != DC_DTYPE_F16 && dtype != DC_DTYPE_BF16) return fail("attention dtype must be fp16 or bf16");
+  if (D != 64 && D != 128) return fail("attention head dim must be 64 or 128 (got %lld)", (long long)D);
+  if (mode != DC_ATTN_MODE_REF && mode != DC_ATTN_MODE_BLOCK64) return fail("unknown attention quant mode %d", mode);
+  if (B <= 0 || H <= 0 || Lq <= 0 || Lk <= 0) return fail("empty attention input");
+  if (B > 65535 || H > 65535) return fail("B and H must be < 65536");
+  if (Lq > (1 << 24) || Lk > (1 << 24)) return fail("sequence length above 2^24");
+  return DC_OK;
+}
+
+int check_strides(const void* ptr, const int64_t* s, const char* name) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return fail("%s must be 16-byte aligned", name);
+  for (int i = 0; i < 3; ++i)
+    if (s[i] % 8 != 0 || s[i] < 0) return fail("%s strides must be non-negative multiples of 8 elements", name);
+  return DC_OK;
+}
+
+template <typename T, int D>
+int attn_prep(const void* q, const void* k, int64_t B, int64_t H, int64_t Lq, int64_t Lk, const int64_t* qs,
+              const int64_t* ks, int mode, uint8_t* ws, const AttnLayout& a, cudaStream_t st) {
+  int8_t* q_codes = reinterpret_cast<int8_t*>(ws + a.q_codes);
+  int8_t* k_codes = reinterpret_cast<int8_t*>(ws + a.k_codes);
+  float* q_scale = reinterpret_cast<float*>(ws + a.q_scale);
+  float* k_scale = reinterpret_cast<float*>(ws + a.k_scale);
+  const T* qp = static_cast<const T*>(q);
+  const T* kp = static_cast<const T*>(k);
+  const int Hi = static_cast<int>(H);
+  if (mode == dc::kModeRef) {
+    float* kpart = reinterpret_cast<float*>(ws + a.kpart);
+    float* ksum = reinterpret_cast<float*>(ws + a.ksum);
+    dc::k_stats_kernel<T, D><<<dim3(static_cast<unsigned>(a.nwin), Hi, static_cast<unsigned>(B)), 16 * (D / 8), 0, st>>>(
+        kp, kpart, static_cast<int>(Lk), Hi, ks[0], ks[1], ks[2]);
+    dc::k_sum_kernel<D><<<static_cast<unsigned>(B * H), D, 0, st>>>(kpart, ksum, static_cast<int>(a.nwin));
+    dc::block_quant_kernel<T, D><<<dim3(static_cast<unsigned>(a.Lk_pad / dc::kAttnKBlk), Hi, static_cast<unsigned>(B)), 256, 0, st>>>(
+        kp, ksum, k_codes, k_scale, nullptr, static_cast<int>(Lk), Hi, static_cast<int>(a.Lk_pad), ks[0], ks[1], ks[2]);
+    const int64_t rows = B * H * a.Lq_pad;
+    constexpr int rows_per_cta = 256 / (D / 8);
+    dc::q_token_quant_kernel<T, D><<<static_cast<unsigned>((rows + rows_per_cta - 1) / rows_per_cta), 256, 0, st>>>(
+        qp, q_codes, q_scale, static_cast<int>(Lq), Hi, static_cast<int>(a.Lq_pad), rows, qs[0], qs[1], qs[2]);
+  } else {
+    dc::block_quant_kernel<T, D><<<dim3(static_cast<unsigned>(a.Lk_pad / dc::kAttnKBlk), Hi, static_cast<unsigned>(B)), 256, 0, st>>>(
+        kp, nullptr, k_codes, k_scale, nullptr, static_cast<int>(Lk), Hi, static_cast<int>(a.Lk_pad), ks[0], ks[1], ks[2]);
+    // Q per 64-row block: only the per-row copy of the block scale is kept (the main kernel
+    // reads one scale per query row in both modes).
+    dc::block_quant_kernel<T, D><<<dim3(static_cast<unsigned>(a.Lq_pad / dc::kAttnKBlk), Hi, static_cast<unsigned>(B)), 256, 0, st>>>(
+        qp, nullptr, q_codes, nullptr, q_scale, static_cast<int>(Lq), Hi, static_cast<int>(a.Lq_pad), qs[0], qs[1],
+        qs[2]);
+  }
+  DC_CHECK_LAUNCH("attention prep launch");
+  return DC_OK;
+}
+
+template <typename T, int D>
+int attn_main(const void* v, int64_t B, int64_t H, int64_t Lq, int64_t Lk, const int64_t* vs, float sm_scale,
+              void* o, const int64_t* os, uint8_t* ws, const AttnLayout& a, cudaStream_t st) {
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  using SM = dc::AttnSmem<D>;
+  CUtensorMap tq, tk, tv;
+  const CUtensorMapSwizzle qk_swz = D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(D), static_cast<uint64_t>(B * H * a.Lq_pad)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(D)};
+    const uint32_t box[2] = {static_cast<uint32_t>(D), dc::kAttnBM};
+    int r = make_map(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, ws + a.q_codes, dims, strides, box, qk_swz);
+    if (r) return r;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(D), static_cast<uint64_t>(B * H * a.Lk_pad)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(D)};
+    const uint32_t box[2] = {static_cast<uint32_t>(D), dc::kAttnBN};
+    int r = make_map(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, ws + a.k_codes, dims, strides, box, qk_swz);
+    if (r) return r;
+  }
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Lk), static_cast<uint64_t>(H),
+                              static_cast<uint64_t>(B)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(vs[1]) * 2, static_cast<uint64_t>(vs[2]) * 2,
+                                 static_cast<uint64_t>(vs[0]) * 2};
+    const uint32_t box[4] = {64, dc::kAttnBN, 1, 1};
+    int r = make_map(&tv, BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, v, dims,
+                     strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (r) return r;
+  }
+  dc::AttnParams p;
+  p.H = static_cast<int>(H); p.Lq = static_cast<int>(Lq); p.Lk = static_cast<int>(Lk);
+  p.Lq_pad = static_cast<int>(a.Lq_pad); p.Lk_pad = static_cast<int>(a.Lk_pad);
+  p.n_ktiles = static_cast<int>(a.Lk_pad / dc::kAttnBN);
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.q_scale = reinterpret_cast<const float*>(ws + a.q_scale);
+  p.k_scale = reinterpret_cast<const float*>(ws + a.k_scale);
+  p.o = o; p.o_sb = os[0]; p.o_sl = os[1]; p.o_sh = os[2];
+  auto kernel = dc::attn_int8_kernel<D, BF16>;
+  int r = set_smem(kernel, SM::kDynamic);
+  if (r) return r;
+  dim3 grid(static_cast<unsigned>(a.Lq_pad / dc::kAttnRows), static_cast<unsigned>(H), static_cast<unsigned>(B));
+  kernel<<<grid, dc::kAttnThreads, SM::kDynamic, st>>>(tq, tk, tv, p);
+  DC_CHECK_LAUNCH("attention launch");
+  return DC_OK;
+}
+
+__global__ void selftest_wait_kernel(long long limit, int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    dc::mbar_init(&bar, 1);
+    abort_flag = 0;
+    dc::fence_barrier_init();
+  }
+  __syncthreads();
+  // Nothing arrives on `bar`: the bounded wait must give up and report it.
+  const bool ok = dc::mbar_wait(&bar, 0, &abort_flag, limit);
+  if (threadIdx.x == 0) {
+    *status = ok ? 0 : 1;
+    if (!ok) atomicCAS(&dc::g_device_error, static_cast<unsigned int>(dc::kErrWaitTimeout),
+                       static_cast<unsigned int>(dc::kErrSelfTest));
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int dc_version(void) { return DC_ABI_VERSION; }
+
+const char* dc_last_error(void) { return g_err; }
+
+int dc_device_error(unsigned int* code, int clear) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, dc::g_device_error, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  if (clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(dc::g_device_error, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the device error word");
+  }
+  if (code) *code = v;
+  return DC_OK;
+}
+
+int dc_quant_rows(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int group, int gelu, int8_t* q,
+                  float* s, void* stream) {
+  if (M < 0 || K <= 0) return fail("quant_rows: bad shape M=%lld K=%lld", (long long)M, (long long)K);
+  if (M == 0) return DC_OK;
+  if (group != 0 && group != 256) return fail("ConvRot group must be 0 or 256 (got %d)", group);
+  if (group && K % 256) return fail("K=%lld is not a multiple of the ConvRot group 256", (long long)K);
+  if (ldx < K) return fail("ldx < K");
+  if (gelu < 0 || gelu > 2) return fail("unknown gelu mode %d", gelu);
+  if (int r = check_sm100()) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (x_dtype) {
+    case DC_DTYPE_BF16: return launch_quant<__nv_bfloat16>(x, M, K, ldx, group, gelu, q, s, st);
+    case DC_DTYPE_F16: return launch_quant<__half>(x, M, K, ldx, group, gelu, q, s, st);
+    case DC_DTYPE_F32:
+      if (gelu) return fail("gelu needs a 16-bit input dtype");
+      return launch_quant<float>(x, M, K, ldx, group, 0, q, s, st);
+    default: return fail("quant_rows: unsupported dtype %d", x_dtype);
+  }
+}
+
+int dc_gemm_w8a8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
+                 const void* bias, void* out, int64_t ldo, int out_dtype, int64_t M, int64_t N, int64_t K,
+                 int gelu, void* stream) {
+  if (M < 0 || N <= 0 || K <= 0) return fail("gemm: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (M == 0) return DC_OK;
+  if (K % 16) return fail("gemm: K=%lld must be a multiple of 16 (TMA row pitch)", (long long)K);
+  if (ldq % 16 || ldw % 16) return fail("gemm: ldq/ldw must be multiples of 16 bytes");
+  if (ldq < K || ldw < K || ldo < N) return fail("gemm: leading dimension smaller than the row");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail("gemm: dimension above 2^31");
+  if (gelu < 0 || gelu > 2) return fail("unknown gelu mode %d", gelu);
+  if (out_dtype != DC_DTYPE_I32 && (sx == nullptr || sw == nullptr)) return fail("gemm: scales are required");
+  if (out_dtype == DC_DTYPE_I32 && (bias != nullptr || gelu)) return fail("gemm: int32 output takes no bias or gelu");
+  if (int r = check_sm100()) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool wide = N > 128;
+  switch (out_dtype) {
+    case DC_DTYPE_BF16:
+      return wide ? launch_gemm<256, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st)
+                  : launch_gemm<128, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st);
+    case DC_DTYPE_F16:
+      return wide ? launch_gemm<256, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st)
+                  : launch_gemm<128, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st);
+    case DC_DTYPE_I32:
+      return wide ? launch_gemm<256, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, st)
+                  : launch_gemm<128, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, st);
+    default: return fail("gemm: unsupported output dtype %d", out_dtype);
+  }
+}
+
+int dc_rescale(const int32_t* acc, int64_t lda, const float* sx, const float* sw, const void* bias, void* out,
+               int64_t ldo, int out_dtype, int64_t M, int64_t N, void* stream) {
+  if (M < 0 || N <= 0) return fail("rescale: bad shape");
+  if (M == 0) return DC_OK;
+  if (lda < N || ldo < N) return fail("rescale: leading dimension smaller than the row");
+  if (M > INT32_MAX || N > INT32_MAX) return fail("rescale: dimension above 2^31");
+  if (int r = check_sm100()) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = static_cast<int>(M < 4096 ? M : 4096);
+  if (out_dtype == DC_DTYPE_BF16)
+    dc::rescale_kernel<dc::kOutBF16><<<grid, 256, 0, st>>>(acc, lda, sx, sw, bias, out, ldo, static_cast<int>(M), static_cast<int>(N));
+  else if (out_dtype == DC_DTYPE_F16)
+    dc::rescale_kernel<dc::kOutF16><<<grid, 256, 0, st>>>(acc, lda, sx, sw, bias, out, ldo, static_cast<int>(M), static_cast<int>(N));
+  else
+    return fail("rescale: output dtype must be fp16 or bf16");
+  DC_CHECK_LAUNCH("rescale launch");
+  return DC_OK;
+}
+
+int dc_attn_workspace_size(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D, int mode, size_t* bytes) {
+  if (int r = check_attn_args(DC_DTYPE_BF16, B, H, Lq, Lk, D, mode)) return r;
+  *bytes = attn_layout(B, H, Lq, Lk, D, mode).total;
+  return DC_OK;
+}
+
+int dc_attn_workspace_layout(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D, int mode, int64_t* out8) {
+  if (int r = check_attn_args(DC_DTYPE_BF16, B, H, Lq, Lk, D, mode)) return r;
+  AttnLayout a = attn_layout(B, H, Lq, Lk, D, mode);
+  out8[0] = a.Lq_pad; out8[1] = a.Lk_pad;
+  out8[2] = static_cast<int64_t>(a.q_codes); out8[3] = static_cast<int64_t>(a.k_codes);
+  out8[4] = static_cast<int64_t>(a.q_scale); out8[5] = static_cast<int64_t>(a.k_scale);
+  out8[6] = static_cast<int64_t>(a.ksum); out8[7] = static_cast<int64_t>(a.total);
+  return DC_OK;
+}
+
+static int attn_common(bool run_prep, bool run_main, const void* q, const void* k, const void* v, int dtype, int64_t B, int64_t H,
+                       int64_t Lq, int64_t Lk, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                       const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
+                       void* workspace, size_t ws_bytes, void* stream) {
+  if (int r = check_attn_args(dtype, B, H, Lq, Lk, D, mode)) return r;
+  if (run_prep) {
+    if (int r = check_strides(q, q_strides, "q")) return r;
+    if (int r = check_strides(k, k_strides, "k")) return r;
+  }
+  if (run_main) {
+    if (int r = check_strides(v, v_strides, "v")) return r;
+    if (int r = check_strides(o, o_strides, "o")) return r;
+  }
+  AttnLayout a = attn_layout(B, H, Lq, Lk, D, mode);
+  if (workspace == nullptr || ws_bytes < a.total)
+    return fail("attention workspace too small: need %zu bytes, got %zu", a.total, ws_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail("attention workspace must be 256-byte aligned");
+  if (int r = check_sm100()) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int r = DC_OK;
+  if (dtype == DC_DTYPE_BF16) {
+    if (run_prep)
+      r = D == 128 ? attn_prep<__nv_bfloat16, 128>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st)
+                   : attn_prep<__nv_bfloat16, 64>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st);
+    if (r || !run_main) return r;
+    return D == 128 ? attn_main<__nv_bfloat16, 128>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a, st)
+                    : attn_main<__nv_bfloat16, 64>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a, st);
+  }
+  if (run_prep)
+    r = D == 128 ? attn_prep<__half, 128>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st)
+                 : attn_prep<__half, 64>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st);
+  if (r || !run_main) return r;
+  return D == 128 ? attn_main<__half, 128>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a, st)
+                  : attn_main<__half, 64>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a, st);
+}
+
+int dc_attn_int8_fwd(const void* q, const void* k, const void* v, int dtype, int64_t B, int64_t H, int64_t Lq,
+                     int64_t Lk, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                     const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  return attn_common(true, true, q, k, v, dtype, B, H, Lq, Lk, D, q_strides, k_strides, v_strides, sm_scale, mode,
+                     o, o_strides, workspace, workspace_bytes, stream);
+}
+
+int dc_attn_int8_main(const void* v, int dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D,
+                      const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  return attn_common(false, true, nullptr, nullptr, v, dtype, B, H, Lq, Lk, D, nullptr, nullptr, v_strides, sm_scale,
+                     mode, o, o_strides, workspace, workspace_bytes, stream);
+}
+
+int dc_attn_int8_prep(const void* q, const void* k, int dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk,
+                      int64_t D, const int64_t* q_strides, const int64_t* k_strides, int mode, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  return attn_common(true, false, q, k, nullptr, dtype, B, H, Lq, Lk, D, q_strides, k_strides, nullptr, 1.0f, mode,
+                     nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+int dc_selftest_wait_timeout(long long limit_cycles, int* status_dev, void* stream) {
+  if (limit_cycles <= 0 || limit_cycles > 4000000000LL) return fail("limit_cycles out of range");
+  if (int r = check_sm100()) return r;
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_cycles, status_dev);
+  DC_CHECK_LAUNCH("selftest launch");
+  return DC_OK;
+}
+
+}  // extern "C"

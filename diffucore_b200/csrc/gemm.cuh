@@ -1,0 +1,279 @@
+// W8A8 GEMM on the sm_100a tensor core: out[M, N] = epilogue(q[M, K] . w[N, K]^T).
+//
+// Persistent, warp-specialised kernel, one CTA per SM:
+//   warp 0      TMA producer: A (activations) and B (weights) tiles, 128-byte swizzle
+//   warp 1      TMEM allocator + single-thread tcgen05.mma.kind::i8 issuer
+//   warps 2..5  epilogue: tcgen05.ld of the int32 accumulator, rescale, bias, store
+// Accumulators live in TMEM, double-buffered (2 x BN columns) so the epilogue of one tile
+// overlaps the main loop of the next.
+//
+// The epilogue rounds exactly like the reference's `rescale` (src/diffucore/models/_int8.py:313-323):
+//   y = dtype(float(acc) * (sx[m] * sw[n]));  if bias: y = dtype(float(y) + float(bias[n]))
+// and with OUT_I32 it writes the raw accumulator (the reference's `int_mm`, _int8.py:200-207).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+#include "sm100.cuh"
+
+namespace dc {
+
+enum GemmOut : int { kOutBF16 = 0, kOutF16 = 1, kOutI32 = 2 };
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 128;            // bytes = int8 elements per k-block (one 128B swizzle row)
+constexpr int kGemmThreads = 192;
+constexpr int kGemmEpiWarp0 = 2;
+
+struct GemmParams {
+  int M, N, K;
+  int tiles_m, tiles_n, num_tiles, num_kb;
+  const float* sx;
+  const float* sw;
+  const void* bias;      // dtype of the output (bf16 / fp16), or null
+  void* out;
+  int64_t ldo;           // output row stride in elements
+  int gelu;              // GeluMode applied to the rescaled value (bf16 / fp16 outputs)
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kA = kGemmBM * kGemmBK;      // 16 KB
+  static constexpr int kB = BN * kGemmBK;           // 16 / 32 KB
+  static constexpr int kStage = kA + kB;
+  static constexpr int kBytes = STAGES * kStage;
+  static constexpr int kDynamic = kBytes + 1024;    // slack for 1024-byte alignment
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int OUT>
+__device__ __forceinline__ float out_round(float y) {
+  if (OUT == kOutBF16) return __bfloat162float(__float2bfloat16_rn(y));
+  return __half2float(__float2half_rn(y));
+}
+
+template <int OUT>
+__device__ __forceinline__ float bias_at(const void* bias, int n) {
+  if (OUT == kOutBF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
+  return __half2float(reinterpret_cast<const __half*>(bias)[n]);
+}
+
+template <int OUT>
+__device__ __forceinline__ float epi_value(uint32_t acc_bits, float sxr, float swn, const void* bias, int n,
+                                           bool has_bias, int gelu) {
+  const float a = __int2float_rn(static_cast<int>(acc_bits));
+  float y = out_round<OUT>(__fmul_rn(a, __fmul_rn(sxr, swn)));
+  if (has_bias) y = out_round<OUT>(__fadd_rn(y, bias_at<OUT>(bias, n)));
+  if (gelu != 0) {
+    if (OUT == kOutBF16) y = gelu_dtype<__nv_bfloat16>(y, gelu);
+    else y = gelu_dtype<__half>(y, gelu);
+  }
+  return y;
+}
+
+template <int BN, int STAGES, int OUT>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                 const GemmParams p) {
+  using S = GemmSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ int abort_flag;
+
+  const int warp = warp_id(), lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 128); }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tma_a); tma_prefetch_desc(&tma_b); }
+  if (warp == 1) { tmem_alloc(&tmem_base_slot, 2 * BN); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_slot;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort)) { ok = false; break; }
+          uint8_t* sa = smem + stage * S::kStage;
+          uint8_t* sb = sa + S::kA;
+          mbar_arrive_expect_tx(&full_bar[stage], S::kStage);
+          tma_load_2d(sa, &tma_a, &full_bar[stage], kb * kGemmBK, tm * kGemmBM);
+          tma_load_2d(sb, &tma_b, &full_bar[stage], kb * kGemmBK, tn * BN);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        // Aborted: give the loads already issued time to land before the CTA can exit.
+        for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_i8(kGemmBM, BN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * BN;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, abort)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sa = smem_u32(smem + stage * S::kStage);
+          const uint32_t sb = sa + S::kA;
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 32; ++k) {
+            const uint64_t ad = smem_desc(sa + k * 32, 16, 1024);
+            const uint64_t bd = smem_desc(sb + k * 32, 16, 1024);
+            mma_i8_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty_bar[stage]);
+          if (kb == p.num_kb - 1) mma_commit(&acc_full[buf]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    // Every MMA issued above has completed once this commit lands.
+    if (lane == 0) mma_commit(&drain_bar);
+    __syncwarp();
+    mbar_wait(&drain_bar, 0, nullptr, 1000000);
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;               // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+      const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
+      const int buf = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[buf], acc_phase, abort)) break;
+      tc_fence_after();
+      const int row = tm * kGemmBM + row_in_tile;
+      const bool row_ok = row < p.M;
+      const float sxr = (OUT != kOutI32 && row_ok) ? p.sx[row] : 0.0f;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        tmem_wait_ld();
+        const int col0 = tn * BN + c;
+        if (!row_ok || col0 >= p.N) continue;
+        if (OUT == kOutI32) {
+          int32_t* dst = reinterpret_cast<int32_t*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0;
+          if (col0 + 32 <= p.N && (p.ldo & 3) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) dst[j] = static_cast<int32_t>(r[j]);
+          }
+        } else {
+          const bool has_bias = p.bias != nullptr;
+          uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0;
+          if (col0 + 32 <= p.N && (p.ldo & 7) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int n = col0 + j + 2 * e;
+                const float y0 = epi_value<OUT>(r[j + 2 * e], sxr, p.sw[n], p.bias, n, has_bias, p.gelu);
+                const float y1 = epi_value<OUT>(r[j + 2 * e + 1], sxr, p.sw[n + 1], p.bias, n + 1, has_bias, p.gelu);
+                w[e] = OUT == kOutBF16 ? pack_bf16x2(y0, y1) : pack_f16x2(y0, y1);
+              }
+              *reinterpret_cast<uint4*>(dst + j) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = col0 + j;
+              if (n >= p.N) continue;
+              const float y = epi_value<OUT>(r[j], sxr, p.sw[n], p.bias, n, has_bias, p.gelu);
+              if (OUT == kOutBF16) {
+                __nv_bfloat16 h = __float2bfloat16_rn(y);
+                dst[j] = *reinterpret_cast<uint16_t*>(&h);
+              } else {
+                __half h = __float2half_rn(y);
+                dst[j] = *reinterpret_cast<uint16_t*>(&h);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// Standalone rescale of an int32 accumulator (the reference's `rescale`,
+// src/diffucore/models/_int8.py:313-323) for callers that hold an int_mm result; the GEMM
+// applies the same epilogue in place. Grid-stride over rows, 8 columns per thread step.
+template <int OUT>
+__global__ void __launch_bounds__(256)
+rescale_kernel(const int32_t* __restrict__ acc, int64_t lda, const float* __restrict__ sx,
+               const float* __restrict__ sw, const void* bias, void* out, int64_t ldo, int M, int N) {
+  const bool has_bias = bias != nullptr;
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const float sxr = sx[row];
+    const int32_t* a = acc + row * lda;
+    uint16_t* dst = reinterpret_cast<uint16_t*>(out) + row * ldo;
+    for (int n = threadIdx.x; n < N; n += blockDim.x) {
+      const float y = epi_value<OUT>(static_cast<uint32_t>(a[n]), sxr, sw[n], bias, n, has_bias, 0);
+      if (OUT == kOutBF16) {
+        __nv_bfloat16 h = __float2bfloat16_rn(y);
+        dst[n] = *reinterpret_cast<uint16_t*>(&h);
+      } else {
+        __half h = __float2half_rn(y);
+        dst[n] = *reinterpret_cast<uint16_t*>(&h);
+      }
+    }
+  }
+}
+
+}  // namespace dc

@@ -1,0 +1,236 @@
+"""Torch-tensor front of the C-ABI: allocates outputs and workspaces with the caching
+allocator, passes raw pointers and the current stream, raises on a non-zero status.
+
+These are the only entry points the module layer (``_int8``, ``_attention``) uses. They run
+on sm_100 CUDA tensors only and raise for anything else; there is no CPU implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_DTYPE = {torch.float32: _lib.DTYPE_F32, torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16}
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError("diffucore_b200 kernels run on CUDA tensors only (got a "
+                               f"{t.device.type} tensor); there is no CPU path")
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def quant_rows(x2: torch.Tensor, group: int = 0, gelu: int = _lib.GELU_NONE):
+    """``(int8 [M, K], fp32 [M])`` per-row codes and scales of ``x2`` [M, K] (any row stride)."""
+    _require_cuda(x2)
+    if x2.dim() != 2:
+        raise ValueError("quant_rows expects a 2-D tensor")
+    if x2.dtype not in _DTYPE:
+        raise TypeError(f"quant_rows: unsupported dtype {x2.dtype}")
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    M, K = x2.shape
+    q = torch.empty(M, K, device=x2.device, dtype=torch.int8)
+    s = torch.empty(M, device=x2.device, dtype=torch.float32)
+    lib = _lib.load()
+    with torch.cuda.device(x2.device):
+        _lib.check(lib.dc_quant_rows(_ptr(x2), _DTYPE[x2.dtype], M, K, x2.stride(0), int(group), int(gelu),
+                                     _ptr(q), _ptr(s), _stream(x2)))
+    return q, s
+
+
+def _gemm_operand(t: torch.Tensor) -> torch.Tensor:
+    if t.dtype != torch.int8 or t.dim() != 2:
+        raise TypeError("GEMM operands are 2-D int8")
+    if t.stride(1) != 1 or t.stride(0) % 16 or t.data_ptr() % 16:
+        t = t.contiguous()
+    return t
+
+
+def _pad_k(q: torch.Tensor, w: torch.Tensor):
+    """Zero-pad K to a multiple of 16 (the TMA row pitch); zeros add nothing to the dot products."""
+    K = q.shape[1]
+    if K % 16 == 0:
+        return q, w
+    pad = 16 - K % 16
+    return torch.nn.functional.pad(q, (0, pad)), torch.nn.functional.pad(w, (0, pad))
+
+
+def gemm_w8a8(q: torch.Tensor, w: torch.Tensor, sx: torch.Tensor | None, sw: torch.Tensor | None,
+              bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
+              gelu: int = _lib.GELU_NONE) -> torch.Tensor:
+    """``epilogue(q @ w.T)``: int32 (``out_dtype=torch.int32``) or rescaled + bias in bf16/fp16."""
+    _require_cuda(q, w)
+    if q.shape[1] != w.shape[1]:
+        raise ValueError(f"K mismatch: q {tuple(q.shape)} vs w {tuple(w.shape)}")
+    q, w = _pad_k(_gemm_operand(q), _gemm_operand(w))
+    M, K = q.shape
+    N = w.shape[0]
+    if out_dtype == torch.int32:
+        code = _lib.DTYPE_I32
+        sx = sw = None
+    elif out_dtype in (torch.bfloat16, torch.float16):
+        code = _DTYPE[out_dtype]
+        sx = sx.to(torch.float32).contiguous()
+        sw = sw.to(torch.float32).contiguous()
+        if bias is not None:
+            bias = bias.to(out_dtype).contiguous()
+    else:
+        raise TypeError(f"gemm_w8a8: unsupported output dtype {out_dtype}")
+    out = torch.empty(M, N, device=q.device, dtype=out_dtype)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        _lib.check(lib.dc_gemm_w8a8(_ptr(q), q.stride(0), _ptr(w), w.stride(0), _ptr(sx), _ptr(sw), _ptr(bias),
+                                    _ptr(out), out.stride(0), code, M, N, K, int(gelu), _stream(q)))
+    return out
+
+
+def rescale(acc: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor, bias: torch.Tensor | None,
+            dtype: torch.dtype) -> torch.Tensor:
+    """``dtype(acc * (sx[:, None] * sw)) (+ bias in dtype)`` for an int32 ``acc`` [M, N]."""
+    _require_cuda(acc)
+    if acc.dtype != torch.int32 or acc.dim() != 2:
+        raise TypeError("rescale expects a 2-D int32 accumulator")
+    if dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"rescale: unsupported dtype {dtype}")
+    acc = acc if acc.stride(1) == 1 else acc.contiguous()
+    M, N = acc.shape
+    sx = sx.to(torch.float32).contiguous()
+    sw = sw.to(torch.float32).contiguous()
+    if bias is not None:
+        bias = bias.to(dtype).contiguous()
+    out = torch.empty(M, N, device=acc.device, dtype=dtype)
+    lib = _lib.load()
+    with torch.cuda.device(acc.device):
+        _lib.check(lib.dc_rescale(_ptr(acc), acc.stride(0), _ptr(sx), _ptr(sw), _ptr(bias), _ptr(out),
+                                  out.stride(0), _DTYPE[dtype], M, N, _stream(acc)))
+    return out
+
+
+def attn_workspace_layout(B: int, H: int, Lq: int, Lk: int, D: int, mode: int) -> dict:
+    lay = (ctypes.c_int64 * 8)()
+    _lib.check(_lib.load().dc_attn_workspace_layout(B, H, Lq, Lk, D, mode, lay))
+    keys = ("Lq_pad", "Lk_pad", "q_codes", "k_codes", "q_scale", "k_scale", "ksum", "total")
+    return dict(zip(keys, (int(v) for v in lay)))
+
+
+def _blhd_strides(t: torch.Tensor):
+    return _lib.i64_array((t.stride(0), t.stride(1), t.stride(2)))
+
+
+def _check_attn_inputs(q, k, v):
+    _require_cuda(q, k, v)
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.dim() != 4 or t.stride(3) != 1:
+            raise ValueError(f"{name} must be (B, L, H, D) with a contiguous head dim")
+    if not (q.dtype == k.dtype == v.dtype) or q.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("q, k, v must share one dtype, fp16 or bf16")
+    B, Lq, H, D = q.shape
+    Lk = k.shape[1]
+    if k.shape != (B, Lk, H, D) or v.shape != (B, Lk, H, D):
+        raise ValueError(f"q, k, v shapes disagree: {tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}")
+    return B, Lq, Lk, H, D
+
+
+def attn_int8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float,
+              mode: int = _lib.MODE_REF, workspace: torch.Tensor | None = None,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """INT8 attention over ``(B, L, H, D)`` q/k/v (any strides with stride(-1) == 1 and the
+    others multiples of 8) -> contiguous ``(B, Lq, H, D)`` in the input dtype."""
+    B, Lq, Lk, H, D = _check_attn_inputs(q, k, v)
+    lib = _lib.load()
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(lib.dc_attn_workspace_size(B, H, Lq, Lk, D, int(mode), ctypes.byref(nbytes)))
+    if workspace is None or workspace.numel() < nbytes.value:
+        workspace = torch.empty(nbytes.value, device=q.device, dtype=torch.uint8)
+    if out is None:
+        out = torch.empty(B, Lq, H, D, device=q.device, dtype=q.dtype)
+    with torch.cuda.device(q.device):
+        _lib.check(lib.dc_attn_int8_fwd(_ptr(q), _ptr(k), _ptr(v), _DTYPE[q.dtype], B, H, Lq, Lk, D,
+                                        _blhd_strides(q), _blhd_strides(k), _blhd_strides(v),
+                                        float(sm_scale), int(mode), _ptr(out), _blhd_strides(out),
+                                        _ptr(workspace), workspace.numel(), _stream(q)))
+    return out
+
+
+def attn_int8_prep(q: torch.Tensor, k: torch.Tensor, mode: int = _lib.MODE_REF) -> dict:
+    """The int8 codes and scales the attention computes for ``q``/``k`` (B, L, H, D):
+    ``q_codes`` [B, H, Lq, D], ``q_scale`` [B, H, Lq], ``k_codes`` [B, H, Lk, D],
+    ``k_scale`` [B, H, ceil(Lk / 64)] and, in mode REF, ``ksum`` [B, H, D]."""
+    B, Lq, Lk, H, D = _check_attn_inputs(q, k, k)
+    lay = attn_workspace_layout(B, H, Lq, Lk, D, int(mode))
+    ws = torch.zeros(lay["total"], device=q.device, dtype=torch.uint8)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        _lib.check(lib.dc_attn_int8_prep(_ptr(q), _ptr(k), _DTYPE[q.dtype], B, H, Lq, Lk, D, _blhd_strides(q),
+                                         _blhd_strides(k), int(mode), _ptr(ws), ws.numel(), _stream(q)))
+    Lqp, Lkp = lay["Lq_pad"], lay["Lk_pad"]
+    BH = B * H
+
+    def view(off, n, dtype, shape):
+        item = torch.tensor([], dtype=dtype).element_size()
+        return ws[off: off + n * item].view(dtype).view(*shape)
+
+    res = {
+        "q_codes": view(lay["q_codes"], BH * Lqp * D, torch.int8, (B, H, Lqp, D))[:, :, :Lq].clone(),
+        "k_codes": view(lay["k_codes"], BH * Lkp * D, torch.int8, (B, H, Lkp, D))[:, :, :Lk].clone(),
+        "q_scale": view(lay["q_scale"], BH * Lqp, torch.float32, (B, H, Lqp))[:, :, :Lq].clone(),
+        "k_scale": view(lay["k_scale"], BH * (Lkp // 64), torch.float32, (B, H, Lkp // 64))[:, :, :(Lk + 63) // 64].clone(),
+    }
+    if mode == _lib.MODE_REF:
+        res["ksum"] = view(lay["ksum"], BH * D, torch.float32, (B, H, D)).clone()
+    return res
+
+
+def selftest_wait_timeout(device: torch.device | str = "cuda", limit_cycles: int = 2_000_000) -> tuple[int, int]:
+    """Run the bounded-wait self-test kernel; returns (kernel status, device error word)."""
+    device = torch.device(device)
+    status = torch.zeros(1, device=device, dtype=torch.int32)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        _lib.device_error(clear=True)
+        _lib.check(lib.dc_selftest_wait_timeout(int(limit_cycles), _ptr(status), _stream(status)))
+        torch.cuda.synchronize(device)
+        return int(status.item()), _lib.device_error(clear=True)
+
+
+class AttnPlan:
+    """A prepared INT8 attention call for fixed shapes: one workspace, reusable across calls.
+    ``prep`` quantizes Q/K into the workspace, ``main`` runs the tensor-core kernel over it;
+    ``__call__`` does both (the same work as :func:`attn_int8`)."""
+
+    def __init__(self, B: int, H: int, Lq: int, Lk: int, D: int, dtype: torch.dtype, mode: int,
+                 device: torch.device | str = "cuda"):
+        self.B, self.H, self.Lq, self.Lk, self.D = B, H, Lq, Lk, D
+        self.dtype, self.mode = dtype, int(mode)
+        self.layout = attn_workspace_layout(B, H, Lq, Lk, D, self.mode)
+        self.workspace = torch.empty(self.layout["total"], device=device, dtype=torch.uint8)
+
+    def prep(self, q: torch.Tensor, k: torch.Tensor) -> None:
+        lib = _lib.load()
+        _lib.check(lib.dc_attn_int8_prep(_ptr(q), _ptr(k), _DTYPE[q.dtype], self.B, self.H, self.Lq, self.Lk,
+                                         self.D, _blhd_strides(q), _blhd_strides(k), self.mode,
+                                         _ptr(self.workspace), self.workspace.numel(), _stream(q)))
+
+    def main(self, v: torch.Tensor, out: torch.Tensor, sm_scale: float) -> torch.Tensor:
+        lib = _lib.load()
+        _lib.check(lib.dc_attn_int8_main(_ptr(v), _DTYPE[v.dtype], self.B, self.H, self.Lq, self.Lk, self.D,
+                                         _blhd_strides(v), float(sm_scale), self.mode, _ptr(out),
+                                         _blhd_strides(out), _ptr(self.workspace), self.workspace.numel(),
+                                         _stream(v)))
+        return out
+
+    def __call__(self, q, k, v, out, sm_scale):
+        self.prep(q, k)
+        return self.main(v, out, sm_scale)

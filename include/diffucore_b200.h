@@ -1,0 +1,127 @@
+/* C-ABI of diffucore_b200: the sm_100a W8A8 linear, activation quantizer and INT8 flash
+ * attention that replace diffucore's quantized hot path.
+ *
+ * Conventions
+ *  - Every function returns an int status: DC_OK (0) or a DC_ERR_* code; dc_last_error()
+ *    then holds a one-line reason for the calling thread.
+ *  - Pointers are device pointers unless stated. The library allocates and frees no device
+ *    memory: outputs and workspaces come from the caller.
+ *  - `stream` is a cudaStream_t (passed as void*); all work is enqueued on it, nothing
+ *    synchronizes the host. Calls on distinct streams may run concurrently.
+ *  - Shapes are int64_t; strides are in elements.
+ *  - There is no CPU path: on a device other than sm_100 every compute entry point fails with
+ *    DC_ERR_INVALID and says why.
+ */
+#ifndef DIFFUCORE_B200_H_
+#define DIFFUCORE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DC_ABI_VERSION 1
+
+#define DC_OK 0
+#define DC_ERR_INVALID 1   /* bad argument, shape, stride, alignment or device */
+#define DC_ERR_CUDA 2      /* a CUDA runtime call or launch failed */
+
+#define DC_DTYPE_F32 0
+#define DC_DTYPE_F16 1
+#define DC_DTYPE_BF16 2
+#define DC_DTYPE_I8 3
+#define DC_DTYPE_I32 4
+
+#define DC_GELU_NONE 0
+#define DC_GELU_ERF 1      /* 0.5 x (1 + erf(x / sqrt 2)), rounded to the input dtype */
+#define DC_GELU_TANH 2     /* 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), rounded likewise */
+
+#define DC_ATTN_MODE_REF 0      /* Q per token, K per 64 keys after subtracting K's mean */
+#define DC_ATTN_MODE_BLOCK64 1  /* Q and K per 64-token block, symmetric abs-max */
+
+int dc_version(void);
+const char* dc_last_error(void);
+
+/* Read (and optionally clear) the device-global error word that bounded in-kernel waits set
+ * when they give up (1 = a wait timed out, 2 = the timeout self-test fired). Synchronous. */
+int dc_device_error(unsigned int* code, int clear);
+
+/* Per-row symmetric int8 quantization of x [M, K] (row stride ldx elements):
+ *   (optional GELU, rounded to x's dtype) -> (optional 256-wide ConvRot rotation) ->
+ *   s[m] = max(amax_m / 127, 1e-30);  q[m, k] = clamp(rint(x / s[m]), -128, 127)
+ * q is [M, K] contiguous int8, s is [M] fp32. group is 0 or 256 (K % 256 == 0).
+ * Replaces diffucore `quantize_activation` (src/diffucore/models/_int8.py:299-310), its
+ * `_quantize_rows` / `_rotate` (:79-97) and the Triton `_rot_quant_kernel` (:399-406); with a
+ * GELU mode it is `_gelu_quantize` / `_gelu_f16_rot_quant_kernel` (:348-358, :436-443). */
+int dc_quant_rows(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int group, int gelu,
+                  int8_t* q, float* s, void* stream);
+
+/* out[M, N] = q[M, K] . w[N, K]^T with int32 accumulation on the tensor core, then
+ *   out_dtype BF16 / F16:  y = dtype(float(acc) * (sx[m] * sw[n]));
+ *                          if bias: y = dtype(float(y) + float(bias[n]))  (bias in out_dtype)
+ *                          if gelu: y = GELU(y) rounded to dtype
+ *   out_dtype I32:         out = acc (sx, sw, bias unused; gelu must be 0)
+ * Leading dimensions ldq, ldw (bytes = elements) must be multiples of 16; K % 16 == 0.
+ * Replaces `int_mm` (src/diffucore/models/_int8.py:200-207), `rescale` (:313-323),
+ * `scaled_mm` (:266-276, whose sm75 kernel is src/diffucore/kernels/int8_gemm_sm75.cu:75-88)
+ * and, with gelu, the first half of `int8_mlp` (:326-345). */
+int dc_gemm_w8a8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
+                 const void* bias, void* out, int64_t ldo, int out_dtype, int64_t M, int64_t N, int64_t K,
+                 int gelu, void* stream);
+
+/* out[M, N] = dtype(float(acc) * (sx[m] * sw[n])) (+ bias in dtype), acc int32 [M, N] with row
+ * stride lda: the epilogue of dc_gemm_w8a8 as a separate pass, for an int32 result already in
+ * hand. Replaces `rescale` (src/diffucore/models/_int8.py:313-323) and its Triton
+ * `_rescale_kernel` (:408-417). */
+int dc_rescale(const int32_t* acc, int64_t lda, const float* sx, const float* sw, const void* bias, void* out,
+               int64_t ldo, int out_dtype, int64_t M, int64_t N, void* stream);
+
+/* Workspace bytes (and its layout) for dc_attn_int8_fwd. layout[8] receives
+ * {Lq_pad, Lk_pad, off_q_codes, off_k_codes, off_q_scale, off_k_scale, off_ksum, total}:
+ * q codes int8 [B*H, Lq_pad, D], k codes int8 [B*H, Lk_pad, D], q scale fp32 [B*H, Lq_pad]
+ * (per row), k scale fp32 [B*H, Lk_pad / 64], ksum fp32 [B*H, D] (mode REF only). */
+int dc_attn_workspace_size(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D, int mode, size_t* bytes);
+int dc_attn_workspace_layout(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D, int mode, int64_t* layout);
+
+/* INT8 attention, non-causal: o = softmax(sm_scale * q k^T) v per (batch, head).
+ * q [B, Lq, H, D], k and v [B, Lk, H, D] in fp16 or bf16 (dtype), each with its own element
+ * strides {stride_b, stride_l, stride_h} (stride_d == 1), strides multiples of 8 and pointers
+ * 16-byte aligned; o has the same dtype and its own strides. D is 64 or 128.
+ * Q and K are quantized to int8 (mode REF: the reference's per-token Q and mean-centred
+ * per-64-key K; mode BLOCK64: per-64-token blocks), S = Q.K^T is exact int32, softmax runs in
+ * fp32 and P.V on the tensor core with P rounded to the input dtype and fp32 accumulation.
+ * workspace: >= dc_attn_workspace_size bytes, 256-byte aligned, contents need not be zeroed.
+ * Replaces the pybind `fwd(q, k, v, sm_scale)` of src/diffucore/kernels/int8_attn_sm80.cu:460-497
+ * (and int8_attn_sm75.cu:477-514) called from `attention_blhd` / `attention_bhld`
+ * (src/diffucore/models/_attention.py:216-217, :268-271). */
+int dc_attn_int8_fwd(const void* q, const void* k, const void* v, int dtype, int64_t B, int64_t H, int64_t Lq,
+                     int64_t Lk, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                     const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Only the quantization stage of dc_attn_int8_fwd: fills the workspace's Q/K codes and scales
+ * (and ksum in mode REF), laid out as dc_attn_workspace_layout describes. Exposes the int8 codes
+ * of the reference's prep kernels (int8_attn_sm80.cu:38-142, and the Q block of :341-388). */
+int dc_attn_int8_prep(const void* q, const void* k, int dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk,
+                      int64_t D, const int64_t* q_strides, const int64_t* k_strides, int mode, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Only the attention stage of dc_attn_int8_fwd, over a workspace that dc_attn_int8_prep (same
+ * B, H, Lq, Lk, D, mode) already filled: lets a caller quantize Q/K once (or elsewhere, e.g. before
+ * a sequence-parallel exchange) and time or run the tensor-core kernel alone. */
+int dc_attn_int8_main(const void* v, int dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D,
+                      const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Failure-detection self-test: launches one CTA that waits on an mbarrier nothing arrives at,
+ * bounded by limit_cycles. The wait gives up, writes 1 to *status_dev (device int) and sets the
+ * device error word to 2. No counterpart in the reference (its kernels have no bounded waits). */
+int dc_selftest_wait_timeout(long long limit_cycles, int* status_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DIFFUCORE_B200_H_ */

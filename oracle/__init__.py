@@ -1,0 +1,13 @@
+"""CPU oracle for the diffucore_b200 hot path — TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference arm
+import this package, as the checker of the CUDA results or as the timed CPU restatement of the
+reference's path. The product (``diffucore_b200``) never imports it.
+
+``oracle/dc_oracle.c`` restates the reference's arithmetic (file:line in each function's
+comment); it is pinned to the reference by the golden vectors under ``tests/golden/`` (made by
+running the reference's own torch-op code) and, for the attention prep, by the reference's CUDA
+prep kernels built from its source by ``oracle/build_ref.py`` into ``oracle/_ref/``.
+"""
+
+from .oracle import *  # noqa: F401,F403
