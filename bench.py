@@ -326,6 +326,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-extras", action="store_true", help="headline attention only (for profiling)")
+    ap.add_argument("--only", default="all", choices=("all", "gemm"),
+                    help="gemm: time only the config-1 W8A8 linear (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -338,6 +340,11 @@ def main() -> int:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     peaks = _peaks()
+    if args.only == "gemm":
+        res = bench_gemm(args, dev, peaks)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return 0
 
     g = torch.Generator().manual_seed(0)
     sets = []
