@@ -200,6 +200,13 @@ def _events(n):
     return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
 
 
+def _cpu_runahead() -> None:
+    """Queue ~50 ms of GPU sleep before a timed region so the host enqueues the timed launches
+    ahead of the GPU: the CUDA events then time kernels back to back, not host launch latency."""
+    import torch
+    torch.cuda._sleep(100_000_000)
+
+
 def bench_attention(args, world, mode_code, sets, plan, out, sampler=None):
     """Times K steps of prep + main over rotating input sets. Returns dict of timings (ms)."""
     import torch
@@ -224,6 +231,7 @@ def bench_attention(args, world, mode_code, sets, plan, out, sampler=None):
     start, end = _events(2)
     _barrier(world)
     torch.cuda.synchronize()
+    _cpu_runahead()
     start.record()
     for i in range(args.steps):
         q, k, v = sets[i % len(sets)]
@@ -291,6 +299,7 @@ def bench_gemm(args, dev, peaks):
         kernels.quant_rows(xs[i % nsets], 0)
     torch.cuda.synchronize()
     ev = _events(3 * steps)
+    _cpu_runahead()
     for i in range(steps):
         x = xs[i % nsets]
         ev[3 * i].record()
@@ -301,6 +310,20 @@ def bench_gemm(args, dev, peaks):
     torch.cuda.synchronize()
     quant_ms = sum(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(steps)) / steps
     gemm_ms = sum(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(steps)) / steps
+    # the library GEMM bar: cuBLASLt int8 GEMM (torch._int_mm, the reference's GEMM on this GPU)
+    ev2 = _events(2)
+    qa = [q for q, _ in qs]
+    wt = layer.weight.t()
+    for i in range(3):
+        torch._int_mm(qa[i % nsets], wt)
+    torch.cuda.synchronize()
+    _cpu_runahead()
+    ev2[0].record()
+    for i in range(steps):
+        torch._int_mm(qa[i % nsets], wt)
+    ev2[1].record()
+    torch.cuda.synchronize()
+    cublas_ms = ev2[0].elapsed_time(ev2[1]) / steps
     tops = GEMM_OPS / (gemm_ms * 1e-3) / 1e12
     peak = _int8_peak_tops(peaks)
     qbytes = GEMM_M * GEMM_K * 2 + GEMM_M * GEMM_K + GEMM_M * 4
@@ -316,6 +339,9 @@ def bench_gemm(args, dev, peaks):
                                                    "unit": "GB/s", "frac": qgbs / peaks["hbm_gbs"],
                                                    "traffic": None, "peak_source": f"hbm_gbs ({peaks['source']})"}},
         "gpu_launches_per_call": 2,
+        "cublaslt_int_mm": {"ms": cublas_ms, "tops": GEMM_OPS / (cublas_ms * 1e-3) / 1e12,
+                            "note": "torch._int_mm (cuBLASLt), int32 out, no quantize/rescale: the "
+                                    "reference's GEMM on this GPU"},
     }
 
 

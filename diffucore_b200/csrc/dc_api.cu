@@ -132,10 +132,9 @@ int launch_quant(const void* x, int64_t M, int64_t K, int64_t ldx, int group, in
 
 // ------------------------------------------------------------------------------ GEMM
 
-template <int BN, int OUT>
+template <int BN, int OUT, bool HAS_BIAS, int GELU>
 int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
-                const void* bias, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K, int gelu,
-                cudaStream_t st) {
+                const void* bias, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
   constexpr int STAGES = BN == 256 ? 4 : 6;
   using S = dc::GemmSmem<BN, STAGES>;
   CUtensorMap ta, tb;
@@ -159,14 +158,36 @@ int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, cons
   p.tiles_n = static_cast<int>((N + BN - 1) / BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.num_kb = static_cast<int>((K + dc::kGemmBK - 1) / dc::kGemmBK);
-  p.sx = sx; p.sw = sw; p.bias = bias; p.out = out; p.ldo = ldo; p.gelu = gelu;
-  auto kernel = dc::gemm_w8a8_kernel<BN, STAGES, OUT>;
+  p.sx = sx; p.sw = sw; p.bias = bias; p.out = out; p.ldo = ldo;
+  auto kernel = dc::gemm_w8a8_kernel<BN, STAGES, OUT, HAS_BIAS, GELU>;
   int r = set_smem(kernel, S::kDynamic);
   if (r) return r;
   const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
   kernel<<<grid, dc::kGemmThreads, S::kDynamic, st>>>(ta, tb, p);
   DC_CHECK_LAUNCH("gemm_w8a8 launch");
   return DC_OK;
+}
+
+template <int BN, int OUT>
+int dispatch_gemm_epilogue(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx,
+                           const float* sw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
+                           int64_t K, int gelu, cudaStream_t st) {
+  if constexpr (OUT == dc::kOutI32) {
+    return launch_gemm<BN, OUT, false, 0>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, st);
+  } else {
+  const bool b = bias != nullptr;
+  switch (gelu) {
+    case DC_GELU_NONE:
+      return b ? launch_gemm<BN, OUT, true, 0>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st)
+               : launch_gemm<BN, OUT, false, 0>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st);
+    case DC_GELU_ERF:
+      return b ? launch_gemm<BN, OUT, true, 1>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st)
+               : launch_gemm<BN, OUT, false, 1>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st);
+    default:
+      return b ? launch_gemm<BN, OUT, true, 2>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st)
+               : launch_gemm<BN, OUT, false, 2>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st);
+  }
+  }
 }
 
 // ------------------------------------------------------------------------------ attention
@@ -374,14 +395,14 @@ int dc_gemm_w8a8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, con
   const bool wide = N > 128;
   switch (out_dtype) {
     case DC_DTYPE_BF16:
-      return wide ? launch_gemm<256, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st)
-                  : launch_gemm<128, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st);
+      return wide ? dispatch_gemm_epilogue<256, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st)
+                  : dispatch_gemm_epilogue<128, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st);
     case DC_DTYPE_F16:
-      return wide ? launch_gemm<256, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st)
-                  : launch_gemm<128, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st);
+      return wide ? dispatch_gemm_epilogue<256, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st)
+                  : dispatch_gemm_epilogue<128, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st);
     case DC_DTYPE_I32:
-      return wide ? launch_gemm<256, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, st)
-                  : launch_gemm<128, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, st);
+      return wide ? dispatch_gemm_epilogue<256, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, st)
+                  : dispatch_gemm_epilogue<128, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, st);
     default: return fail("gemm: unsupported output dtype %d", out_dtype);
   }
 }

@@ -22,8 +22,8 @@ enum GemmOut : int { kOutBF16 = 0, kOutF16 = 1, kOutI32 = 2 };
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 128;            // bytes = int8 elements per k-block (one 128B swizzle row)
-constexpr int kGemmThreads = 192;
-constexpr int kGemmEpiWarp0 = 2;
+constexpr int kGemmEpiWarps = 8;        // two warps per TMEM lane quarter, each half of the columns
+constexpr int kGemmThreads = 64 + 32 * kGemmEpiWarps;
 
 struct GemmParams {
   int M, N, K;
@@ -33,7 +33,6 @@ struct GemmParams {
   const void* bias;      // dtype of the output (bf16 / fp16), or null
   void* out;
   int64_t ldo;           // output row stride in elements
-  int gelu;              // GeluMode applied to the rescaled value (bf16 / fp16 outputs)
 };
 
 template <int BN, int STAGES>
@@ -66,24 +65,26 @@ __device__ __forceinline__ float bias_at(const void* bias, int n) {
   return __half2float(reinterpret_cast<const __half*>(bias)[n]);
 }
 
-template <int OUT>
-__device__ __forceinline__ float epi_value(uint32_t acc_bits, float sxr, float swn, const void* bias, int n,
-                                           bool has_bias, int gelu) {
+// y = dtype(float(acc) * (sx * sw)); y = dtype(float(y) + bias); y = GELU(y) in dtype. The value
+// returned is exactly representable in the output dtype, so the final pack does not round again.
+template <int OUT, bool HAS_BIAS, int GELU>
+__device__ __forceinline__ float epi_value(uint32_t acc_bits, float sxr, float swn, float bn) {
   const float a = __int2float_rn(static_cast<int>(acc_bits));
   float y = out_round<OUT>(__fmul_rn(a, __fmul_rn(sxr, swn)));
-  if (has_bias) y = out_round<OUT>(__fadd_rn(y, bias_at<OUT>(bias, n)));
-  if (gelu != 0) {
-    if (OUT == kOutBF16) y = gelu_dtype<__nv_bfloat16>(y, gelu);
-    else y = gelu_dtype<__half>(y, gelu);
+  if (HAS_BIAS) y = out_round<OUT>(__fadd_rn(y, bn));
+  if (GELU != 0) {
+    if (OUT == kOutBF16) y = gelu_dtype<__nv_bfloat16>(y, GELU);
+    else y = gelu_dtype<__half>(y, GELU);
   }
   return y;
 }
 
-template <int BN, int STAGES, int OUT>
+template <int BN, int STAGES, int OUT, bool HAS_BIAS, int GELU>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                  const GemmParams p) {
   using S = GemmSmem<BN, STAGES>;
+  constexpr int kHalf = BN / 2;                 // columns per epilogue warp
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -92,6 +93,8 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ __align__(16) float col_sw[kGemmEpiWarps][kHalf];    // per-warp staging of sw / bias
+  __shared__ __align__(16) float col_bias[kGemmEpiWarps][kHalf];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
 
@@ -99,7 +102,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 128); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 32 * kGemmEpiWarps); }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
     fence_barrier_init();
@@ -137,22 +140,22 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc = idesc_i8(kGemmBM, BN);
-    int stage = 0;
-    uint32_t phase = 0;
-    int local = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
-      const int buf = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t d_tmem = tmem_base + buf * BN;
-      for (int kb = 0; kb < p.num_kb; ++kb) {
-        if (!mbar_wait(&full_bar[stage], phase, abort)) { ok = false; break; }
+    // ------------------------------------------------------------------ MMA issuer (lane 0)
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(kGemmBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort)) { ok = false; break; }
         tc_fence_after();
-        if (lane == 0) {
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort)) { ok = false; break; }
+          tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * S::kStage);
           const uint32_t sb = sa + S::kA;
 #pragma unroll
@@ -163,36 +166,51 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
           }
           mma_commit(&empty_bar[stage]);
           if (kb == p.num_kb - 1) mma_commit(&acc_full[buf]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        __syncwarp();
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
+      // Every MMA issued above has completed once this commit lands.
+      mma_commit(&drain_bar);
+      mbar_wait(&drain_bar, 0, nullptr, 1000000);
     }
-    // Every MMA issued above has completed once this commit lands.
-    if (lane == 0) mma_commit(&drain_bar);
     __syncwarp();
-    mbar_wait(&drain_bar, 0, nullptr, 1000000);
   } else {
-    // ------------------------------------------------------------------ epilogue
+    // ------------------------------------------------------------------ epilogue (8 warps)
+    const int ew = warp - 2;
     const int quarter = warp & 3;               // TMEM lane quarter this warp may access
+    const int half = ew >> 2;                   // which half of the tile's columns
     const int row_in_tile = quarter * 32 + lane;
+    float* my_sw = col_sw[ew];
+    float* my_bias = col_bias[ew];
     int local = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
       const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&acc_full[buf], acc_phase, abort)) break;
+      const int ncol0 = tn * BN + half * kHalf;         // first output column of this warp
+      if (OUT != kOutI32) {
+        // Stage this warp's column scales (and bias) in shared memory: broadcast reads below.
+        __syncwarp();
+        for (int i = lane; i < kHalf; i += 32) {
+          const int n = ncol0 + i;
+          my_sw[i] = n < p.N ? p.sw[n] : 0.0f;
+          if (HAS_BIAS) my_bias[i] = n < p.N ? bias_at<OUT>(p.bias, n) : 0.0f;
+        }
+        __syncwarp();
+      }
+      bool ok = mbar_wait(&acc_full[buf], acc_phase, abort);
+      if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const int row = tm * kGemmBM + row_in_tile;
       const bool row_ok = row < p.M;
       const float sxr = (OUT != kOutI32 && row_ok) ? p.sx[row] : 0.0f;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + half * kHalf;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < kHalf; c += 32) {
         uint32_t r[32];
         tmem_ld32(taddr + c, r);
         tmem_wait_ld();
-        const int col0 = tn * BN + c;
+        const int col0 = ncol0 + c;
         if (!row_ok || col0 >= p.N) continue;
         if (OUT == kOutI32) {
           int32_t* dst = reinterpret_cast<int32_t*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0;
@@ -206,35 +224,28 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
               if (col0 + j < p.N) dst[j] = static_cast<int32_t>(r[j]);
           }
         } else {
-          const bool has_bias = p.bias != nullptr;
           uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0;
+          uint32_t w[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 s4 = *reinterpret_cast<const float4*>(my_sw + c + j);
+            float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (HAS_BIAS) b4 = *reinterpret_cast<const float4*>(my_bias + c + j);
+            const float y0 = epi_value<OUT, HAS_BIAS, GELU>(r[j], sxr, s4.x, b4.x);
+            const float y1 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 1], sxr, s4.y, b4.y);
+            const float y2 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 2], sxr, s4.z, b4.z);
+            const float y3 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 3], sxr, s4.w, b4.w);
+            w[j / 2] = OUT == kOutBF16 ? pack_bf16x2(y0, y1) : pack_f16x2(y0, y1);
+            w[j / 2 + 1] = OUT == kOutBF16 ? pack_bf16x2(y2, y3) : pack_f16x2(y2, y3);
+          }
           if (col0 + 32 <= p.N && (p.ldo & 7) == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint32_t w[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int n = col0 + j + 2 * e;
-                const float y0 = epi_value<OUT>(r[j + 2 * e], sxr, p.sw[n], p.bias, n, has_bias, p.gelu);
-                const float y1 = epi_value<OUT>(r[j + 2 * e + 1], sxr, p.sw[n + 1], p.bias, n + 1, has_bias, p.gelu);
-                w[e] = OUT == kOutBF16 ? pack_bf16x2(y0, y1) : pack_f16x2(y0, y1);
-              }
-              *reinterpret_cast<uint4*>(dst + j) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<uint4*>(dst + 2 * j) = make_uint4(w[j], w[j + 1], w[j + 2], w[j + 3]);
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = col0 + j;
-              if (n >= p.N) continue;
-              const float y = epi_value<OUT>(r[j], sxr, p.sw[n], p.bias, n, has_bias, p.gelu);
-              if (OUT == kOutBF16) {
-                __nv_bfloat16 h = __float2bfloat16_rn(y);
-                dst[j] = *reinterpret_cast<uint16_t*>(&h);
-              } else {
-                __half h = __float2half_rn(y);
-                dst[j] = *reinterpret_cast<uint16_t*>(&h);
-              }
-            }
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) dst[j] = static_cast<uint16_t>(w[j / 2] >> (16 * (j & 1)));
           }
         }
       }
@@ -264,7 +275,9 @@ rescale_kernel(const int32_t* __restrict__ acc, int64_t lda, const float* __rest
     const int32_t* a = acc + row * lda;
     uint16_t* dst = reinterpret_cast<uint16_t*>(out) + row * ldo;
     for (int n = threadIdx.x; n < N; n += blockDim.x) {
-      const float y = epi_value<OUT>(static_cast<uint32_t>(a[n]), sxr, sw[n], bias, n, has_bias, 0);
+      const float bn = has_bias ? bias_at<OUT>(bias, n) : 0.0f;
+      const float y = has_bias ? epi_value<OUT, true, 0>(static_cast<uint32_t>(a[n]), sxr, sw[n], bn)
+                               : epi_value<OUT, false, 0>(static_cast<uint32_t>(a[n]), sxr, sw[n], bn);
       if (OUT == kOutBF16) {
         __nv_bfloat16 h = __float2bfloat16_rn(y);
         dst[n] = *reinterpret_cast<uint16_t*>(&h);
