@@ -45,6 +45,7 @@ _SIGNATURES = {
                                          _c_i64p, _c_i64p, ctypes.c_int, _c_p, ctypes.c_size_t, _c_p]),
     "dc_attn_int8_main": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64p,
                                          ctypes.c_float, ctypes.c_int, _c_p, _c_i64p, _c_p, ctypes.c_size_t, _c_p]),
+    "dc_selftest_exp2": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_i64, _c_p]),
     "dc_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_longlong, _c_p, _c_p]),
 }
 

@@ -205,10 +205,34 @@ __device__ __forceinline__ uint64_t smem_desc_sw(uint32_t saddr, uint32_t lbo_by
   return d;
 }
 
+constexpr int kMagicI = 0x4B400000;         // bits of 1.5 * 2^23
+constexpr float kMagicF = 12582912.0f;      // int32 s -> float(s) + 1.5 * 2^23 by an integer add
+constexpr float kLazyRescale = 8.0f;        // log2 headroom before O is rescaled
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^a for a pair on the FMA pipe (offloads the MUFU): Cody-Waite style range reduction
+// a = j + f, j = rint(a) via the 1.5 * 2^23 rounding constant, f in [-0.5, 0.5]; 2^f by a degree-3
+// polynomial fitted here for minimum relative error on [-0.5, 0.5] (max 7.5e-5, far below the
+// bf16 / fp16 rounding P receives); 2^j added to the exponent field with an integer add.
+// Arguments are clamped at -125 so the exponent field stays positive (2^-125 is 0 for softmax).
+__device__ __forceinline__ float2 exp2_poly2(float2 a) {
+  a.x = fmaxf(a.x, -125.0f);
+  a.y = fmaxf(a.y, -125.0f);
+  const float2 magic = make_float2(kMagicF, kMagicF);
+  const float2 t = __fadd2_rn(a, magic);                          // j in the low mantissa bits
+  const float2 jf = __fadd2_rn(t, make_float2(-kMagicF, -kMagicF));
+  const float2 f = __fadd2_rn(a, make_float2(-jf.x, -jf.y));
+  float2 p = __ffma2_rn(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.2426111400f, 0.2426111400f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609677f, 0.6932609677f));
+  p = __ffma2_rn(p, f, make_float2(0.9999280572f, 0.9999280572f));
+  // bits(t) = bits(1.5 * 2^23) + j and bits(1.5 * 2^23) << 23 == 0 (mod 2^32): (bits(t) << 23) == j << 23
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 
 template <bool BF16>
@@ -221,9 +245,58 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-constexpr int kMagicI = 0x4B400000;         // bits of 1.5 * 2^23
-constexpr float kMagicF = 12582912.0f;      // int32 s -> float(s) + 1.5 * 2^23 by an integer add
-constexpr float kLazyRescale = 8.0f;        // log2 headroom before O is rescaled
+
+// Max of 64 int32 scores: four independent 3-input-max chains (two new values per op).
+__device__ __forceinline__ int row_max64(const uint32_t (&r)[64]) {
+  int m4[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    int mx = static_cast<int>(r[16 * c]);
+#pragma unroll
+    for (int k = 1; k < 15; k += 2)
+      mx = __vimax3_s32(mx, static_cast<int>(r[16 * c + k]), static_cast<int>(r[16 * c + k + 1]));
+    m4[c] = max(mx, static_cast<int>(r[16 * c + 15]));
+  }
+  return max(max(m4[0], m4[1]), max(m4[2], m4[3]));
+}
+
+__device__ __forceinline__ void mask_tail64(uint32_t (&r)[64], int valid) {
+#pragma unroll
+  for (int c = 0; c < 64; ++c)
+    if (c >= valid) r[c] = static_cast<uint32_t>(INT_MIN);
+}
+
+// P for 64 keys of one row: p = 2^(s * c - m) with x = float(s) + 1.5 * 2^23 formed by an integer
+// add, so s * c - m = fma(x, c, -(1.5 * 2^23 * c + m)) = fma(x, c, nb), two keys per packed FMA,
+// exp2 on the MUFU. Keys at or past `valid` get p = 0 (TAIL only). The sum of p goes to `lsum`
+// (four independent accumulators, so no long dependency chain); P as 16-bit pairs to pk[0..31].
+// (exp2_poly2 above can take a share of the exponentials off the MUFU; measured on this kernel
+// it did not pay while the softmax is latency- rather than MUFU-bound.)
+template <bool BF16, bool TAIL>
+__device__ __forceinline__ void p_half(const uint32_t (&r)[64], float c, float nb, int valid, float2& lsum,
+                                       uint32_t* pk) {
+  const float2 cvec = make_float2(c, c), nvec = make_float2(nb, nb);
+  float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    const int col = 2 * e;
+    const float2 x = make_float2(__int_as_float(static_cast<int>(r[col]) + kMagicI),
+                                 __int_as_float(static_cast<int>(r[col + 1]) + kMagicI));
+    const float2 a = __ffma2_rn(x, cvec, nvec);
+    float2 pr = make_float2(ex2_approx(a.x), ex2_approx(a.y));
+    if (TAIL) {
+      if (col >= valid) pr.x = 0.f;
+      if (col + 1 >= valid) pr.y = 0.f;
+    }
+    acc[e & 3] = __fadd2_rn(acc[e & 3], pr);
+    pk[e] = pack_p<BF16>(pr.x, pr.y);
+  }
+  lsum = __fadd2_rn(lsum, __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3])));
+}
+
+__device__ __forceinline__ float scaled_max(int mx, float c) {
+  return mx == INT_MIN ? -INFINITY : __fmul_rn(static_cast<float>(mx), c);
+}
 
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -240,8 +313,8 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
   __shared__ __align__(8) uint64_t v_full[kAttnStages];
   __shared__ __align__(8) uint64_t kv_empty[kAttnStages];
   __shared__ __align__(8) uint64_t s_ready[2];
-  __shared__ __align__(8) uint64_t p_ready[2];
-  __shared__ __align__(8) uint64_t pv_done[2];
+  __shared__ __align__(8) uint64_t p_ready[2][2];   // [Q tile][key half]
+  __shared__ __align__(8) uint64_t pv_done[2][2];
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
@@ -256,7 +329,10 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
     for (int s = 0; s < kAttnStages; ++s) {
       mbar_init(&k_full[s], 1); mbar_init(&v_full[s], 1); mbar_init(&kv_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) { mbar_init(&s_ready[i], 1); mbar_init(&p_ready[i], 128); mbar_init(&pv_done[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_ready[i], 1);
+      for (int hh = 0; hh < 2; ++hh) { mbar_init(&p_ready[i][hh], 4); mbar_init(&pv_done[i][hh], 1); }
+    }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
     fence_barrier_init();
@@ -268,8 +344,10 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   volatile int* abort = &abort_flag;
-  // TMEM columns: S0 [0,128), S1 [128,256) (P_i aliases the first 64 columns of S_i),
-  // O0 [256, 256 + D), O1 [256 + D, 256 + 2D).
+  // TMEM columns: S0 [0,128), S1 [128,256), O0 [256, 256 + D), O1 [256 + D, 256 + 2D).
+  // P_i (16-bit, two keys per column) overwrites S_i half by half: keys 0-63 go to columns
+  // [0, 32) once S_i[0, 64) is in registers, keys 64-127 to [64, 96) once S_i[64, 128) is.
+  // P.V runs per half, so the tensor core works on one half while the softmax does the other.
   constexpr uint32_t kOCol = 256;
 
   if (warp == 8) {
@@ -301,24 +379,31 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
       constexpr uint32_t idesc_s = idesc_i8(kAttnBM, kAttnBN);
       constexpr uint32_t idesc_o = idesc_f16(kAttnBM, D, BF16, true);
       const uint32_t sq_addr = smem_u32(sq);
+      // Descriptors advance by adding to the start-address field (bits 0-13, in 16-byte units).
       auto issue_s = [&](int i, int st) {
         const uint32_t sk_addr = smem_u32(sstage + st * SM::kStage);
-        const uint32_t qa = sq_addr + i * SM::kQTile;
-#pragma unroll
+        uint64_t ad = smem_desc_sw(sq_addr + i * SM::kQTile, 16, SM::kQKAtom, SM::kQKSwizzle);
+        uint64_t bd = smem_desc_sw(sk_addr, 16, SM::kQKAtom, SM::kQKSwizzle);
+        const uint32_t d = tmem + i * 128;
+#pragma unroll 1
         for (int kk = 0; kk < D / 32; ++kk) {
-          const uint64_t ad = smem_desc_sw(qa + kk * 32, 16, SM::kQKAtom, SM::kQKSwizzle);
-          const uint64_t bd = smem_desc_sw(sk_addr + kk * 32, 16, SM::kQKAtom, SM::kQKSwizzle);
-          mma_i8_ss(tmem + i * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          mma_i8_ss(d, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          ad += 32 >> 4;
+          bd += 32 >> 4;
         }
       };
-      auto issue_pv = [&](int i, int st, bool acc) {
-        const uint32_t sv_addr = smem_u32(sstage + st * SM::kStage + SM::kKTile);
-#pragma unroll
-        for (int kk = 0; kk < kAttnBN / 16; ++kk) {
-          // B = V[16 keys x D], MN-major, 128B swizzle: 8-key groups 1024 B apart, 64-column
-          // boxes kVHalf apart.
-          const uint64_t bd = smem_desc_sw(sv_addr + kk * 16 * 128, SM::kVHalf, 1024, 2);
-          mma_f16_ts(tmem + kOCol + i * D, tmem + i * 128 + kk * 8, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
+      // O_i += P_i[:, 64 keys of half hh] . V[those keys, :]. B = V rows, MN-major, 128B swizzle:
+      // 8-key groups 1024 B apart, 64-column boxes kVHalf apart; each step moves 16 keys (2048 B).
+      auto issue_pv = [&](int i, int hh, int st, bool acc) {
+        uint64_t bd = smem_desc_sw(smem_u32(sstage + st * SM::kStage + SM::kKTile) + hh * 64 * 128, SM::kVHalf,
+                                   1024, 2);
+        const uint32_t d = tmem + kOCol + i * D;
+        uint32_t a = tmem + i * 128 + hh * 64;
+#pragma unroll 1
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_f16_ts(d, a, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
+          bd += 2048 >> 4;
+          a += 8;
         }
       };
       bool ok = mbar_wait(&q_full, 0, abort) && mbar_wait(&k_full[0], 0, abort);
@@ -334,19 +419,22 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
         const uint32_t ph1 = ((j + 1) / kAttnStages) & 1;
         const bool more = j + 1 < n;
         if (!mbar_wait(&v_full[st], ph, abort)) { ok = false; break; }
-        if (!mbar_wait(&p_ready[0], j & 1, abort)) { ok = false; break; }
-        tc_fence_after();
-        issue_pv(0, st, j > 0); mma_commit(&pv_done[0]);
-        if (more) {
-          if (!mbar_wait(&k_full[st1], ph1, abort)) { ok = false; break; }
-          tc_fence_after();
-          issue_s(0, st1); mma_commit(&s_ready[0]);
+        for (int i = 0; i < 2 && ok; ++i) {
+          for (int hh = 0; hh < 2; ++hh) {
+            if (!mbar_wait(&p_ready[i][hh], j & 1, abort)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(i, hh, st, j > 0 || hh > 0);
+            mma_commit(&pv_done[i][hh]);
+          }
+          if (!ok) break;
+          if (i == 1) mma_commit(&kv_empty[st]);
+          if (more) {
+            if (i == 0 && !mbar_wait(&k_full[st1], ph1, abort)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(i, st1);
+            mma_commit(&s_ready[i]);
+          }
         }
-        if (!mbar_wait(&p_ready[1], j & 1, abort)) { ok = false; break; }
-        tc_fence_after();
-        issue_pv(1, st, j > 0); mma_commit(&pv_done[1]);
-        mma_commit(&kv_empty[st]);
-        if (more) { issue_s(1, st1); mma_commit(&s_ready[1]); }
       }
       mma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, nullptr, 1000000);
@@ -362,91 +450,99 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + wg * 128;
     const uint32_t o_addr = tmem + lane_off + kOCol + wg * D;
-    float m = -INFINITY, l = 0.f;
+    const int tail_valid = p.Lk - (n - 1) * kAttnBN;      // keys in the last tile (1..128)
+    float m = -INFINITY;
+    float2 l2 = make_float2(0.f, 0.f);
+    float ks_cur[2] = {ksc[0], ksc[1]};
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
+    // Multiply this row of O by alpha once every P.V issued so far for this Q tile has landed
+    // (waiting for `bar` at `parity`, the latest of them). Rare: only when the running max moves.
+    auto rescale_o = [&](uint64_t* bar, uint32_t parity, float alpha) -> bool {
+      bool w = mbar_wait(bar, parity, abort);
+      if (!__all_sync(0xffffffffu, w)) return false;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + c, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float2 v = __fmul2_rn(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])),
+                                      make_float2(alpha, alpha));
+          o[e] = __float_as_uint(v.x);
+          o[e + 1] = __float_as_uint(v.y);
+        }
+        tmem_st32(o_addr + c, o);
+      }
+      return true;
+    };
+    uint32_t r[64];
+    for (int j = 0; j < n && ok; ++j) {
+      // next tile's K scales, loaded a tile ahead so their latency hides behind this one
+      float ks_next[2] = {0.f, 0.f};
+      if (j + 1 < n) { ks_next[0] = ksc[2 * j + 2]; ks_next[1] = ksc[2 * j + 3]; }
       ok = mbar_wait(&s_ready[wg], j & 1, abort);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      uint32_t r[128];
+      const bool tail = j == n - 1 && tail_valid < kAttnBN;
       tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
       tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
-      tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
       tmem_wait_ld();
-      const int valid = p.Lk - j * kAttnBN;     // keys of this tile that exist
-      if (valid < kAttnBN) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) if (c >= valid) r[c] = static_cast<uint32_t>(INT_MIN);
-      }
-      int mx0 = static_cast<int>(r[0]), mx1 = static_cast<int>(r[64]);
-#pragma unroll
-      for (int c = 1; c < 64; ++c) {
-        mx0 = max(mx0, static_cast<int>(r[c]));
-        mx1 = max(mx1, static_cast<int>(r[64 + c]));
-      }
-      const float c0 = __fmul_rn(cq, ksc[2 * j]);
-      const float c1 = __fmul_rn(cq, ksc[2 * j + 1]);
-      const float mt0 = mx0 == INT_MIN ? -INFINITY : __fmul_rn(static_cast<float>(mx0), c0);
-      const float mt1 = mx1 == INT_MIN ? -INFINITY : __fmul_rn(static_cast<float>(mx1), c1);
-      const float mt = fmaxf(mt0, mt1);
-      const bool need = mt > m + kLazyRescale;
-      if (__any_sync(0xffffffffu, need)) {
-        // Move this row's max up (every lane whose tile max exceeds its running max) and
-        // rescale its O row once the previous P.V has landed.
-        const float mnew = fmaxf(m, mt);
-        const float alpha = ex2_approx(m - mnew);      // 0 when m = -inf
-        l = __fmul_rn(l, alpha);
-        m = mnew;
-        if (j > 0) {
-          ok = mbar_wait(&pv_done[wg], (j - 1) & 1, abort);
-          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-          tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < D; c += 32) {
-            uint32_t o[32];
-            tmem_ld32(o_addr + c, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__fmul_rn(__uint_as_float(o[e]), alpha));
-            tmem_st32(o_addr + c, o);
+      for (int hh = 0; hh < 2; ++hh) {
+        // r holds S[:, 64 hh, 64 hh + 64) here.
+        const int valid = tail ? tail_valid - 64 * hh : 64;
+        if (valid < 64) mask_tail64(r, valid);
+        const float c = __fmul_rn(cq, ks_cur[hh]);
+        const int mx = row_max64(r);
+        if (j == 0 && hh == 0) m = scaled_max(mx, c);    // the running max starts at tile 0's first half
+        // P with the running max; if this half's max exceeds it by more than 2^8 somewhere in the
+        // warp, move the max up, recompute from the registers in hand and rescale O.
+        float2 lt = make_float2(0.f, 0.f);
+        uint32_t pk[32];
+        if (valid < 64) p_half<BF16, true>(r, c, -__fmaf_rn(kMagicF, c, m), valid, lt, pk);
+        else p_half<BF16, false>(r, c, -__fmaf_rn(kMagicF, c, m), valid, lt, pk);
+        const float mt = scaled_max(mx, c);
+        if (__any_sync(0xffffffffu, mt > m + kLazyRescale)) {
+          const float mnew = fmaxf(m, mt);
+          const float alpha = ex2_approx(m - mnew);
+          l2 = __fmul2_rn(l2, make_float2(alpha, alpha));
+          m = mnew;
+          lt = make_float2(0.f, 0.f);
+          if (valid < 64) p_half<BF16, true>(r, c, -__fmaf_rn(kMagicF, c, m), valid, lt, pk);
+          else p_half<BF16, false>(r, c, -__fmaf_rn(kMagicF, c, m), valid, lt, pk);
+          // O holds P.V of every half before this one: tile j-1's second half, or tile j's first.
+          const bool have_o = j > 0 || hh > 0;
+          if (have_o) {
+            const bool w = hh == 0 ? rescale_o(&pv_done[wg][1], (j - 1) & 1, alpha)
+                                   : rescale_o(&pv_done[wg][0], j & 1, alpha);
+            if (!w) { ok = false; break; }
           }
         }
-      }
-      const float nb0 = -__fmaf_rn(kMagicF, c0, m);
-      const float nb1 = -__fmaf_rn(kMagicF, c1, m);
-      float lsum = 0.f;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const float c = cc < 2 ? c0 : c1;
-        const float nb = cc < 2 ? nb0 : nb1;
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int col = cc * 32 + 2 * e;
-          float p0 = ex2_approx(__fmaf_rn(__int_as_float(static_cast<int>(r[col]) + kMagicI), c, nb));
-          float p1 = ex2_approx(__fmaf_rn(__int_as_float(static_cast<int>(r[col + 1]) + kMagicI), c, nb));
-          if (valid < kAttnBN) {
-            if (col >= valid) p0 = 0.f;
-            if (col + 1 >= valid) p1 = 0.f;
-          }
-          lsum = __fadd_rn(lsum, __fadd_rn(p0, p1));
-          pk[e] = pack_p<BF16>(p0, p1);
+        l2 = __fadd2_rn(l2, lt);
+        if (hh == 0) {
+          // prefetch the second half while P of the first is stored
+          tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         }
-        tmem_st16(s_addr + cc * 16, pk);
+        tmem_st32(s_addr + 64 * hh, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_ready[wg][hh]);
+        if (hh == 0) tmem_wait_ld();
       }
-      l = __fadd_rn(l, lsum);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_ready[wg]);
+      ks_cur[0] = ks_next[0];
+      ks_cur[1] = ks_next[1];
     }
     if (ok) {
-      ok = mbar_wait(&pv_done[wg], (n - 1) & 1, abort);
+      ok = mbar_wait(&pv_done[wg][1], (n - 1) & 1, abort);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
       tc_fence_after();
-      const float inv = __fdiv_rn(1.0f, l);
+      const float inv = __fdiv_rn(1.0f, __fadd_rn(l2.x, l2.y));
       const bool row_ok = qrow < p.Lq;
       uint16_t* dst = reinterpret_cast<uint16_t*>(p.o) + b * p.o_sb + static_cast<int64_t>(qrow) * p.o_sl + h * p.o_sh;
 #pragma unroll 1

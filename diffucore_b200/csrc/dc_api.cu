@@ -337,6 +337,18 @@ __global__ void selftest_wait_kernel(long long limit, int* status) {
   }
 }
 
+__global__ void selftest_exp2_kernel(const float* __restrict__ x, float* __restrict__ poly, float* __restrict__ ref,
+                                     int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (2 * i + 1 < n) {
+    const float2 p = dc::exp2_poly2(make_float2(x[2 * i], x[2 * i + 1]));
+    poly[2 * i] = p.x;
+    poly[2 * i + 1] = p.y;
+    ref[2 * i] = exp2f(x[2 * i]);
+    ref[2 * i + 1] = exp2f(x[2 * i + 1]);
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -499,6 +511,16 @@ int dc_attn_int8_prep(const void* q, const void* k, int dtype, int64_t B, int64_
                       size_t workspace_bytes, void* stream) {
   return attn_common(true, false, q, k, nullptr, dtype, B, H, Lq, Lk, D, q_strides, k_strides, nullptr, 1.0f, mode,
                      nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+int dc_selftest_exp2(const float* x, float* poly, float* ref, int64_t n, void* stream) {
+  if (n < 2 || n % 2 || n > (1 << 30)) return fail("selftest_exp2: n must be even, 2 <= n <= 2^30");
+  if (int r = check_sm100()) return r;
+  const int threads = 256;
+  const int blocks = static_cast<int>((n / 2 + threads - 1) / threads);
+  selftest_exp2_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(x, poly, ref, static_cast<int>(n));
+  DC_CHECK_LAUNCH("selftest_exp2 launch");
+  return DC_OK;
 }
 
 int dc_selftest_wait_timeout(long long limit_cycles, int* status_dev, void* stream) {

@@ -234,3 +234,12 @@ class AttnPlan:
     def __call__(self, q, k, v, out, sm_scale):
         self.prep(q, k)
         return self.main(v, out, sm_scale)
+
+
+def selftest_exp2(x: torch.Tensor):
+    """(FMA-pipe exp2 used by the attention softmax, CUDA exp2f) of a CUDA fp32 tensor."""
+    _require_cuda(x)
+    x = x.contiguous().float()
+    poly, ref = torch.empty_like(x), torch.empty_like(x)
+    _lib.check(_lib.load().dc_selftest_exp2(_ptr(x), _ptr(poly), _ptr(ref), x.numel(), _stream(x)))
+    return poly, ref

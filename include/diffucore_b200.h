@@ -115,6 +115,11 @@ int dc_attn_int8_main(const void* v, int dtype, int64_t B, int64_t H, int64_t Lq
                       const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* Accuracy self-test of the attention softmax's FMA-pipe exp2 (range reduction + degree-3
+ * polynomial): poly[i] = that exp2(x[i]), ref[i] = CUDA exp2f(x[i]); n even. No counterpart in the
+ * reference (its kernel uses the MUFU ex2 only). */
+int dc_selftest_exp2(const float* x, float* poly, float* ref, int64_t n, void* stream);
+
 /* Failure-detection self-test: launches one CTA that waits on an mbarrier nothing arrives at,
  * bounded by limit_cycles. The wait gives up, writes 1 to *status_dev (device int) and sets the
  * device error word to 2. No counterpart in the reference (its kernels have no bounded waits). */
