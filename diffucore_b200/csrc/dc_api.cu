@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/diffucore_b200.h"
 #include "sm100.cuh"
@@ -104,30 +105,66 @@ inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
 // ------------------------------------------------------------------------------ quantizer
 
+template <typename T, bool GROUP, int GELU>
+int launch_quant_t(const T* xp, int64_t M, int64_t K, int64_t ldx, int8_t* q, float* s, bool vec, cudaStream_t st) {
+  if constexpr (!GROUP && GELU == 0 && sizeof(T) == 2) {
+    if (vec && K > 4096) {
+      const int64_t ctas64 = (M + 3) / 4;
+      const int ctas = static_cast<int>(ctas64 < static_cast<int64_t>(sm_count()) * 48 ? ctas64 : sm_count() * 48);
+      dc::quant_rows_stream_kernel<T><<<ctas, 128, 0, st>>>(xp, M, static_cast<int>(K), ldx, q, s);
+      DC_CHECK_LAUNCH("quant_rows launch");
+      return DC_OK;
+    }
+  }
+  if (vec && K <= 4096) {
+    // warp per row, 4 rows per CTA
+    const int64_t ctas64 = (M + 3) / 4;
+    const int ctas = static_cast<int>(ctas64 < static_cast<int64_t>(sm_count()) * 32 ? ctas64 : sm_count() * 32);
+    const int vpt = static_cast<int>((K / 8 + 31) / 32);
+    const int Ki = static_cast<int>(K);
+    if (vpt <= 4) dc::quant_rows_warp_kernel<T, 4, GROUP, GELU><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, q, s);
+    else if (vpt <= 8) dc::quant_rows_warp_kernel<T, 8, GROUP, GELU><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, q, s);
+    else if (vpt <= 12) dc::quant_rows_warp_kernel<T, 12, GROUP, GELU><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, q, s);
+    else dc::quant_rows_warp_kernel<T, 16, GROUP, GELU><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, q, s);
+  } else if (vec) {
+    const int64_t grid64 = M < static_cast<int64_t>(sm_count()) * 16 ? M : static_cast<int64_t>(sm_count()) * 16;
+    const int grid = static_cast<int>(grid64);
+    const int vpt = static_cast<int>((K / 8 + dc::kQuantThreads - 1) / dc::kQuantThreads);
+    const int Ki = static_cast<int>(K);
+    if (vpt <= 8) dc::quant_rows_kernel<T, 8, GROUP, GELU><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, Ki, ldx, q, s);
+    else dc::quant_rows_kernel<T, 16, GROUP, GELU><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, Ki, ldx, q, s);
+  } else {
+    const int64_t grid64 = M < static_cast<int64_t>(sm_count()) * 16 ? M : static_cast<int64_t>(sm_count()) * 16;
+    dc::quant_rows_scalar_kernel<T, GELU><<<static_cast<int>(grid64), dc::kQuantThreads, 0, st>>>(
+        xp, M, static_cast<int>(K), ldx, q, s);
+  }
+  DC_CHECK_LAUNCH("quant_rows launch");
+  return DC_OK;
+}
+
 template <typename T>
 int launch_quant(const void* x, int64_t M, int64_t K, int64_t ldx, int group, int gelu, int8_t* q, float* s,
                  cudaStream_t st) {
-  const int64_t grid64 = M < static_cast<int64_t>(sm_count()) * 16 ? M : static_cast<int64_t>(sm_count()) * 16;
-  const int grid = static_cast<int>(grid64);
   const T* xp = static_cast<const T*>(x);
   const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(q) % 8 == 0) && K <= 16384;
   if (group != 0 && !vec) return fail("rotated quantization needs K %% 256 == 0, ldx %% 8 == 0, 16-byte aligned rows");
-  if (vec) {
-    const int vpt = static_cast<int>((K / 8 + dc::kQuantThreads - 1) / dc::kQuantThreads);
-    if (vpt <= 2)
-      dc::quant_rows_kernel<T, 2><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, static_cast<int>(K), ldx, group, gelu, q, s);
-    else if (vpt <= 4)
-      dc::quant_rows_kernel<T, 4><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, static_cast<int>(K), ldx, group, gelu, q, s);
-    else if (vpt <= 8)
-      dc::quant_rows_kernel<T, 8><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, static_cast<int>(K), ldx, group, gelu, q, s);
-    else
-      dc::quant_rows_kernel<T, 16><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, static_cast<int>(K), ldx, group, gelu, q, s);
+  if constexpr (std::is_same<T, float>::value) {
+    return group ? launch_quant_t<T, true, 0>(xp, M, K, ldx, q, s, vec, st)
+                 : launch_quant_t<T, false, 0>(xp, M, K, ldx, q, s, vec, st);
   } else {
-    dc::quant_rows_scalar_kernel<T><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, static_cast<int>(K), ldx, gelu, q, s);
+    switch (gelu) {
+      case DC_GELU_ERF:
+        return group ? launch_quant_t<T, true, 1>(xp, M, K, ldx, q, s, vec, st)
+                     : launch_quant_t<T, false, 1>(xp, M, K, ldx, q, s, vec, st);
+      case DC_GELU_TANH:
+        return group ? launch_quant_t<T, true, 2>(xp, M, K, ldx, q, s, vec, st)
+                     : launch_quant_t<T, false, 2>(xp, M, K, ldx, q, s, vec, st);
+      default:
+        return group ? launch_quant_t<T, true, 0>(xp, M, K, ldx, q, s, vec, st)
+                     : launch_quant_t<T, false, 0>(xp, M, K, ldx, q, s, vec, st);
+    }
   }
-  DC_CHECK_LAUNCH("quant_rows launch");
-  return DC_OK;
 }
 
 // ------------------------------------------------------------------------------ GEMM

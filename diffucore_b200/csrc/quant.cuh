@@ -27,6 +27,12 @@ template <> struct Vec8<__nv_bfloat16> {
 #pragma unroll
     for (int i = 0; i < 4; ++i) { float2 t = __bfloat1622float2(h[i]); f[2 * i] = t.x; f[2 * i + 1] = t.y; }
   }
+  __device__ static void from_raw(const uint4& u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { f[2 * i] = __uint_as_float(w[i] << 16); f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u); }
+  }
+  __device__ static float half_bits_to_float(uint32_t h) { return __uint_as_float(h << 16); }
   __device__ static float one(const __nv_bfloat16* p) { return __bfloat162float(*p); }
   __device__ static float round_trip(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 };
@@ -37,6 +43,12 @@ template <> struct Vec8<__half> {
 #pragma unroll
     for (int i = 0; i < 4; ++i) { float2 t = __half22float2(h[i]); f[2 * i] = t.x; f[2 * i + 1] = t.y; }
   }
+  __device__ static void from_raw(const uint4& u, float (&f)[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { float2 t = __half22float2(h[i]); f[2 * i] = t.x; f[2 * i + 1] = t.y; }
+  }
+  __device__ static float half_bits_to_float(uint32_t h) { return __half2float(__ushort_as_half(static_cast<unsigned short>(h))); }
   __device__ static float one(const __half* p) { return __half2float(*p); }
   __device__ static float round_trip(float x) { return __half2float(__float2half_rn(x)); }
 };
@@ -45,6 +57,11 @@ template <> struct Vec8<float> {
     float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
     f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
   }
+  __device__ static void from_raw(const uint4& u, float (&f)[8]) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y); f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+    f[4] = f[5] = f[6] = f[7] = 0.0f;   // unused: raw fp32 rows are not kept
+  }
+  __device__ static float half_bits_to_float(uint32_t h) { return __uint_as_float(h); }
   __device__ static float one(const float* p) { return *p; }
   __device__ static float round_trip(float x) { return x; }
 };
@@ -126,14 +143,187 @@ __device__ __forceinline__ int8_t quant_code(float x, float scale) {
   return static_cast<int8_t>(static_cast<int>(t));
 }
 
+// Eight codes without a division or a float->int conversion on the common path. y = x * (1 / scale)
+// is within ~2^-23 relative (|y| <= 127.5, so within 2e-5 absolute) of the IEEE quotient x / scale;
+// t = y + 1.5 * 2^23 rounds y to an integer with ties to even (the float grid there has unit
+// spacing), and the code is the low byte of t's bits (|codes| <= 127, so no clamp is reached).
+// When some y lies within 1e-4 of a rounding boundary k + 1/2, the quotient and y might round
+// differently, so those eight values are redone with the exact division (quant_code). The result
+// is bit-identical to quant_code on every element.
+constexpr float kRoundMagic = 12582912.0f;      // 1.5 * 2^23
+
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], float scale, float inv_scale) {
+  uint32_t b[8];
+  uint32_t d[8];     // |y - rint(y)| as sign-cleared float bits: unsigned order == magnitude order
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float y = __fmul_rn(v[j], inv_scale);
+    const float t = __fadd_rn(y, kRoundMagic);
+    d[j] = __float_as_uint(__fsub_rn(y, __fsub_rn(t, kRoundMagic))) & 0x7FFFFFFFu;
+    b[j] = __float_as_uint(t);
+  }
+  const uint32_t dmax = max(max(max(d[0], d[1]), max(d[2], d[3])), max(max(d[4], d[5]), max(d[6], d[7])));
+  if (dmax > __float_as_uint(0.5f - 1e-4f)) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) b[j] = static_cast<uint32_t>(static_cast<uint8_t>(quant_code(v[j], scale)));
+  }
+  // low bytes of b[0..3] -> w0, b[4..7] -> w1
+  const uint32_t w0 = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+  const uint32_t w1 = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
+  return make_uint2(w0, w1);
+}
+
+// Warp-per-row quantizer for K <= 32 * 8 * VPT (K % 8 == 0, 16-byte aligned rows): the amax
+// reduction is warp shuffles only and a CTA holds several rows at once. Without rotation or GELU
+// the row stays in registers as raw 16-byte vectors (half the registers, more rows in flight) and
+// is converted twice; otherwise the transformed fp32 values are kept.
+// Plain rows (no rotation, no GELU), 16-bit input: warp per row in two streaming passes, amax
+// then codes. The second pass re-reads the row from L2 (the rows in flight are a few MB), so
+// registers stay few and many rows are in flight per SM.
+template <typename T>
+__global__ void __launch_bounds__(128, 12)
+quant_rows_stream_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int8_t* __restrict__ q,
+                         float* __restrict__ s) {
+  constexpr int kBatch = 4;
+  const int lane = threadIdx.x & 31;
+  const int nvec = K >> 3;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
+       row += warps) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+    uint32_t am2 = 0u;
+    for (int v0 = lane; v0 < nvec; v0 += 32 * kBatch) {
+      uint4 raw[kBatch];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int vi = v0 + 32 * b;
+        raw[b] = vi < nvec ? __ldg(xr + vi) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        am2 = __vmaxu2(am2, __vmaxu2(__vmaxu2(raw[b].x & 0x7FFF7FFFu, raw[b].y & 0x7FFF7FFFu),
+                                     __vmaxu2(raw[b].z & 0x7FFF7FFFu, raw[b].w & 0x7FFF7FFFu)));
+      }
+    }
+    float amax = Vec8<T>::half_bits_to_float(max(am2 & 0xFFFFu, am2 >> 16));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    const float inv = __fdiv_rn(1.0f, scale);
+    uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(K));
+    for (int v0 = lane; v0 < nvec; v0 += 32 * kBatch) {
+      uint4 raw[kBatch];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int vi = v0 + 32 * b;
+        raw[b] = vi < nvec ? __ldg(xr + vi) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int vi = v0 + 32 * b;
+        if (vi < nvec) {
+          float f[8];
+          Vec8<T>::from_raw(raw[b], f);
+          qr[vi] = quant8(f, scale, inv);
+        }
+      }
+    }
+    if (lane == 0) s[row] = scale;
+  }
+}
+
+template <typename T, int VPT, bool GROUP, int GELU>
+__global__ void __launch_bounds__(128, 4)
+quant_rows_warp_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int8_t* __restrict__ q,
+                       float* __restrict__ s) {
+  constexpr bool kRaw = !GROUP && GELU == kGeluNone && sizeof(T) == 2;
+  constexpr int kRawVecs = kRaw ? VPT : 1;
+  constexpr int kFloatVecs = kRaw ? 1 : VPT;
+  const int lane = threadIdx.x & 31;
+  const int nvec = K >> 3;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
+       row += warps) {
+    const T* xr = x + row * ldx;
+    uint4 raw[kRawVecs];
+    float v[kFloatVecs][8];
+    float am[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};   // independent max chains
+    uint32_t am2[4] = {0u, 0u, 0u, 0u};                       // packed 16-bit |x| maxima (raw rows)
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lane + 32 * i;
+      if (kRaw) {
+        raw[kRaw ? i : 0] = vi < nvec ? *reinterpret_cast<const uint4*>(xr + vi * 8) : make_uint4(0, 0, 0, 0);
+      } else {
+        const int fi = kRaw ? 0 : i;
+        if (vi < nvec) {
+          Vec8<T>::load(xr + vi * 8, v[fi]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[fi][j] = 0.0f;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      if (kRaw) {
+        // |x| of 16-bit floats: clear the sign bits; unsigned order then equals magnitude order,
+        // so two lanes of a packed 16-bit max do two elements at a time.
+        const uint4 u = raw[kRaw ? i : 0];
+        am2[0] = __vmaxu2(am2[0], u.x & 0x7FFF7FFFu);
+        am2[1] = __vmaxu2(am2[1], u.y & 0x7FFF7FFFu);
+        am2[2] = __vmaxu2(am2[2], u.z & 0x7FFF7FFFu);
+        am2[3] = __vmaxu2(am2[3], u.w & 0x7FFF7FFFu);
+      } else {
+        const int fi = kRaw ? 0 : i;
+        if (GELU != kGeluNone) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[fi][j] = gelu_dtype<T>(v[fi][j], GELU);
+        }
+        // the 32 lanes at one i hold one 256-wide group (vectors 32 i .. 32 i + 31)
+        if (GROUP) hadamard256_warp(v[fi]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) am[j] = fmaxf(am[j], fabsf(v[fi][j]));
+      }
+    }
+    float amax = fmaxf(fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3])), fmaxf(fmaxf(am[4], am[5]), fmaxf(am[6], am[7])));
+    if (kRaw) {
+      const uint32_t m2 = __vmaxu2(__vmaxu2(am2[0], am2[1]), __vmaxu2(am2[2], am2[3]));
+      const uint32_t hmax = max(m2 & 0xFFFFu, m2 >> 16);
+      amax = Vec8<T>::half_bits_to_float(hmax);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    const float inv = __fdiv_rn(1.0f, scale);
+    int8_t* qr = q + row * static_cast<int64_t>(K);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) {
+        uint2 w;
+        if (kRaw) {
+          float f[8];
+          Vec8<T>::from_raw(raw[kRaw ? i : 0], f);
+          w = quant8(f, scale, inv);
+        } else {
+          w = quant8(v[kRaw ? 0 : i], scale, inv);
+        }
+        *reinterpret_cast<uint2*>(qr + vi * 8) = w;
+      }
+    }
+    if (lane == 0) s[row] = scale;
+  }
+}
+
 constexpr int kQuantThreads = 128;
 
 // Vector path: K % 8 == 0, ldx % 8 == 0 (elements), x 16-byte aligned. One CTA per row
 // (grid-stride). Each thread holds up to VPT vectors of 8 elements. `group` is 0 or 256.
-template <typename T, int VPT>
+template <typename T, int VPT, bool GROUP, int GELU>
 __global__ void __launch_bounds__(kQuantThreads)
-quant_rows_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int group, int gelu,
-                  int8_t* __restrict__ q, float* __restrict__ s) {
+quant_rows_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int8_t* __restrict__ q,
+                  float* __restrict__ s) {
   __shared__ float red[kQuantThreads / 32];
   const int tid = threadIdx.x;
   const int nvec = K >> 3;
@@ -150,13 +340,13 @@ quant_rows_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int gr
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
       }
-      if (gelu != kGeluNone) {
+      if (GELU != kGeluNone) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] = gelu_dtype<T>(v[i][j], gelu);
+        for (int j = 0; j < 8; ++j) v[i][j] = gelu_dtype<T>(v[i][j], GELU);
       }
       // A 256-group is 32 consecutive vectors = the 32 lanes of one warp at one i. Groups
       // past the row end hold zeros and are discarded; every lane joins the shuffles.
-      if (group) hadamard256_warp(v[i]);
+      if (GROUP) hadamard256_warp(v[i]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
     }
@@ -169,29 +359,22 @@ quant_rows_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int gr
     for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
     __syncthreads();
     const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    const float inv = __fdiv_rn(1.0f, scale);
     int8_t* qr = q + row * static_cast<int64_t>(K);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = tid + i * kQuantThreads;
-      if (vi < nvec) {
-        uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          w0 |= static_cast<uint32_t>(static_cast<uint8_t>(quant_code(v[i][j], scale))) << (8 * j);
-          w1 |= static_cast<uint32_t>(static_cast<uint8_t>(quant_code(v[i][j + 4], scale))) << (8 * j);
-        }
-        *reinterpret_cast<uint2*>(qr + vi * 8) = make_uint2(w0, w1);
-      }
+      if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant8(v[i], scale, inv);
     }
     if (tid == 0) s[row] = scale;
   }
 }
 
 // Generic path for any K and stride (no rotation): two passes over the row.
-template <typename T>
+template <typename T, int GELU>
 __global__ void __launch_bounds__(kQuantThreads)
-quant_rows_scalar_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int gelu,
-                         int8_t* __restrict__ q, float* __restrict__ s) {
+quant_rows_scalar_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int8_t* __restrict__ q,
+                         float* __restrict__ s) {
   __shared__ float red[kQuantThreads / 32];
   const int tid = threadIdx.x;
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
@@ -199,7 +382,7 @@ quant_rows_scalar_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx,
     float amax = 0.0f;
     for (int c = tid; c < K; c += kQuantThreads) {
       float t = Vec8<T>::one(xr + c);
-      if (gelu != kGeluNone) t = gelu_dtype<T>(t, gelu);
+      if (GELU != kGeluNone) t = gelu_dtype<T>(t, GELU);
       amax = fmaxf(amax, fabsf(t));
     }
 #pragma unroll
@@ -214,7 +397,7 @@ quant_rows_scalar_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx,
     int8_t* qr = q + row * static_cast<int64_t>(K);
     for (int c = tid; c < K; c += kQuantThreads) {
       float t = Vec8<T>::one(xr + c);
-      if (gelu != kGeluNone) t = gelu_dtype<T>(t, gelu);
+      if (GELU != kGeluNone) t = gelu_dtype<T>(t, GELU);
       qr[c] = quant_code(t, scale);
     }
     if (tid == 0) s[row] = scale;
