@@ -36,6 +36,11 @@ ATTN_OPS = 4 * B * H * S * S * D                     # QK^T (int8) + PV (bf16), 
 GEMM_M, GEMM_N, GEMM_K = 4096, 3072, 3072
 GEMM_OPS = 2 * GEMM_M * GEMM_N * GEMM_K
 METRIC = "INT8 TOPS, INT8 flash attention (BASELINE config 2: B=1, H=24, S=4608, D=128, bf16)"
+# DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, one capture of each
+# kernel on these workloads): attention main kernel, W8A8 GEMM, activation quantizer.
+TRAFFIC_ATTN = 60.65e6
+TRAFFIC_GEMM = 22.09e6
+TRAFFIC_QUANT = 25.21e6
 CONFIG = {"workload": "int8_flash_attention_config2", "batch": B, "heads": H, "seq_len": S, "head_dim": D,
           "quant": "per-64-token-block Q and K (block64)", "causal": False,
           "l2": "4 rotating input sets (4 x 85 MB > 126 MB L2)", "parallelism": "replicas (weak scaling)"}
@@ -333,11 +338,11 @@ def bench_gemm(args, dev, peaks):
         "value": GEMM_OPS / ((quant_ms + gemm_ms) * 1e-3) / 1e12, "unit": "TOPS",
         "ms_per_call": quant_ms + gemm_ms,
         "gemm": {"ms": gemm_ms, "roofline": {"bound": "tensor", "achieved": tops, "peak": peak, "unit": "TOPS",
-                                             "frac": tops / peak, "traffic": None,
+                                             "frac": tops / peak, "traffic": TRAFFIC_GEMM,
                                              "peak_source": f"2 x bf16_tflops ({peaks['source']})"}},
         "quantizer": {"ms": quant_ms, "roofline": {"bound": "hbm", "achieved": qgbs, "peak": peaks["hbm_gbs"],
                                                    "unit": "GB/s", "frac": qgbs / peaks["hbm_gbs"],
-                                                   "traffic": None, "peak_source": f"hbm_gbs ({peaks['source']})"}},
+                                                   "traffic": TRAFFIC_QUANT, "peak_source": f"hbm_gbs ({peaks['source']})"}},
         "gpu_launches_per_call": 2,
         "cublaslt_int_mm": {"ms": cublas_ms, "tops": GEMM_OPS / (cublas_ms * 1e-3) / 1e12,
                             "note": "torch._int_mm (cuBLASLt), int32 out, no quantize/rescale: the "
@@ -393,7 +398,8 @@ def main() -> int:
         "data": "synthetic N(0,1) bf16, seeded", "config": CONFIG,
         "prep_ms": t["prep_ms"], "attn_kernel_ms": t["main_ms"],
         "roofline": {"bound": "tensor", "achieved": main_tops, "peak": peak, "unit": "TOPS",
-                     "frac": main_tops / peak, "traffic": None,
+                     "frac": main_tops / peak, "traffic": TRAFFIC_ATTN,
+                     "traffic_note": "bytes per launch, ncu dram__bytes_read + write (one capture)",
                      "peak_source": f"2 x bf16_tflops ({peaks['source']}); nominal dense INT8 4500 TOPS",
                      "kernel": "attn_int8_kernel<128, bf16>"},
         "clocks": t["clocks"],
