@@ -19,6 +19,7 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_I8, DTYPE_I32 = 0, 1, 2, 3, 4
 GELU_NONE, GELU_ERF, GELU_TANH = 0, 1, 2
 MODE_REF, MODE_BLOCK64 = 0, 1
 ABI_VERSION = 1
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 _c_i64 = ctypes.c_int64
 _c_p = ctypes.c_void_p
@@ -45,6 +46,9 @@ _SIGNATURES = {
                                          _c_i64p, _c_i64p, ctypes.c_int, _c_p, ctypes.c_size_t, _c_p]),
     "dc_attn_int8_main": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64p,
                                          ctypes.c_float, ctypes.c_int, _c_p, _c_i64p, _c_p, ctypes.c_size_t, _c_p]),
+    "dc_attn_int8_fwd_noalloc": (ctypes.c_int, [_c_p, _c_p, _c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64,
+                                                _c_i64, _c_i64p, _c_i64p, _c_i64p, ctypes.c_float, ctypes.c_int,
+                                                _c_p, _c_i64p, _c_p]),
     "dc_selftest_exp2": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_i64, _c_p]),
     "dc_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_longlong, _c_p, _c_p]),
 }

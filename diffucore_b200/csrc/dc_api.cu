@@ -12,6 +12,9 @@
 #include <type_traits>
 
 #include "../../include/diffucore_b200.h"
+
+// Size of the fixed scratch behind dc_attn_int8_fwd_noalloc (32 MiB per GPU).
+constexpr size_t kNoAllocScratch = static_cast<size_t>(DC_NOALLOC_SCRATCH_BYTES);
 #include "sm100.cuh"
 #include "quant.cuh"
 #include "gemm.cuh"
@@ -548,6 +551,57 @@ int dc_attn_int8_prep(const void* q, const void* k, int dtype, int64_t B, int64_
                       size_t workspace_bytes, void* stream) {
   return attn_common(true, false, q, k, nullptr, dtype, B, H, Lq, Lk, D, q_strides, k_strides, nullptr, 1.0f, mode,
                      nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Attention for callers that cannot allocate device memory: an application that owns every byte
+// of GPU memory through its own pool and has no way to hand this library a workspace, or that
+// calls at a point where cudaMalloc's implicit device synchronization is not allowed. The Q/K
+// codes and scales the attention needs between its two stages live instead in one fixed
+// file-scope device array. Every GPU that loads this library holds that array (kNoAllocScratch
+// bytes) until the process exits.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratch];
+
+namespace {
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[256] = {};   // device address of g_noalloc_scratch, per device ordinal
+
+// The scratch array's device address for the current device. In host code the array's name is
+// only a host-side stand-in, so the address comes from cudaGetSymbolAddress, once per device,
+// with that device current (the first call on each device does this).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 256) return fail("device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return DC_OK;
+}
+}  // namespace
+
+int dc_attn_int8_fwd_noalloc(const void* q, const void* k, const void* v, int dtype, int64_t B, int64_t H,
+                             int64_t Lq, int64_t Lk, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                             const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
+                             void* stream) {
+  if (int r = check_attn_args(dtype, B, H, Lq, Lk, D, mode)) return r;
+  const size_t need = attn_layout(B, H, Lq, Lk, D, mode).total;
+  if (need > kNoAllocScratch)
+    return fail("attention without allocation: these shapes need %zu bytes of scratch, the fixed scratch "
+                "holds %zu (B*H*(Lq + Lk)*D ~ 32 MiB at most); use dc_attn_int8_fwd with a workspace",
+                need, kNoAllocScratch);
+  if (int r = check_sm100()) return r;
+  void* scratch = nullptr;
+  if (int r = noalloc_scratch(&scratch)) return r;
+  // Nothing in the scratch has to start at zero: each call writes every byte it later reads.
+  return attn_common(true, true, q, k, v, dtype, B, H, Lq, Lk, D, q_strides, k_strides, v_strides, sm_scale, mode,
+                     o, o_strides, scratch, kNoAllocScratch, stream);
 }
 
 int dc_selftest_exp2(const float* x, float* poly, float* ref, int64_t n, void* stream) {

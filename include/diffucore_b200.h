@@ -115,6 +115,24 @@ int dc_attn_int8_main(const void* v, int dtype, int64_t B, int64_t H, int64_t Lq
                       const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* dc_attn_int8_fwd for callers that cannot allocate device memory — an application whose GPU
+ * memory is all owned by its own pool and cannot give this library a workspace, or that runs where
+ * cudaMalloc's implicit synchronization is not allowed. Same arguments and results as
+ * dc_attn_int8_fwd minus the workspace: the Q/K codes and scales live in one fixed device array of
+ * DC_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads the library holds until
+ * the process exits. Shapes whose workspace (dc_attn_workspace_size) exceeds that size are
+ * rejected with DC_ERR_INVALID. Allocates nothing (no cudaMalloc / cudaFree). The first call on each
+ * device looks up the array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture. All calls on a device share the one array and it
+ * keeps the last call's contents (nothing in it needs to start at zero); calls that overlap on the
+ * GPU (different streams) race on it, so order them on one stream or with events.
+ * No counterpart in the reference (its pybind `fwd` always allocates its workspace). */
+#define DC_NOALLOC_SCRATCH_BYTES (32u << 20)
+int dc_attn_int8_fwd_noalloc(const void* q, const void* k, const void* v, int dtype, int64_t B, int64_t H,
+                             int64_t Lq, int64_t Lk, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                             const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
+                             void* stream);
+
 /* Accuracy self-test of the attention softmax's FMA-pipe exp2 (range reduction + degree-3
  * polynomial): poly[i] = that exp2(x[i]), ref[i] = CUDA exp2f(x[i]); n even. No counterpart in the
  * reference (its kernel uses the MUFU ex2 only). */
