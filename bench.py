@@ -350,6 +350,84 @@ def bench_gemm(args, dev, peaks):
     }
 
 
+# ─── FLUX-architecture DiT (BASELINE configs 4 and 5) ────────────────────────────────────
+
+FLUX_STEPS = 4          # Euler flow-matching steps (FLUX.1 [schnell], shift 1)
+FLUX_TXT = 512
+
+
+def flux_work(L: int, C: int = 3072, F: int = 12288, H: int = 24, Dh: int = 128, blocks: int = 57) -> dict:
+    """Algorithmic work of one FLUX.1 forward over L tokens: every block's token-wise linears are
+    24 L C^2 int8 ops (double: qkv 6, proj 2, MLP 16 per stream row; single: linear1 14, linear2 10),
+    its attention 2 L^2 Dh H int8 ops (QK^T) + 2 L^2 Dh H bf16 ops (PV)."""
+    lin = blocks * 24 * L * C * C
+    att = blocks * 2 * L * L * Dh * H
+    return {"linear_int8_ops": lin, "attn_int8_ops": att, "attn_bf16_ops": att}
+
+
+def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048)) -> dict:
+    """Seconds per Euler step of the FLUX.1-architecture DiT (random bf16 weights, block linears
+    W8A8 with ConvRot group 256, INT8 attention in the reference's quant mode) at the given image
+    sides: 1024 -> 512 text + 4096 image tokens, 2048 -> 512 + 16384. With world > 1 the tokens are
+    split over the ranks (Ulysses all-to-all around every attention)."""
+    import torch
+    import torch.distributed as dist
+    from diffucore_b200 import _attention, _lib, flux
+    t0 = time.perf_counter()
+    model = flux.build_flux(flux.FluxConfig(), seed=0, device=dev, group=256)
+    _attention.set_attention_backend(model, "int8_turing")
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    pg = dist.group.WORLD if world > 1 else None
+    int8_peak = _int8_peak_tops(peaks) * 1e12
+    bf16_peak = peaks["bf16_tflops"] * 1e12
+    out = {"model": "FLUX.1-schnell architecture (19 double + 38 single blocks, 3072 hidden, 24 heads), "
+                    "random bf16 weights, block linears W8A8 (ConvRot 256), INT8 attention (mode ref)",
+           "steps": FLUX_STEPS, "sampler": "euler, shift 1", "build_s": build_s}
+    for side in sides:
+        lat = side // 8
+        n_img = (lat // 2) ** 2
+        L = FLUX_TXT + n_img
+        runner = flux.FluxRunner(model, FLUX_TXT, n_img, process_group=pg, device=dev, attn_mode=_lib.MODE_REF)
+        runner.set_positions(flux.img_ids(lat, lat, 2, device=dev), flux.txt_ids(FLUX_TXT, device=dev))
+        g = torch.Generator(device=dev).manual_seed(1)
+        x_all = flux.patchify(torch.randn(1, 16, lat, lat, generator=g, device=dev)).to(torch.bfloat16)[0]
+        txt_all = torch.randn(FLUX_TXT, 4096, generator=g, device=dev).to(torch.bfloat16)
+        y = torch.randn(1, 768, generator=g, device=dev).to(torch.bfloat16)
+        i0, i1 = runner.img_rows
+        r0 = runner.rows[0]
+        x, txt = x_all[i0:i1].contiguous(), txt_all[r0: r0 + runner.t_loc].contiguous()
+        sigmas = flux.flow_schedule(FLUX_STEPS, 1.0)
+        xo = flux.euler_sample(runner, x, txt, y, sigmas)          # warm-up: one whole sampling run
+        torch.cuda.synchronize()
+        _barrier(world)
+        s, e = _events(2)
+        s.record()
+        xo = flux.euler_sample(runner, x, txt, y, sigmas)
+        e.record()
+        torch.cuda.synchronize()
+        finite = bool(torch.isfinite(xo).all())
+        s_step = _max_over_ranks(s.elapsed_time(e) * 1e-3 / FLUX_STEPS, world)
+        w = flux_work(L)
+        compute_s = (w["linear_int8_ops"] + w["attn_int8_ops"]) / int8_peak + w["attn_bf16_ops"] / bf16_peak
+        roof = compute_s / world
+        a2a = 0.0
+        if world > 1:
+            Lr = L // world
+            per_block = (Lr * 3 * 3072 + Lr * 3072) * 2 * (world - 1) / world      # bytes sent per rank
+            a2a = 57 * per_block / 770e9                                          # measured peer copy GB/s
+            roof = max(roof, a2a)
+        out[f"{side}px"] = {"tokens": L, "s_per_step": s_step, "n_gpus": world,
+                            "roofline_s_per_step": roof, "frac_of_roofline": roof / s_step,
+                            "a2a_s_per_step_at_770GBps": a2a, "finite": finite,
+                            "work_per_step": {k: v / 1e12 for k, v in w.items()}, "work_unit": "T ops"}
+        del runner, x_all, txt_all, xo
+        torch.cuda.empty_cache()
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -357,8 +435,9 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-extras", action="store_true", help="headline attention only (for profiling)")
-    ap.add_argument("--only", default="all", choices=("all", "gemm"),
-                    help="gemm: time only the config-1 W8A8 linear (for profiling)")
+    ap.add_argument("--only", default="all", choices=("all", "gemm", "flux"),
+                    help="gemm / flux: time only the config-1 W8A8 linear / the FLUX DiT")
+    ap.add_argument("--no-flux", action="store_true", help="skip the FLUX DiT timing")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -371,10 +450,13 @@ def main() -> int:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     peaks = _peaks()
-    if args.only == "gemm":
-        res = bench_gemm(args, dev, peaks)
+    if args.only in ("gemm", "flux"):
+        res = bench_gemm(args, dev, peaks) if args.only == "gemm" else bench_flux(args, world, rank, dev, peaks)
         if rank == 0:
             print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
         return 0
 
     g = torch.Generator().manual_seed(0)
@@ -416,6 +498,10 @@ def main() -> int:
         line["e2e"] = bench_e2e(args, dev)
         if rank == 0 and world == 1:
             line["cpu_baseline"] = _cpu_baseline()
+    if not args.no_extras and not args.no_flux:
+        del plan, sets
+        torch.cuda.empty_cache()
+        line["flux_dit"] = bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048) if world == 1 else (2048,))
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

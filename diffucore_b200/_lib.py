@@ -34,6 +34,15 @@ _SIGNATURES = {
                                      _c_p, _c_p, _c_p]),
     "dc_gemm_w8a8": (ctypes.c_int, [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, ctypes.c_int,
                                     _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_p]),
+    "dc_gemm_w8a8_ex": (ctypes.c_int, [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_p, ctypes.c_int, _c_p, _c_p,
+                                       _c_i64, _c_p, _c_i64, _c_i64, _c_i64, ctypes.c_int, _c_i64, _c_i64, _c_i64,
+                                       _c_p]),
+    "dc_quant_rows_seg": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p,
+                                         _c_i64, ctypes.c_int, _c_p, _c_p, _c_p]),
+    "dc_ln_mod_quant": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64,
+                                       ctypes.c_int, _c_p, _c_p, _c_p]),
+    "dc_qk_norm_rope": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p,
+                                       _c_p, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p]),
     "dc_rescale": (ctypes.c_int, [_c_p, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, ctypes.c_int, _c_i64, _c_i64,
                                   _c_p]),
     "dc_attn_workspace_size": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int,

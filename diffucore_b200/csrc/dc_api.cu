@@ -19,6 +19,7 @@ constexpr size_t kNoAllocScratch = static_cast<size_t>(DC_NOALLOC_SCRATCH_BYTES)
 #include "quant.cuh"
 #include "gemm.cuh"
 #include "attn.cuh"
+#include "dit.cuh"
 
 namespace {
 
@@ -108,13 +109,13 @@ inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
 // ------------------------------------------------------------------------------ quantizer
 
-template <typename T, bool GROUP, int GELU>
-int launch_quant_t(const T* xp, int64_t M, int64_t K, int64_t ldx, int8_t* q, float* s, bool vec, cudaStream_t st) {
+template <typename T, bool GROUP, int GELU, bool SEG = false>
+int launch_quant_t(const dc::RowSrc& src, int64_t M, int64_t K, int8_t* q, float* s, bool vec, cudaStream_t st) {
   if constexpr (!GROUP && GELU == 0 && sizeof(T) == 2) {
     if (vec && K > 4096) {
       const int64_t ctas64 = (M + 3) / 4;
       const int ctas = static_cast<int>(ctas64 < static_cast<int64_t>(sm_count()) * 48 ? ctas64 : sm_count() * 48);
-      dc::quant_rows_stream_kernel<T><<<ctas, 128, 0, st>>>(xp, M, static_cast<int>(K), ldx, q, s);
+      dc::quant_rows_stream_kernel<T, SEG><<<ctas, 128, 0, st>>>(src, M, static_cast<int>(K), q, s);
       DC_CHECK_LAUNCH("quant_rows launch");
       return DC_OK;
     }
@@ -125,21 +126,25 @@ int launch_quant_t(const T* xp, int64_t M, int64_t K, int64_t ldx, int8_t* q, fl
     const int ctas = static_cast<int>(ctas64 < static_cast<int64_t>(sm_count()) * 32 ? ctas64 : sm_count() * 32);
     const int vpt = static_cast<int>((K / 8 + 31) / 32);
     const int Ki = static_cast<int>(K);
-    if (vpt <= 4) dc::quant_rows_warp_kernel<T, 4, GROUP, GELU><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, q, s);
-    else if (vpt <= 8) dc::quant_rows_warp_kernel<T, 8, GROUP, GELU><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, q, s);
-    else if (vpt <= 12) dc::quant_rows_warp_kernel<T, 12, GROUP, GELU><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, q, s);
-    else dc::quant_rows_warp_kernel<T, 16, GROUP, GELU><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, q, s);
+    if (vpt <= 4) dc::quant_rows_warp_kernel<T, 4, GROUP, GELU, SEG><<<ctas, 128, 0, st>>>(src, M, Ki, q, s);
+    else if (vpt <= 8) dc::quant_rows_warp_kernel<T, 8, GROUP, GELU, SEG><<<ctas, 128, 0, st>>>(src, M, Ki, q, s);
+    else if (vpt <= 12) dc::quant_rows_warp_kernel<T, 12, GROUP, GELU, SEG><<<ctas, 128, 0, st>>>(src, M, Ki, q, s);
+    else dc::quant_rows_warp_kernel<T, 16, GROUP, GELU, SEG><<<ctas, 128, 0, st>>>(src, M, Ki, q, s);
   } else if (vec) {
     const int64_t grid64 = M < static_cast<int64_t>(sm_count()) * 16 ? M : static_cast<int64_t>(sm_count()) * 16;
     const int grid = static_cast<int>(grid64);
     const int vpt = static_cast<int>((K / 8 + dc::kQuantThreads - 1) / dc::kQuantThreads);
     const int Ki = static_cast<int>(K);
-    if (vpt <= 8) dc::quant_rows_kernel<T, 8, GROUP, GELU><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, Ki, ldx, q, s);
-    else dc::quant_rows_kernel<T, 16, GROUP, GELU><<<grid, dc::kQuantThreads, 0, st>>>(xp, M, Ki, ldx, q, s);
+    if (vpt <= 8) dc::quant_rows_kernel<T, 8, GROUP, GELU, SEG><<<grid, dc::kQuantThreads, 0, st>>>(src, M, Ki, q, s);
+    else dc::quant_rows_kernel<T, 16, GROUP, GELU, SEG><<<grid, dc::kQuantThreads, 0, st>>>(src, M, Ki, q, s);
   } else {
-    const int64_t grid64 = M < static_cast<int64_t>(sm_count()) * 16 ? M : static_cast<int64_t>(sm_count()) * 16;
-    dc::quant_rows_scalar_kernel<T, GELU><<<static_cast<int>(grid64), dc::kQuantThreads, 0, st>>>(
-        xp, M, static_cast<int>(K), ldx, q, s);
+    if constexpr (!SEG) {
+      const int64_t grid64 = M < static_cast<int64_t>(sm_count()) * 16 ? M : static_cast<int64_t>(sm_count()) * 16;
+      dc::quant_rows_scalar_kernel<T, GELU><<<static_cast<int>(grid64), dc::kQuantThreads, 0, st>>>(
+          static_cast<const T*>(src.x), M, static_cast<int>(K), src.ldx, q, s);
+    } else {
+      return fail("segmented quant_rows needs 16-byte aligned segments");
+    }
   }
   DC_CHECK_LAUNCH("quant_rows launch");
   return DC_OK;
@@ -148,33 +153,63 @@ int launch_quant_t(const T* xp, int64_t M, int64_t K, int64_t ldx, int8_t* q, fl
 template <typename T>
 int launch_quant(const void* x, int64_t M, int64_t K, int64_t ldx, int group, int gelu, int8_t* q, float* s,
                  cudaStream_t st) {
-  const T* xp = static_cast<const T*>(x);
+  const dc::RowSrc src = dc::plain_rows(x, ldx);
   const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(q) % 8 == 0) && K <= 16384;
   if (group != 0 && !vec) return fail("rotated quantization needs K %% 256 == 0, ldx %% 8 == 0, 16-byte aligned rows");
   if constexpr (std::is_same<T, float>::value) {
-    return group ? launch_quant_t<T, true, 0>(xp, M, K, ldx, q, s, vec, st)
-                 : launch_quant_t<T, false, 0>(xp, M, K, ldx, q, s, vec, st);
+    return group ? launch_quant_t<T, true, 0>(src, M, K, q, s, vec, st)
+                 : launch_quant_t<T, false, 0>(src, M, K, q, s, vec, st);
   } else {
     switch (gelu) {
       case DC_GELU_ERF:
-        return group ? launch_quant_t<T, true, 1>(xp, M, K, ldx, q, s, vec, st)
-                     : launch_quant_t<T, false, 1>(xp, M, K, ldx, q, s, vec, st);
+        return group ? launch_quant_t<T, true, 1>(src, M, K, q, s, vec, st)
+                     : launch_quant_t<T, false, 1>(src, M, K, q, s, vec, st);
       case DC_GELU_TANH:
-        return group ? launch_quant_t<T, true, 2>(xp, M, K, ldx, q, s, vec, st)
-                     : launch_quant_t<T, false, 2>(xp, M, K, ldx, q, s, vec, st);
+        return group ? launch_quant_t<T, true, 2>(src, M, K, q, s, vec, st)
+                     : launch_quant_t<T, false, 2>(src, M, K, q, s, vec, st);
       default:
-        return group ? launch_quant_t<T, true, 0>(xp, M, K, ldx, q, s, vec, st)
-                     : launch_quant_t<T, false, 0>(xp, M, K, ldx, q, s, vec, st);
+        return group ? launch_quant_t<T, true, 0>(src, M, K, q, s, vec, st)
+                     : launch_quant_t<T, false, 0>(src, M, K, q, s, vec, st);
     }
   }
 }
 
+// ------------------------------------------------------------------------------ DiT glue
+
+template <typename T, bool GROUP>
+int launch_ln_mod_quant(const void* x, int64_t M, int64_t K, int64_t ldx, const void* shift, const void* scale,
+                        int64_t rows_per_mod, int64_t mod_ld, int8_t* q, float* s, cudaStream_t st) {
+  const int64_t ctas64 = (M + 3) / 4;
+  const int ctas = static_cast<int>(ctas64 < static_cast<int64_t>(sm_count()) * 32 ? ctas64 : sm_count() * 32);
+  const int vpt = static_cast<int>((K / 8 + 31) / 32);
+  const int Ki = static_cast<int>(K);
+  const T* xp = static_cast<const T*>(x);
+  const T* sh = static_cast<const T*>(shift);
+  const T* sc = static_cast<const T*>(scale);
+  if (vpt <= 4) dc::ln_mod_quant_kernel<T, 4, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s);
+  else if (vpt <= 8) dc::ln_mod_quant_kernel<T, 8, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s);
+  else if (vpt <= 12) dc::ln_mod_quant_kernel<T, 12, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s);
+  else dc::ln_mod_quant_kernel<T, 16, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s);
+  DC_CHECK_LAUNCH("ln_mod_quant launch");
+  return DC_OK;
+}
+
 // ------------------------------------------------------------------------------ GEMM
 
-template <int BN, int OUT, bool HAS_BIAS, int GELU>
+// Epilogue options beyond rescale / bias / GELU.
+struct GemmEpi {
+  const void* gate = nullptr;       // with residual: out = dtype(residual + dtype(gate * y))
+  const void* residual = nullptr;
+  int64_t ldr = 0;
+  int64_t col_block = 0;            // > 0: column-block output layout
+  int64_t block_stride = 0;
+};
+
+template <int BN, int OUT, bool HAS_BIAS, int GELU, bool GATED>
 int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
-                const void* bias, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+                const void* bias, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K, const GemmEpi& epi,
+                cudaStream_t st) {
   constexpr int STAGES = BN == 256 ? 4 : 6;
   using S = dc::GemmSmem<BN, STAGES>;
   CUtensorMap ta, tb;
@@ -199,7 +234,9 @@ int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, cons
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.num_kb = static_cast<int>((K + dc::kGemmBK - 1) / dc::kGemmBK);
   p.sx = sx; p.sw = sw; p.bias = bias; p.out = out; p.ldo = ldo;
-  auto kernel = dc::gemm_w8a8_kernel<BN, STAGES, OUT, HAS_BIAS, GELU>;
+  p.gate = epi.gate; p.residual = epi.residual; p.ldr = epi.ldr;
+  p.col_block = epi.col_block; p.block_stride = epi.block_stride;
+  auto kernel = dc::gemm_w8a8_kernel<BN, STAGES, OUT, HAS_BIAS, GELU, GATED>;
   int r = set_smem(kernel, S::kDynamic);
   if (r) return r;
   const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
@@ -211,22 +248,68 @@ int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, cons
 template <int BN, int OUT>
 int dispatch_gemm_epilogue(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx,
                            const float* sw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
-                           int64_t K, int gelu, cudaStream_t st) {
+                           int64_t K, int gelu, const GemmEpi& epi, cudaStream_t st) {
   if constexpr (OUT == dc::kOutI32) {
-    return launch_gemm<BN, OUT, false, 0>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, st);
+    return launch_gemm<BN, OUT, false, 0, false>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, epi, st);
   } else {
-  const bool b = bias != nullptr;
-  switch (gelu) {
-    case DC_GELU_NONE:
-      return b ? launch_gemm<BN, OUT, true, 0>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st)
-               : launch_gemm<BN, OUT, false, 0>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st);
-    case DC_GELU_ERF:
-      return b ? launch_gemm<BN, OUT, true, 1>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st)
-               : launch_gemm<BN, OUT, false, 1>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st);
-    default:
-      return b ? launch_gemm<BN, OUT, true, 2>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st)
-               : launch_gemm<BN, OUT, false, 2>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, st);
+    const bool b = bias != nullptr;
+    if (epi.residual != nullptr) {
+      return b ? launch_gemm<BN, OUT, true, 0, true>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
+               : launch_gemm<BN, OUT, false, 0, true>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
+    }
+    switch (gelu) {
+      case DC_GELU_NONE:
+        return b ? launch_gemm<BN, OUT, true, 0, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
+                 : launch_gemm<BN, OUT, false, 0, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
+      case DC_GELU_ERF:
+        return b ? launch_gemm<BN, OUT, true, 1, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
+                 : launch_gemm<BN, OUT, false, 1, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
+      default:
+        return b ? launch_gemm<BN, OUT, true, 2, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
+                 : launch_gemm<BN, OUT, false, 2, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
+    }
   }
+}
+
+int gemm_checked(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
+                 const void* bias, void* out, int64_t ldo, int out_dtype, int64_t M, int64_t N, int64_t K, int gelu,
+                 const GemmEpi& epi, cudaStream_t st) {
+  if (M < 0 || N <= 0 || K <= 0) return fail("gemm: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (M == 0) return DC_OK;
+  if (K % 16) return fail("gemm: K=%lld must be a multiple of 16 (TMA row pitch)", (long long)K);
+  if (ldq % 16 || ldw % 16) return fail("gemm: ldq/ldw must be multiples of 16 bytes");
+  if (ldq < K || ldw < K) return fail("gemm: leading dimension smaller than the row");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail("gemm: dimension above 2^31");
+  if (gelu < 0 || gelu > 2) return fail("unknown gelu mode %d", gelu);
+  if (out_dtype != DC_DTYPE_I32 && (sx == nullptr || sw == nullptr)) return fail("gemm: scales are required");
+  if (out_dtype == DC_DTYPE_I32 && (bias != nullptr || gelu)) return fail("gemm: int32 output takes no bias or gelu");
+  if ((epi.gate == nullptr) != (epi.residual == nullptr)) return fail("gemm: gate and residual go together");
+  if (epi.residual != nullptr) {
+    if (out_dtype == DC_DTYPE_I32) return fail("gemm: a gated residual needs a 16-bit output");
+    if (gelu) return fail("gemm: a gated residual takes no gelu");
+    if (epi.ldr < N) return fail("gemm: residual leading dimension smaller than the row");
+  }
+  // Wide tiles unless the column blocks are not a multiple of them.
+  bool wide = N > 128;
+  if (epi.col_block > 0) {
+    if (epi.col_block % 128 || epi.block_stride % 8) return fail("gemm: col_block must be a multiple of 128 and block_stride of 8");
+    if (ldo < epi.col_block) return fail("gemm: ldo smaller than col_block");
+    if (epi.col_block % 256) wide = false;
+  } else if (ldo < N) {
+    return fail("gemm: leading dimension smaller than the row");
+  }
+  if (int r = check_sm100()) return r;
+  switch (out_dtype) {
+    case DC_DTYPE_BF16:
+      return wide ? dispatch_gemm_epilogue<256, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st)
+                  : dispatch_gemm_epilogue<128, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st);
+    case DC_DTYPE_F16:
+      return wide ? dispatch_gemm_epilogue<256, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st)
+                  : dispatch_gemm_epilogue<128, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st);
+    case DC_DTYPE_I32:
+      return wide ? dispatch_gemm_epilogue<256, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, epi, st)
+                  : dispatch_gemm_epilogue<128, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, epi, st);
+    default: return fail("gemm: unsupported output dtype %d", out_dtype);
   }
 }
 
@@ -433,30 +516,101 @@ int dc_quant_rows(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
 int dc_gemm_w8a8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
                  const void* bias, void* out, int64_t ldo, int out_dtype, int64_t M, int64_t N, int64_t K,
                  int gelu, void* stream) {
-  if (M < 0 || N <= 0 || K <= 0) return fail("gemm: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  return gemm_checked(q, ldq, w, ldw, sx, sw, bias, out, ldo, out_dtype, M, N, K, gelu, GemmEpi(),
+                      static_cast<cudaStream_t>(stream));
+}
+
+int dc_gemm_w8a8_ex(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
+                    const void* bias, int gelu, const void* gate, const void* residual, int64_t ldr, void* out,
+                    int64_t ldo, int64_t col_block, int64_t block_stride, int out_dtype, int64_t M, int64_t N,
+                    int64_t K, void* stream) {
+  GemmEpi epi;
+  epi.gate = gate; epi.residual = residual; epi.ldr = ldr;
+  epi.col_block = col_block; epi.block_stride = block_stride;
+  if (col_block < 0 || (col_block == 0 && block_stride != 0)) return fail("gemm: bad column-block layout");
+  return gemm_checked(q, ldq, w, ldw, sx, sw, bias, out, ldo, out_dtype, M, N, K, gelu, epi,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int dc_quant_rows_seg(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int64_t seg_len,
+                      int64_t seg_stride, int64_t k1, const void* x2, int64_t ldx2, int group, int8_t* q, float* s,
+                      void* stream) {
+  if (M < 0 || K <= 0) return fail("quant_rows_seg: bad shape");
   if (M == 0) return DC_OK;
-  if (K % 16) return fail("gemm: K=%lld must be a multiple of 16 (TMA row pitch)", (long long)K);
-  if (ldq % 16 || ldw % 16) return fail("gemm: ldq/ldw must be multiples of 16 bytes");
-  if (ldq < K || ldw < K || ldo < N) return fail("gemm: leading dimension smaller than the row");
-  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail("gemm: dimension above 2^31");
-  if (gelu < 0 || gelu > 2) return fail("unknown gelu mode %d", gelu);
-  if (out_dtype != DC_DTYPE_I32 && (sx == nullptr || sw == nullptr)) return fail("gemm: scales are required");
-  if (out_dtype == DC_DTYPE_I32 && (bias != nullptr || gelu)) return fail("gemm: int32 output takes no bias or gelu");
+  if (group != 0 && group != 256) return fail("ConvRot group must be 0 or 256 (got %d)", group);
+  if (group && K % 256) return fail("K=%lld is not a multiple of the ConvRot group 256", (long long)K);
+  if (K % 8 || K > 16384) return fail("quant_rows_seg: K must be a multiple of 8 and at most 16384");
+  if (seg_len <= 0 || seg_len % 8 || k1 <= 0 || k1 > K || k1 % seg_len)
+    return fail("quant_rows_seg: seg_len must be a positive multiple of 8 dividing k1, 0 < k1 <= K");
+  if (seg_stride % 8 || ldx % 8 || ldx < seg_len) return fail("quant_rows_seg: strides must be multiples of 8 elements");
+  if (k1 < K && (x2 == nullptr || ldx2 % 8 || ldx2 < K - k1 || reinterpret_cast<uintptr_t>(x2) % 16))
+    return fail("quant_rows_seg: the second operand needs a 16-byte aligned base and ldx2 >= K - k1, a multiple of 8");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(q) % 8)
+    return fail("quant_rows_seg: x must be 16-byte and q 8-byte aligned");
+  if (x_dtype != DC_DTYPE_BF16 && x_dtype != DC_DTYPE_F16) return fail("quant_rows_seg: dtype must be fp16 or bf16");
+  if (int r = check_sm100()) return r;
+  dc::RowSrc src;
+  src.x = x; src.ldx = ldx; src.seg_len = static_cast<int>(seg_len); src.seg_stride = seg_stride;
+  src.k1 = static_cast<int>(k1); src.x2 = x2; src.ldx2 = ldx2;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (x_dtype == DC_DTYPE_BF16)
+    return group ? launch_quant_t<__nv_bfloat16, true, 0, true>(src, M, K, q, s, true, st)
+                 : launch_quant_t<__nv_bfloat16, false, 0, true>(src, M, K, q, s, true, st);
+  return group ? launch_quant_t<__half, true, 0, true>(src, M, K, q, s, true, st)
+               : launch_quant_t<__half, false, 0, true>(src, M, K, q, s, true, st);
+}
+
+int dc_ln_mod_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const void* shift,
+                    const void* scale, int64_t rows_per_mod, int64_t mod_ld, int group, int8_t* q, float* s,
+                    void* stream) {
+  if (M < 0 || K <= 0) return fail("ln_mod_quant: bad shape");
+  if (M == 0) return DC_OK;
+  if (group != 0 && group != 256) return fail("ConvRot group must be 0 or 256 (got %d)", group);
+  if (group && K % 256) return fail("K=%lld is not a multiple of the ConvRot group 256", (long long)K);
+  if (K % 8 || K > 4096) return fail("ln_mod_quant: K must be a multiple of 8 and at most 4096");
+  if (ldx < K || ldx % 8 || mod_ld % 8 || rows_per_mod <= 0) return fail("ln_mod_quant: bad strides");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(shift) % 16 ||
+      reinterpret_cast<uintptr_t>(scale) % 16 || reinterpret_cast<uintptr_t>(q) % 8)
+    return fail("ln_mod_quant: x, shift, scale must be 16-byte and q 8-byte aligned");
   if (int r = check_sm100()) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool wide = N > 128;
-  switch (out_dtype) {
+  switch (x_dtype) {
     case DC_DTYPE_BF16:
-      return wide ? dispatch_gemm_epilogue<256, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st)
-                  : dispatch_gemm_epilogue<128, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st);
+      return group ? launch_ln_mod_quant<__nv_bfloat16, true>(x, M, K, ldx, shift, scale, rows_per_mod, mod_ld, q, s, st)
+                   : launch_ln_mod_quant<__nv_bfloat16, false>(x, M, K, ldx, shift, scale, rows_per_mod, mod_ld, q, s, st);
     case DC_DTYPE_F16:
-      return wide ? dispatch_gemm_epilogue<256, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st)
-                  : dispatch_gemm_epilogue<128, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, st);
-    case DC_DTYPE_I32:
-      return wide ? dispatch_gemm_epilogue<256, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, st)
-                  : dispatch_gemm_epilogue<128, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, st);
-    default: return fail("gemm: unsupported output dtype %d", out_dtype);
+      return group ? launch_ln_mod_quant<__half, true>(x, M, K, ldx, shift, scale, rows_per_mod, mod_ld, q, s, st)
+                   : launch_ln_mod_quant<__half, false>(x, M, K, ldx, shift, scale, rows_per_mod, mod_ld, q, s, st);
+    default: return fail("ln_mod_quant: dtype must be fp16 or bf16");
   }
+}
+
+int dc_qk_norm_rope(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64_t ld_row, int64_t q_off,
+                    int64_t k_off, const void* q_scale0, const void* k_scale0, const void* q_scale1,
+                    const void* k_scale1, int64_t split_row, const float* pe, int64_t pe_row0, void* stream) {
+  if (L < 0 || H <= 0) return fail("qk_norm_rope: bad shape");
+  if (L == 0) return DC_OK;
+  if (D != 128) return fail("qk_norm_rope: head dim must be 128 (got %lld)", (long long)D);
+  if (ld_row % 4 || q_off % 4 || k_off % 4 || reinterpret_cast<uintptr_t>(qkv) % 8)
+    return fail("qk_norm_rope: rows and offsets must be 8-byte aligned");
+  if (q_scale0 == nullptr || k_scale0 == nullptr || pe == nullptr) return fail("qk_norm_rope: scales and pe are required");
+  if (split_row < L && (q_scale1 == nullptr || k_scale1 == nullptr)) return fail("qk_norm_rope: second scales missing");
+  if (pe_row0 < 0) return fail("qk_norm_rope: pe_row0 < 0");
+  if (int r = check_sm100()) return r;
+  dc::QkNormRopeParams p;
+  p.qkv = qkv; p.L = L; p.H = H; p.ld_row = ld_row; p.q_off = q_off; p.k_off = k_off;
+  p.q_scale[0] = q_scale0; p.k_scale[0] = k_scale0;
+  p.q_scale[1] = q_scale1 ? q_scale1 : q_scale0; p.k_scale[1] = k_scale1 ? k_scale1 : k_scale0;
+  p.split_row = split_row; p.pe = pe; p.pe_row0 = pe_row0;
+  const int64_t tasks = L * H * 2;
+  const int64_t ctas64 = (tasks + 7) / 8;
+  const int ctas = static_cast<int>(ctas64 < static_cast<int64_t>(sm_count()) * 16 ? ctas64 : sm_count() * 16);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == DC_DTYPE_BF16) dc::qk_norm_rope_kernel<__nv_bfloat16><<<ctas, 256, 0, st>>>(p);
+  else if (dtype == DC_DTYPE_F16) dc::qk_norm_rope_kernel<__half><<<ctas, 256, 0, st>>>(p);
+  else return fail("qk_norm_rope: dtype must be fp16 or bf16");
+  DC_CHECK_LAUNCH("qk_norm_rope launch");
+  return DC_OK;
 }
 
 int dc_rescale(const int32_t* acc, int64_t lda, const float* sx, const float* sw, const void* bias, void* out,

@@ -1,0 +1,181 @@
+// Producer-side glue of a FLUX-architecture DiT block, fused around the W8A8 linears and the
+// INT8 attention (HBM-bound, one read and one write of each row):
+//
+//  * ln_mod_quant_kernel: LayerNorm (no affine, eps 1e-6) -> AdaLN modulation -> optional
+//    256-wide rotation -> per-row int8 codes. It replaces the torch sequence
+//        x_mod = (1 + mod.scale) * norm(x) + mod.shift        (src/diffucore/models/flux_dit.py:282,
+//                                                              :287, :328)
+//    followed by `Int8Linear.forward`'s `quantize_activation` (src/diffucore/models/_int8.py:299-310),
+//    so the modulated activation never exists in HBM. Each torch op of that sequence rounds to the
+//    model dtype; the kernel rounds at the same points: n = dtype(LN(x)), a = dtype(1 + scale),
+//    t = dtype(a * n), y = dtype(t + shift).
+//  * qk_norm_rope_kernel: per-head RMSNorm of q and k with their learned scales, then the axial
+//    RoPE rotation, in place on the packed qkv rows (flux_dit.py:129-151 `RMSNorm`/`QKNorm`,
+//    :179-184 `apply_rope`). Rounding points as in torch: dtype(x * rrms), dtype(that * scale),
+//    RoPE in fp32 as two products and a sum, then dtype.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+#include <type_traits>
+#include "sm100.cuh"
+#include "quant.cuh"
+#include "gemm.cuh"
+
+namespace dc {
+
+template <typename T>
+__device__ __forceinline__ float rnd(float x) { return Vec8<T>::round_trip(x); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Warp per row, K <= 32 * 8 * VPT, K % 8 == 0 (K % 256 == 0 with GROUP). Rows of batch element b
+// (b = row / rows_per_mod) use shift/scale + b * mod_ld.
+template <typename T, int VPT, bool GROUP>
+__global__ void __launch_bounds__(128)
+ln_mod_quant_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, const T* __restrict__ shift,
+                    const T* __restrict__ scale, int64_t rows_per_mod, int64_t mod_ld, int8_t* __restrict__ q,
+                    float* __restrict__ s) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = K >> 3;
+  const float inv_k = 1.0f / static_cast<float>(K);
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
+       row += warps) {
+    const T* xr = x + row * ldx;
+    float v[VPT][8];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) {
+        Vec8<T>::load(xr + vi * 8, v[i]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+      }
+    }
+    // mean and biased variance in fp32 (two passes over registers)
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc += v[i][j];
+    const float mean = __fmul_rn(warp_sum(acc), inv_k);
+    acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { const float d = __fsub_rn(v[i][j], mean); acc = __fmaf_rn(d, d, acc); }
+      }
+    }
+    const float rstd = rsqrtf(__fadd_rn(__fmul_rn(warp_sum(acc), inv_k), 1e-6f));
+    const int64_t b = row / rows_per_mod;
+    const T* shr = shift + b * mod_ld;
+    const T* scr = scale + b * mod_ld;
+    float am = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) {
+        float sh[8], sc[8];
+        Vec8<T>::load(shr + vi * 8, sh);
+        Vec8<T>::load(scr + vi * 8, sc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float n = rnd<T>(__fmul_rn(__fsub_rn(v[i][j], mean), rstd));
+          const float a = rnd<T>(__fadd_rn(1.0f, sc[j]));
+          v[i][j] = rnd<T>(__fadd_rn(rnd<T>(__fmul_rn(a, n)), sh[j]));
+        }
+      }
+      // the 32 lanes at one i hold one 256-wide group; lanes past the row end hold zeros
+      if (GROUP) hadamard256_warp(v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(v[i][j]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const float sc = fmaxf(__fdiv_rn(am, 127.0f), 1e-30f);
+    const float inv = __fdiv_rn(1.0f, sc);
+    int8_t* qr = q + row * static_cast<int64_t>(K);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant8(v[i], sc, inv);
+    }
+    if (lane == 0) s[row] = sc;
+  }
+}
+
+struct QkNormRopeParams {
+  void* qkv;                 // row r, head h: q at qkv + r*ld_row + q_off + h*128, k at + k_off
+  int64_t L, H, ld_row, q_off, k_off;
+  const void* q_scale[2];    // per-dim RMSNorm scales: [0] for rows < split_row, [1] for the rest
+  const void* k_scale[2];
+  int64_t split_row;
+  const float* pe;           // [L, 64, 2, 2] fp32: rows {cos, -sin}, {sin, cos} per rotary pair
+  int64_t pe_row0;           // row r of qkv uses pe row pe_row0 + r
+};
+
+// One warp per (row, head, q|k) vector of 128: lane holds elements 4 lane .. 4 lane + 3, i.e.
+// rotary pairs 2 lane and 2 lane + 1.
+template <typename T>
+__global__ void __launch_bounds__(256)
+qk_norm_rope_kernel(const QkNormRopeParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t tasks = p.L * p.H * 2;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < tasks; t += nwarps) {
+    const int64_t row = t / (2 * p.H);
+    const int rem = static_cast<int>(t - row * 2 * p.H);
+    const int is_k = rem & 1;
+    const int h = rem >> 1;
+    T* base = static_cast<T*>(p.qkv) + row * p.ld_row + (is_k ? p.k_off : p.q_off) + static_cast<int64_t>(h) * 128 + lane * 4;
+    const bool first = row < p.split_row;
+    const void* sv = is_k ? (first ? p.k_scale[0] : p.k_scale[1]) : (first ? p.q_scale[0] : p.q_scale[1]);
+    const T* scl = static_cast<const T*>(sv) + lane * 4;
+    const float4* pe4 = reinterpret_cast<const float4*>(p.pe + (p.pe_row0 + row) * 256 + lane * 8);
+    const uint2 raw = *reinterpret_cast<const uint2*>(base);
+    const uint2 sraw = *reinterpret_cast<const uint2*>(scl);
+    const float4 f0 = pe4[0], f1 = pe4[1];
+    float x[4], g[4];
+    {
+      const uint4 u = make_uint4(raw.x, raw.y, 0u, 0u);
+      const uint4 su = make_uint4(sraw.x, sraw.y, 0u, 0u);
+      float tmp[8], stmp[8];
+      Vec8<T>::from_raw(u, tmp);
+      Vec8<T>::from_raw(su, stmp);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { x[j] = tmp[j]; g[j] = stmp[j]; }
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(x[j], x[j]));
+    const float rrms = rsqrtf(__fadd_rn(__fmul_rn(warp_sum(ss), 1.0f / 128.0f), 1e-6f));
+    float y[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) y[j] = rnd<T>(__fmul_rn(rnd<T>(__fmul_rn(x[j], rrms)), g[j]));
+    // pair 0: (y0, y1) with f0 = {f00, f01, f10, f11}; pair 1: (y2, y3) with f1
+    float o[4];
+    o[0] = rnd<T>(__fadd_rn(__fmul_rn(f0.x, y[0]), __fmul_rn(f0.y, y[1])));
+    o[1] = rnd<T>(__fadd_rn(__fmul_rn(f0.z, y[0]), __fmul_rn(f0.w, y[1])));
+    o[2] = rnd<T>(__fadd_rn(__fmul_rn(f1.x, y[2]), __fmul_rn(f1.y, y[3])));
+    o[3] = rnd<T>(__fadd_rn(__fmul_rn(f1.z, y[2]), __fmul_rn(f1.w, y[3])));
+    uint2 out;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      out.x = pack_bf16x2(o[0], o[1]);
+      out.y = pack_bf16x2(o[2], o[3]);
+    } else {
+      out.x = pack_f16x2(o[0], o[1]);
+      out.y = pack_f16x2(o[2], o[3]);
+    }
+    *reinterpret_cast<uint2*>(base) = out;
+  }
+}
+
+}  // namespace dc

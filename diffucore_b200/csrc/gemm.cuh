@@ -10,6 +10,12 @@
 // The epilogue rounds exactly like the reference's `rescale` (src/diffucore/models/_int8.py:313-323):
 //   y = dtype(float(acc) * (sx[m] * sw[n]));  if bias: y = dtype(float(y) + float(bias[n]))
 // and with OUT_I32 it writes the raw accumulator (the reference's `int_mm`, _int8.py:200-207).
+// GATED adds a DiT residual branch in the same pass: out = dtype(res + dtype(gate[n] * y)), the
+// rounding of `x + mod.gate * linear(h)` in the model dtype (src/diffucore/models/flux_dit.py:302-305,
+// :339); res may be the output itself (each element is read before it is written, by one thread).
+// A column-block output (col_block > 0) stores column n of row m at
+//   out + (n / col_block) * block_stride + m * ldo + n % col_block,
+// which lays a projection's output out as [blocks, M, col_block] for an all-to-all.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -33,6 +39,11 @@ struct GemmParams {
   const void* bias;      // dtype of the output (bf16 / fp16), or null
   void* out;
   int64_t ldo;           // output row stride in elements
+  const void* gate;      // GATED: [N] in the output dtype
+  const void* residual;  // GATED: [M, N] with row stride ldr, in the output dtype
+  int64_t ldr;
+  int64_t col_block;     // 0: plain [M, N] output; else a multiple of BN (see above)
+  int64_t block_stride;  // elements between column blocks
 };
 
 template <int BN, int STAGES>
@@ -79,7 +90,15 @@ __device__ __forceinline__ float epi_value(uint32_t acc_bits, float sxr, float s
   return y;
 }
 
-template <int BN, int STAGES, int OUT, bool HAS_BIAS, int GELU>
+// out = dtype(res + dtype(gate * y)), res given as its 16-bit pattern.
+template <int OUT>
+__device__ __forceinline__ float gated_residual(uint32_t res_bits, float gate, float y) {
+  const float rv = OUT == kOutBF16 ? __uint_as_float(res_bits << 16)
+                                   : __half2float(__ushort_as_half(static_cast<unsigned short>(res_bits)));
+  return out_round<OUT>(__fadd_rn(rv, out_round<OUT>(__fmul_rn(gate, y))));
+}
+
+template <int BN, int STAGES, int OUT, bool HAS_BIAS, int GELU, bool GATED = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                  const GemmParams p) {
@@ -95,6 +114,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ __align__(16) float col_sw[kGemmEpiWarps][kHalf];    // per-warp staging of sw / bias
   __shared__ __align__(16) float col_bias[kGemmEpiWarps][kHalf];
+  __shared__ __align__(16) float col_gate[GATED ? kGemmEpiWarps : 1][GATED ? kHalf : 4];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
 
@@ -182,6 +202,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     const int row_in_tile = quarter * 32 + lane;
     float* my_sw = col_sw[ew];
     float* my_bias = col_bias[ew];
+    float* my_gate = col_gate[GATED ? ew : 0];
     int local = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
       const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
@@ -195,6 +216,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
           const int n = ncol0 + i;
           my_sw[i] = n < p.N ? p.sw[n] : 0.0f;
           if (HAS_BIAS) my_bias[i] = n < p.N ? bias_at<OUT>(p.bias, n) : 0.0f;
+          if (GATED) my_gate[i] = n < p.N ? bias_at<OUT>(p.gate, n) : 0.0f;
         }
         __syncwarp();
       }
@@ -205,6 +227,14 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       const bool row_ok = row < p.M;
       const float sxr = (OUT != kOutI32 && row_ok) ? p.sx[row] : 0.0f;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + half * kHalf;
+      // output tile origin: with column blocks the tile lies inside one block (col_block % BN == 0)
+      int64_t out_off = static_cast<int64_t>(row) * p.ldo;
+      int col_base = 0;                                   // first column of the tile's block
+      if (p.col_block > 0) {
+        const int64_t blk = static_cast<int64_t>(tn * BN) / p.col_block;
+        out_off += blk * p.block_stride;
+        col_base = static_cast<int>(blk * p.col_block);
+      }
 #pragma unroll 1
       for (int c = 0; c < kHalf; c += 32) {
         uint32_t r[32];
@@ -213,7 +243,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         const int col0 = ncol0 + c;
         if (!row_ok || col0 >= p.N) continue;
         if (OUT == kOutI32) {
-          int32_t* dst = reinterpret_cast<int32_t*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0;
+          int32_t* dst = reinterpret_cast<int32_t*>(p.out) + out_off + (col0 - col_base);
           if (col0 + 32 <= p.N && (p.ldo & 3) == 0) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
@@ -224,17 +254,42 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
               if (col0 + j < p.N) dst[j] = static_cast<int32_t>(r[j]);
           }
         } else {
-          uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0;
+          uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + out_off + (col0 - col_base);
           uint32_t w[16];
+          uint32_t res[16];
+          if (GATED) {
+            const uint16_t* rp = reinterpret_cast<const uint16_t*>(p.residual) + static_cast<int64_t>(row) * p.ldr + col0;
+            if (col0 + 32 <= p.N && (p.ldr & 7) == 0) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                const uint4 u = *reinterpret_cast<const uint4*>(rp + 2 * j);
+                res[j] = u.x; res[j + 1] = u.y; res[j + 2] = u.z; res[j + 3] = u.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const uint32_t lo = col0 + 2 * j < p.N ? rp[2 * j] : 0u;
+                const uint32_t hi = col0 + 2 * j + 1 < p.N ? rp[2 * j + 1] : 0u;
+                res[j] = lo | (hi << 16);
+              }
+            }
+          }
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
             const float4 s4 = *reinterpret_cast<const float4*>(my_sw + c + j);
             float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
             if (HAS_BIAS) b4 = *reinterpret_cast<const float4*>(my_bias + c + j);
-            const float y0 = epi_value<OUT, HAS_BIAS, GELU>(r[j], sxr, s4.x, b4.x);
-            const float y1 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 1], sxr, s4.y, b4.y);
-            const float y2 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 2], sxr, s4.z, b4.z);
-            const float y3 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 3], sxr, s4.w, b4.w);
+            float y0 = epi_value<OUT, HAS_BIAS, GELU>(r[j], sxr, s4.x, b4.x);
+            float y1 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 1], sxr, s4.y, b4.y);
+            float y2 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 2], sxr, s4.z, b4.z);
+            float y3 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 3], sxr, s4.w, b4.w);
+            if (GATED) {
+              const float4 g4 = *reinterpret_cast<const float4*>(my_gate + c + j);
+              y0 = gated_residual<OUT>(res[j / 2] & 0xFFFFu, g4.x, y0);
+              y1 = gated_residual<OUT>(res[j / 2] >> 16, g4.y, y1);
+              y2 = gated_residual<OUT>(res[j / 2 + 1] & 0xFFFFu, g4.z, y2);
+              y3 = gated_residual<OUT>(res[j / 2 + 1] >> 16, g4.w, y3);
+            }
             w[j / 2] = OUT == kOutBF16 ? pack_bf16x2(y0, y1) : pack_f16x2(y0, y1);
             w[j / 2 + 1] = OUT == kOutBF16 ? pack_bf16x2(y2, y3) : pack_f16x2(y2, y3);
           }

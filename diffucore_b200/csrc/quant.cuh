@@ -137,6 +137,37 @@ __device__ __forceinline__ void hadamard256_warp(float (&x)[8]) {
   }
 }
 
+// Where element c of row r lives. Plain rows (SEG false): x + r * ldx + c. Segmented rows: the
+// first k1 elements are spread over segments of seg_len elements, segment i starting at
+// x + i * seg_stride (row r at + r * ldx inside it); elements k1.. come from x2 + r * ldx2 + (c - k1).
+// The segmented form reads an all-to-all's receive buffer [P, rows, seg_len] (and a second operand
+// concatenated after it) as one row without a copy. seg_len and k1 are multiples of 8.
+struct RowSrc {
+  const void* x;
+  int64_t ldx;
+  int seg_len;
+  int64_t seg_stride;
+  int k1;
+  const void* x2;
+  int64_t ldx2;
+};
+
+__host__ __device__ inline RowSrc plain_rows(const void* x, int64_t ldx) {
+  RowSrc r;
+  r.x = x; r.ldx = ldx; r.seg_len = 0; r.seg_stride = 0; r.k1 = 0; r.x2 = nullptr; r.ldx2 = 0;
+  return r;
+}
+
+template <typename T, bool SEG>
+__device__ __forceinline__ const T* src_ptr(const RowSrc& s, int64_t row, int c) {
+  if (!SEG) return static_cast<const T*>(s.x) + row * s.ldx + c;
+  if (c < s.k1) {
+    const int seg = c / s.seg_len;
+    return static_cast<const T*>(s.x) + seg * s.seg_stride + row * s.ldx + (c - seg * s.seg_len);
+  }
+  return static_cast<const T*>(s.x2) + row * s.ldx2 + (c - s.k1);
+}
+
 __device__ __forceinline__ int8_t quant_code(float x, float scale) {
   float t = rintf(__fdiv_rn(x, scale));
   t = fminf(fmaxf(t, -128.0f), 127.0f);
@@ -180,24 +211,23 @@ __device__ __forceinline__ uint2 quant8(const float (&v)[8], float scale, float 
 // Plain rows (no rotation, no GELU), 16-bit input: warp per row in two streaming passes, amax
 // then codes. The second pass re-reads the row from L2 (the rows in flight are a few MB), so
 // registers stay few and many rows are in flight per SM.
-template <typename T>
+template <typename T, bool SEG = false>
 __global__ void __launch_bounds__(128, 12)
-quant_rows_stream_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int8_t* __restrict__ q,
-                         float* __restrict__ s) {
+quant_rows_stream_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, float* __restrict__ s) {
   constexpr int kBatch = 4;
   const int lane = threadIdx.x & 31;
   const int nvec = K >> 3;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
        row += warps) {
-    const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
     uint32_t am2 = 0u;
     for (int v0 = lane; v0 < nvec; v0 += 32 * kBatch) {
       uint4 raw[kBatch];
 #pragma unroll
       for (int b = 0; b < kBatch; ++b) {
         const int vi = v0 + 32 * b;
-        raw[b] = vi < nvec ? __ldg(xr + vi) : make_uint4(0, 0, 0, 0);
+        raw[b] = vi < nvec ? __ldg(reinterpret_cast<const uint4*>(src_ptr<T, SEG>(src, row, vi * 8)))
+                           : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
       for (int b = 0; b < kBatch; ++b) {
@@ -216,7 +246,8 @@ quant_rows_stream_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx,
 #pragma unroll
       for (int b = 0; b < kBatch; ++b) {
         const int vi = v0 + 32 * b;
-        raw[b] = vi < nvec ? __ldg(xr + vi) : make_uint4(0, 0, 0, 0);
+        raw[b] = vi < nvec ? __ldg(reinterpret_cast<const uint4*>(src_ptr<T, SEG>(src, row, vi * 8)))
+                           : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
       for (int b = 0; b < kBatch; ++b) {
@@ -232,10 +263,9 @@ quant_rows_stream_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx,
   }
 }
 
-template <typename T, int VPT, bool GROUP, int GELU>
+template <typename T, int VPT, bool GROUP, int GELU, bool SEG = false>
 __global__ void __launch_bounds__(128, 4)
-quant_rows_warp_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int8_t* __restrict__ q,
-                       float* __restrict__ s) {
+quant_rows_warp_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, float* __restrict__ s) {
   constexpr bool kRaw = !GROUP && GELU == kGeluNone && sizeof(T) == 2;
   constexpr int kRawVecs = kRaw ? VPT : 1;
   constexpr int kFloatVecs = kRaw ? 1 : VPT;
@@ -244,7 +274,6 @@ quant_rows_warp_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, i
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
        row += warps) {
-    const T* xr = x + row * ldx;
     uint4 raw[kRawVecs];
     float v[kFloatVecs][8];
     float am[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};   // independent max chains
@@ -253,11 +282,12 @@ quant_rows_warp_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, i
     for (int i = 0; i < VPT; ++i) {
       const int vi = lane + 32 * i;
       if (kRaw) {
-        raw[kRaw ? i : 0] = vi < nvec ? *reinterpret_cast<const uint4*>(xr + vi * 8) : make_uint4(0, 0, 0, 0);
+        raw[kRaw ? i : 0] = vi < nvec ? *reinterpret_cast<const uint4*>(src_ptr<T, SEG>(src, row, vi * 8))
+                                      : make_uint4(0, 0, 0, 0);
       } else {
         const int fi = kRaw ? 0 : i;
         if (vi < nvec) {
-          Vec8<T>::load(xr + vi * 8, v[fi]);
+          Vec8<T>::load(src_ptr<T, SEG>(src, row, vi * 8), v[fi]);
         } else {
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[fi][j] = 0.0f;
@@ -320,22 +350,20 @@ constexpr int kQuantThreads = 128;
 
 // Vector path: K % 8 == 0, ldx % 8 == 0 (elements), x 16-byte aligned. One CTA per row
 // (grid-stride). Each thread holds up to VPT vectors of 8 elements. `group` is 0 or 256.
-template <typename T, int VPT, bool GROUP, int GELU>
+template <typename T, int VPT, bool GROUP, int GELU, bool SEG = false>
 __global__ void __launch_bounds__(kQuantThreads)
-quant_rows_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int8_t* __restrict__ q,
-                  float* __restrict__ s) {
+quant_rows_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, float* __restrict__ s) {
   __shared__ float red[kQuantThreads / 32];
   const int tid = threadIdx.x;
   const int nvec = K >> 3;
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
-    const T* xr = x + row * ldx;
     float v[VPT][8];
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = tid + i * kQuantThreads;
       if (vi < nvec) {
-        Vec8<T>::load(xr + vi * 8, v[i]);
+        Vec8<T>::load(src_ptr<T, SEG>(src, row, vi * 8), v[i]);
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;

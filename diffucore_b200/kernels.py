@@ -118,6 +118,88 @@ def rescale(acc: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor, bias: torch.T
     return out
 
 
+def gemm_w8a8_into(q: torch.Tensor, w: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor,
+                   bias: torch.Tensor | None, out: torch.Tensor, *, ldo: int | None = None,
+                   gelu: int = _lib.GELU_NONE, gate: torch.Tensor | None = None,
+                   residual: torch.Tensor | None = None, col_block: int = 0, block_stride: int = 0) -> None:
+    """``gemm_w8a8`` into caller memory, with the DiT epilogue options of ``dc_gemm_w8a8_ex``.
+
+    ``out`` supplies the base address and dtype; rows are ``ldo`` elements apart (default
+    ``out.stride(0)``). ``gate``/``residual`` (residual a row-strided [M, N] view, possibly ``out``
+    itself) give ``out = dtype(residual + dtype(gate * y))``. ``col_block > 0`` writes the
+    [N / col_block, M, col_block] block layout with blocks ``block_stride`` elements apart.
+    Operands are used as given (no copies): q [M, K] and w [N, K] int8 with 16-byte aligned rows,
+    sx [M], sw [N] fp32, bias and gate [N] in ``out``'s dtype, all contiguous."""
+    _require_cuda(q, w, out)
+    M, K = q.shape
+    N = w.shape[0]
+    if ldo is None:
+        ldo = out.stride(0)
+    ldr = residual.stride(0) if residual is not None else 0
+    lib = _lib.load()
+    _lib.check(lib.dc_gemm_w8a8_ex(_ptr(q), q.stride(0), _ptr(w), w.stride(0), _ptr(sx), _ptr(sw), _ptr(bias),
+                                   int(gelu), _ptr(gate), _ptr(residual), ldr, _ptr(out), int(ldo), int(col_block),
+                                   int(block_stride), _DTYPE[out.dtype], M, N, K, _stream(q)))
+
+
+def ln_mod_quant(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, group: int,
+                 q: torch.Tensor | None = None, s: torch.Tensor | None = None):
+    """Codes of ``dtype(dtype(dtype(1 + scale) * LN(x)) + shift)`` per row of ``x`` [M, K]
+    (LayerNorm without affine, eps 1e-6), as ``dc_quant_rows`` would give for that activation.
+    ``shift``/``scale`` are [K] vectors in x's dtype. Returns ``(q int8 [M, K], s fp32 [M])``."""
+    _require_cuda(x)
+    M, K = x.shape
+    if q is None:
+        q = torch.empty(M, K, device=x.device, dtype=torch.int8)
+    if s is None:
+        s = torch.empty(M, device=x.device, dtype=torch.float32)
+    lib = _lib.load()
+    _lib.check(lib.dc_ln_mod_quant(_ptr(x), _DTYPE[x.dtype], M, K, x.stride(0), _ptr(shift), _ptr(scale), max(M, 1),
+                                   0, int(group), _ptr(q), _ptr(s), _stream(x)))
+    return q, s
+
+
+def quant_rows_into(x: torch.Tensor, group: int, q: torch.Tensor, s: torch.Tensor) -> None:
+    """``quant_rows`` of a row-strided [M, K] view into caller buffers (q [M, K] contiguous)."""
+    _require_cuda(x)
+    M, K = x.shape
+    lib = _lib.load()
+    _lib.check(lib.dc_quant_rows(_ptr(x), _DTYPE[x.dtype], M, K, x.stride(0), int(group), _lib.GELU_NONE,
+                                 _ptr(q), _ptr(s), _stream(x)))
+
+
+def quant_rows_seg(recv: torch.Tensor, x2: torch.Tensor | None, group: int, q: torch.Tensor,
+                   s: torch.Tensor) -> None:
+    """Codes of the rows ``cat([recv[0], ..., recv[P-1], x2], dim=1)`` for an all-to-all receive
+    buffer ``recv`` [P, M, W] (contiguous) and an optional row-strided ``x2`` [M, K2], without
+    forming the concatenation."""
+    _require_cuda(recv)
+    P, M, W = recv.shape
+    K = P * W + (x2.shape[1] if x2 is not None else 0)
+    lib = _lib.load()
+    _lib.check(lib.dc_quant_rows_seg(_ptr(recv), _DTYPE[recv.dtype], M, K, W, W, M * W, P * W, _ptr(x2),
+                                     x2.stride(0) if x2 is not None else 0, int(group), _ptr(q), _ptr(s),
+                                     _stream(recv)))
+
+
+def qk_norm_rope(qkv: torch.Tensor, q_scale0: torch.Tensor, k_scale0: torch.Tensor, pe: torch.Tensor,
+                 q_scale1: torch.Tensor | None = None, k_scale1: torch.Tensor | None = None,
+                 split_row: int | None = None) -> None:
+    """In place on ``qkv`` [L, 3, H, 128] (row-strided): RMSNorm of q and k per head with their
+    scales, then RoPE with ``pe`` [L, 64, 2, 2] fp32. Rows below ``split_row`` use the ``*0``
+    scales, the rest the ``*1`` scales."""
+    _require_cuda(qkv, pe)
+    L, three, H, D = qkv.shape
+    if three != 3 or qkv.stride(3) != 1 or qkv.stride(2) != D or qkv.stride(1) != H * D:
+        raise ValueError("qk_norm_rope expects rows laid out as [3, H, D]")
+    if split_row is None:
+        split_row = L
+    lib = _lib.load()
+    _lib.check(lib.dc_qk_norm_rope(_ptr(qkv), _DTYPE[qkv.dtype], L, H, D, qkv.stride(0), 0, H * D, _ptr(q_scale0),
+                                   _ptr(k_scale0), _ptr(q_scale1), _ptr(k_scale1), int(split_row), _ptr(pe), 0,
+                                   _stream(qkv)))
+
+
 def attn_workspace_layout(B: int, H: int, Lq: int, Lk: int, D: int, mode: int) -> dict:
     lay = (ctypes.c_int64 * 8)()
     _lib.check(_lib.load().dc_attn_workspace_layout(B, H, Lq, Lk, D, mode, lay))

@@ -71,6 +71,55 @@ int dc_gemm_w8a8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, con
                  const void* bias, void* out, int64_t ldo, int out_dtype, int64_t M, int64_t N, int64_t K,
                  int gelu, void* stream);
 
+/* dc_gemm_w8a8 with the epilogue options a DiT block needs (bf16 / fp16 output):
+ *  - gate [N] and residual [M, N] (row stride ldr), both or neither: after rescale and bias,
+ *      out = dtype(residual + dtype(gate[n] * y))
+ *    the gated residual branch `x + mod.gate * linear(h)` of FLUX blocks
+ *    (src/diffucore/models/flux_dit.py:302-305, :339); residual may be out itself (in place).
+ *    No GELU with a residual.
+ *  - col_block > 0 (a multiple of 128; block_stride a multiple of 8): column n of row m goes to
+ *      out + (n / col_block) * block_stride + m * ldo + n % col_block
+ *    i.e. the output is laid out as [N / col_block, M, col_block] blocks, the send layout of an
+ *    all-to-all that gives each destination its contiguous block. col_block = 0: plain [M, N]
+ *    with row stride ldo (then block_stride must be 0). */
+int dc_gemm_w8a8_ex(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
+                    const void* bias, int gelu, const void* gate, const void* residual, int64_t ldr, void* out,
+                    int64_t ldo, int64_t col_block, int64_t block_stride, int out_dtype, int64_t M, int64_t N,
+                    int64_t K, void* stream);
+
+/* dc_quant_rows over rows gathered from segments (fp16 / bf16, no GELU): element c < k1 of row m
+ * is at x + (c / seg_len) * seg_stride + m * ldx + c % seg_len, element c >= k1 at
+ * x2 + m * ldx2 + (c - k1). seg_len, strides and offsets are multiples of 8 elements, seg_len
+ * divides k1, k1 <= K <= 16384. With an all-to-all's receive buffer [P, M, seg_len] as x (and,
+ * for a FLUX single-stream block, the MLP half as x2) this quantizes the concatenated row that
+ * `linear2(cat(attn, mlp))` / `proj(attn)` consume (src/diffucore/models/flux_dit.py:335, :302)
+ * without materialising it. Codes and scales equal dc_quant_rows on the gathered rows. */
+int dc_quant_rows_seg(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int64_t seg_len,
+                      int64_t seg_stride, int64_t k1, const void* x2, int64_t ldx2, int group, int8_t* q, float* s,
+                      void* stream);
+
+/* LayerNorm (no affine, eps 1e-6) + AdaLN modulation + int8 codes in one pass, for the
+ * modulated inputs of FLUX blocks (src/diffucore/models/flux_dit.py:282, :287, :328):
+ *   n = dtype(LN(x)); y = dtype(dtype(dtype(1 + scale[k]) * n) + shift[k])
+ * then exactly dc_quant_rows(y, group). Rows m of batch element b = m / rows_per_mod use
+ * shift/scale + b * mod_ld (fp16 / bf16 like x). K % 8 == 0, K <= 4096; x, shift, scale 16-byte
+ * aligned. The modulated activation is never written. */
+int dc_ln_mod_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const void* shift,
+                    const void* scale, int64_t rows_per_mod, int64_t mod_ld, int group, int8_t* q, float* s,
+                    void* stream);
+
+/* In-place per-head RMSNorm + axial RoPE of q and k inside packed qkv rows (FLUX `QKNorm` and
+ * `apply_rope`, src/diffucore/models/flux_dit.py:129-151, :179-184). Row r, head h (D = 128):
+ * q at qkv + r * ld_row + q_off + h * D, k at + k_off + h * D.
+ *   y = dtype(dtype(x * rsqrt(mean(x^2) + 1e-6)) * scale[d])
+ *   (y0, y1) of rotary pair i -> dtype(f[i][0][0] y0 + f[i][0][1] y1), dtype(f[i][1][0] y0 + f[i][1][1] y1)
+ * with pe fp32 [rows, D/2, 2, 2] (row r uses pe row pe_row0 + r). Rows r < split_row use
+ * (q_scale0, k_scale0), the others (q_scale1, k_scale1): the text and image streams of a joint
+ * double-stream attention. */
+int dc_qk_norm_rope(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64_t ld_row, int64_t q_off,
+                    int64_t k_off, const void* q_scale0, const void* k_scale0, const void* q_scale1,
+                    const void* k_scale1, int64_t split_row, const float* pe, int64_t pe_row0, void* stream);
+
 /* out[M, N] = dtype(float(acc) * (sx[m] * sw[n])) (+ bias in dtype), acc int32 [M, N] with row
  * stride lda: the epilogue of dc_gemm_w8a8 as a separate pass, for an int32 result already in
  * hand. Replaces `rescale` (src/diffucore/models/_int8.py:313-323) and its Triton

@@ -1,0 +1,99 @@
+"""Ulysses (sequence-split, head-exchanging) FLUX runner over NCCL on 2 GPUs against the
+single-GPU runner. Needs two sm_100 GPUs; skipped otherwise.
+
+Every rank owns half of the joint text + image rows; q/k/v leave the qkv GEMM in the per-rank
+send layout, cross NVLink in one all-to-all, are normed, rotated and attended per head over the
+whole sequence, and come back in a second all-to-all read in place by the projection's quantizer.
+The per-token kernels are row-independent and the attention per head, so the only source of
+difference from one GPU is cuBLAS picking other reduction orders for the bf16 input embeddings at
+a different row count; the check is the north-star tolerance.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from diffucore_b200 import flux
+
+pytestmark = pytest.mark.gpu
+
+CASES = {
+    "tiny": (dict(in_channels=64, context_in_dim=64, vec_in_dim=32, hidden_size=256, mlp_ratio=4.0, num_heads=2,
+                  depth=2, depth_single_blocks=2), 40, (16, 24)),
+    "full_width": (dict(depth=1, depth_single_blocks=1), 512, (64, 64)),
+}
+
+
+def _two_gpus() -> bool:
+    return torch.cuda.is_available() and torch.cuda.device_count() >= 2
+
+
+def _setup(case: str, dev, pg=None):
+    cfg_kw, n_txt, (gh, gw) = CASES[case]
+    cfg = flux.FluxConfig(**cfg_kw)
+    model = flux.build_flux(cfg, seed=3, device=dev, group=256, init_device="cpu" if case == "tiny" else dev)
+    for b in list(model.double_blocks) + list(model.single_blocks):
+        b.attn_backend = "int8_turing"
+    n_img = gh * gw
+    runner = flux.FluxRunner(model, n_txt, n_img, process_group=pg, device=dev)
+    runner.set_positions(flux.img_ids(2 * gh, 2 * gw, 2), flux.txt_ids(n_txt))
+    g = torch.Generator().manual_seed(5)
+    img = torch.randn(n_img, cfg.in_channels, generator=g).to(torch.bfloat16)
+    txt = torch.randn(n_txt, cfg.context_in_dim, generator=g).to(torch.bfloat16)
+    y = torch.randn(1, cfg.vec_in_dim, generator=g).to(torch.bfloat16)
+    return runner, img, txt, y
+
+
+def _forward(runner, img, txt, y, dev):
+    i0, i1 = runner.img_rows
+    r0 = runner.rows[0]
+    t = torch.full((1,), 0.6, dtype=torch.bfloat16, device=dev)
+    v = runner.forward(img[i0:i1].to(dev), txt[r0: r0 + runner.t_loc].to(dev), t, y.to(dev))
+    return v.cpu(), (i0, i1)
+
+
+def _worker(rank: int, port: int, case: str, path: str) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        runner, img, txt, y = _setup(case, dev, dist.group.WORLD)
+        v, rows = _forward(runner, img, txt, y, dev)
+        torch.cuda.synchronize()
+        torch.save({"v": v, "rows": rows}, f"{path}.{rank}")
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
+@pytest.mark.parametrize("case", ["tiny", "full_width"])
+def test_ulysses_two_gpus_match_one(tmp_path, case):
+    dev = torch.device("cuda", 0)
+    runner, img, txt, y = _setup(case, dev)
+    single, _ = _forward(runner, img, txt, y, dev)
+    del runner
+    torch.cuda.empty_cache()
+    path = str(tmp_path / "v")
+    mp.start_processes(_worker, args=(_free_port(), case, path), nprocs=2, join=True, start_method="spawn")
+    parts = [torch.load(f"{path}.{r}") for r in range(2)]
+    joined = torch.cat([p["v"] for p in parts], dim=0).float()
+    want = single.float()
+    assert joined.shape == want.shape and torch.isfinite(joined).all()
+    cos = torch.nn.functional.cosine_similarity(joined.flatten().double(), want.flatten().double(), dim=0).item()
+    assert (joined - want).abs().max().item() <= 2e-2 and cos >= 0.999
