@@ -398,16 +398,28 @@ def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048)) -> dict:
         r0 = runner.rows[0]
         x, txt = x_all[i0:i1].contiguous(), txt_all[r0: r0 + runner.t_loc].contiguous()
         sigmas = flux.flow_schedule(FLUX_STEPS, 1.0)
-        xo = flux.euler_sample(runner, x, txt, y, sigmas)          # warm-up: one whole sampling run
-        torch.cuda.synchronize()
-        _barrier(world)
-        s, e = _events(2)
-        s.record()
-        xo = flux.euler_sample(runner, x, txt, y, sigmas)
-        e.record()
-        torch.cuda.synchronize()
-        finite = bool(torch.isfinite(xo).all())
-        s_step = _max_over_ranks(s.elapsed_time(e) * 1e-3 / FLUX_STEPS, world)
+        res = {}
+        for mode in ("eager", "graph"):
+            step_fn = runner
+            if mode == "graph":
+                try:
+                    step_fn = flux.FluxGraph(runner, x, txt, y)
+                except Exception as exc:                    # report, keep the eager number
+                    res["graph_error"] = f"{type(exc).__name__}: {exc}"[:300]
+                    break
+            xo = flux.euler_sample(step_fn, x, txt, y, sigmas)       # warm-up: one whole sampling run
+            torch.cuda.synchronize()
+            _barrier(world)
+            s, e = _events(2)
+            s.record()
+            xo = flux.euler_sample(step_fn, x, txt, y, sigmas)
+            e.record()
+            torch.cuda.synchronize()
+            res[mode] = _max_over_ranks(s.elapsed_time(e) * 1e-3 / FLUX_STEPS, world)
+            res["finite"] = bool(torch.isfinite(xo).all())
+            del step_fn
+        finite = res.pop("finite")
+        s_step = min(v for k, v in res.items() if k in ("eager", "graph"))
         w = flux_work(L)
         compute_s = (w["linear_int8_ops"] + w["attn_int8_ops"]) / int8_peak + w["attn_bf16_ops"] / bf16_peak
         roof = compute_s / world
@@ -418,6 +430,8 @@ def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048)) -> dict:
             a2a = 57 * per_block / 770e9                                          # measured peer copy GB/s
             roof = max(roof, a2a)
         out[f"{side}px"] = {"tokens": L, "s_per_step": s_step, "n_gpus": world,
+                            "s_per_step_eager": res.get("eager"), "s_per_step_graph": res.get("graph"),
+                            **({"graph_error": res["graph_error"]} if "graph_error" in res else {}),
                             "roofline_s_per_step": roof, "frac_of_roofline": roof / s_step,
                             "a2a_s_per_step_at_770GBps": a2a, "finite": finite,
                             "work_per_step": {k: v / 1e12 for k, v in w.items()}, "work_unit": "T ops"}

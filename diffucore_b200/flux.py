@@ -561,14 +561,52 @@ class FluxRunner:
         return fl.linear(h)
 
 
-def euler_sample(runner: FluxRunner, x: torch.Tensor, txt: torch.Tensor, y: torch.Tensor | None,
+class FluxGraph:
+    """One captured CUDA graph of ``runner.forward``: the ~1000 launches of a FLUX forward (and,
+    with Ulysses, its NCCL all-to-alls) replay as one graph launch, so the host no longer paces
+    the GPU. Inputs are copied into static buffers before each replay; the returned velocity is a
+    static buffer overwritten by the next replay. The runner's buffers are already persistent; the
+    torch ops of the forward allocate from the graph's private pool."""
+
+    def __init__(self, runner: FluxRunner, img: torch.Tensor, txt: torch.Tensor, y: torch.Tensor | None,
+                 guidance: torch.Tensor | None = None):
+        self.runner = runner
+        self.img, self.txt = img.clone(), txt.clone()
+        self.y = y.clone() if y is not None else None
+        self.t = torch.zeros(1, device=img.device, dtype=img.dtype)
+        self.guidance = guidance.clone() if guidance is not None else None
+        side = torch.cuda.Stream(device=img.device)
+        side.wait_stream(torch.cuda.current_stream(img.device))
+        with torch.cuda.stream(side):
+            for _ in range(2):                       # warm-up outside capture (torch requirement)
+                runner.forward(self.img, self.txt, self.t, self.y, self.guidance)
+        torch.cuda.current_stream(img.device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = runner.forward(self.img, self.txt, self.t, self.y, self.guidance)
+
+    def __call__(self, img: torch.Tensor, t: torch.Tensor, txt: torch.Tensor | None = None) -> torch.Tensor:
+        if img.data_ptr() != self.img.data_ptr():
+            self.img.copy_(img)
+        if txt is not None and txt.data_ptr() != self.txt.data_ptr():
+            self.txt.copy_(txt)
+        self.t.copy_(t)
+        self.graph.replay()
+        return self.out
+
+
+def euler_sample(runner, x: torch.Tensor, txt: torch.Tensor, y: torch.Tensor | None,
                  sigmas: torch.Tensor, guidance: torch.Tensor | None = None) -> torch.Tensor:
     """Euler flow-matching integration of this rank's image tokens ``x`` [n_img_local, C_in]:
-    x += (sigma_next - sigma) v(x, sigma) per step (src/diffucore/pipelines/_flux.py:226-236)."""
+    x += (sigma_next - sigma) v(x, sigma) per step (src/diffucore/pipelines/_flux.py:226-236).
+    ``runner`` is a :class:`FluxRunner` or a :class:`FluxGraph` captured on it."""
     dt = x.dtype
     for i in range(len(sigmas) - 1):
         sigma, sigma_next = sigmas[i], sigmas[i + 1]
         t = torch.full((1,), float(sigma), device=x.device, dtype=dt)
-        v = runner.forward(x, txt, t, y, guidance)
+        if isinstance(runner, FluxGraph):
+            v = runner(x, t, txt)
+        else:
+            v = runner.forward(x, txt, t, y, guidance)
         x = x + (sigma_next - sigma).to(dt) * v
     return x
