@@ -385,7 +385,7 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
         uint64_t ad = smem_desc_sw(sq_addr + i * SM::kQTile, 16, SM::kQKAtom, SM::kQKSwizzle);
         uint64_t bd = smem_desc_sw(sk_addr, 16, SM::kQKAtom, SM::kQKSwizzle);
         const uint32_t d = tmem + i * 128;
-#pragma unroll 1
+#pragma unroll
         for (int kk = 0; kk < D / 32; ++kk) {
           mma_i8_ss(d, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
           ad += 32 >> 4;
@@ -399,7 +399,7 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
                                    1024, 2);
         const uint32_t d = tmem + kOCol + i * D;
         uint32_t a = tmem + i * 128 + hh * 64;
-#pragma unroll 1
+#pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           mma_f16_ts(d, a, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
           bd += 2048 >> 4;
@@ -559,6 +559,288 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
             w.z = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e + 4]), inv), __fmul_rn(__uint_as_float(o[e + 5]), inv));
             w.w = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e + 6]), inv), __fmul_rn(__uint_as_float(o[e + 7]), inv));
             *reinterpret_cast<uint4*>(dst + c + e) = w;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ----------------------------------------------------------------------------- main kernel, S double-buffered
+//
+// One CTA per 128-row Q tile. TMEM holds two S buffers and O: S(j) lands in buffer j & 1 while
+// the softmax works on S(j - 1) from the other, so Q.K^T of the next tile runs on the tensor core
+// during the exponentials of this one. P(j) is written over the S(j) columns its warp has already
+// read, so the buffer is free again once P.V(j) has run (the MMA that overwrites it with S(j + 2)
+// is issued after P.V(j), and tcgen05 MMAs of one CTA execute in issue order).
+//   warps 0-7   softmax: warp w owns TMEM lane quarter w & 3 (32 query rows) and key half w >> 2
+//               (64 of the tile's 128 keys): two warps per row, two per SM sub-partition
+//   warp 8      TMA producer (Q once; K and V per stage)
+//   warp 9      TMEM allocator + MMA issuer
+// The two warps of a row exchange their half-row maxima once per tile through shared memory
+// (a bounded mbarrier round), so both apply the same running max; their partial row sums are
+// added at the end. O is rescaled lazily (only when the row max grows by more than 2^8), each warp
+// its half of the columns.
+constexpr int kDbRows = 128;
+constexpr int kDbStages = 3;
+
+template <int D>
+struct AttnDbSmem {
+  static constexpr int kQTile = kDbRows * D;
+  static constexpr int kKTile = kAttnBN * D;
+  static constexpr int kVTile = kAttnBN * D * 2;
+  static constexpr int kVHalf = kAttnBN * 64 * 2;
+  static constexpr int kStage = kKTile + kVTile;
+  static constexpr int kBytes = kQTile + kDbStages * kStage;
+  static constexpr int kDynamic = kBytes + 1024;
+  static constexpr uint32_t kQKSwizzle = D == 128 ? 2u : 4u;
+  static constexpr uint32_t kQKAtom = D == 128 ? 1024u : 512u;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+attn_db_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
+               const __grid_constant__ CUtensorMap tma_v, const AttnParams p) {
+  using SM = AttnDbSmem<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = smem;
+  uint8_t* sstage = smem + SM::kQTile;
+
+  __shared__ __align__(8) uint64_t q_full;
+  __shared__ __align__(8) uint64_t k_full[kDbStages];
+  __shared__ __align__(8) uint64_t v_full[kDbStages];
+  __shared__ __align__(8) uint64_t kv_empty[kDbStages];
+  __shared__ __align__(8) uint64_t s_full[2];
+  __shared__ __align__(8) uint64_t p_full[2];
+  __shared__ __align__(8) uint64_t pv_done;
+  __shared__ __align__(8) uint64_t pair_bar[4];      // per lane quarter: the two warps of those rows
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ float s_xchg[2][2][kDbRows];             // [tile parity][key half][row]
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = warp_id(), lane = lane_id();
+  const int qtile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int bh = b * p.H + h;
+  const int n = p.n_ktiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < kDbStages; ++s) { mbar_init(&k_full[s], 1); mbar_init(&v_full[s], 1); mbar_init(&kv_empty[s], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&p_full[i], 8); }
+    mbar_init(&pv_done, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 64);
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8 && lane == 0) { tma_prefetch_desc(&tma_q); tma_prefetch_desc(&tma_k); tma_prefetch_desc(&tma_v); }
+  if (warp == 9) { tmem_alloc(&tmem_slot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+  constexpr uint32_t kOCol = 256;   // S buffers at [0, 128) and [128, 256), O at [256, 256 + D)
+
+  if (warp == 8) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      mbar_arrive_expect_tx(&q_full, SM::kQTile);
+      tma_load_2d(sq, &tma_q, &q_full, 0, bh * p.Lq_pad + qtile * kDbRows);
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j % kDbStages;
+        const uint32_t ph = (j / kDbStages) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort)) { ok = false; break; }
+        uint8_t* sk = sstage + st * SM::kStage;
+        uint8_t* sv = sk + SM::kKTile;
+        mbar_arrive_expect_tx(&k_full[st], SM::kKTile);
+        tma_load_2d(sk, &tma_k, &k_full[st], 0, bh * p.Lk_pad + j * kAttnBN);
+        mbar_arrive_expect_tx(&v_full[st], SM::kVTile);
+#pragma unroll
+        for (int dh = 0; dh < D / 64; ++dh)
+          tma_load_4d(sv + dh * SM::kVHalf, &tma_v, &v_full[st], dh * 64, j * kAttnBN, h, b);
+      }
+      if (!ok) for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMA issuer (lane 0)
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_i8(kDbRows, kAttnBN);
+      constexpr uint32_t idesc_o = idesc_f16(kDbRows, D, BF16, true);
+      const uint32_t sq_addr = smem_u32(sq);
+      auto issue_s = [&](int buf, int st) {
+        uint64_t ad = smem_desc_sw(sq_addr, 16, SM::kQKAtom, SM::kQKSwizzle);
+        uint64_t bd = smem_desc_sw(smem_u32(sstage + st * SM::kStage), 16, SM::kQKAtom, SM::kQKSwizzle);
+        const uint32_t d = tmem + buf * 128;
+#pragma unroll
+        for (int kk = 0; kk < D / 32; ++kk) {
+          mma_i8_ss(d, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          ad += 32 >> 4;
+          bd += 32 >> 4;
+        }
+      };
+      // O += P(buf) . V(stage): 16 keys per MMA; P of keys [64 hf, 64 hf + 64) sits at columns
+      // [64 hf, 64 hf + 32) of the buffer (two keys per column).
+      auto issue_pv = [&](int buf, int st, bool acc) {
+        const uint64_t bd0 = smem_desc_sw(smem_u32(sstage + st * SM::kStage + SM::kKTile), SM::kVHalf, 1024, 2);
+        const uint32_t d = tmem + kOCol;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t a = tmem + buf * 128 + (kk >> 2) * 64 + (kk & 3) * 8;
+          mma_f16_ts(d, a, bd0 + static_cast<uint64_t>((kk * 2048) >> 4), idesc_o, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(&q_full, 0, abort) && mbar_wait(&k_full[0], 0, abort);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        mma_commit(&s_full[0]);
+      }
+      if (ok && n > 1) {
+        ok = mbar_wait(&k_full[1 % kDbStages], (1 / kDbStages) & 1, abort);
+        if (ok) {
+          tc_fence_after();
+          issue_s(1, 1 % kDbStages);
+          mma_commit(&s_full[1]);
+        }
+      }
+      for (int j = 0; j < n && ok; ++j) {
+        const int buf = j & 1;
+        const int st = j % kDbStages;
+        if (!mbar_wait(&p_full[buf], (j >> 1) & 1, abort)) { ok = false; break; }
+        if (!mbar_wait(&v_full[st], (j / kDbStages) & 1, abort)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(buf, st, j > 0);
+        mma_commit(&pv_done);
+        mma_commit(&kv_empty[st]);
+        if (j + 2 < n) {
+          const int st2 = (j + 2) % kDbStages;
+          if (!mbar_wait(&k_full[st2], ((j + 2) / kDbStages) & 1, abort)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(buf, st2);
+          mma_commit(&s_full[buf]);
+        }
+      }
+      mma_commit(&drain_bar);
+      mbar_wait(&drain_bar, 0, nullptr, 1000000);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax warps
+    const int quarter = warp & 3;
+    const int hf = warp >> 2;                 // key half of every tile this warp owns
+    const int r_local = quarter * 32 + lane;
+    const int qrow = qtile * kDbRows + r_local;
+    const float cq = __fmul_rn(p.q_scale[static_cast<int64_t>(bh) * p.Lq_pad + qrow], p.scale_log2);
+    const float* ksc = p.k_scale + static_cast<int64_t>(bh) * (p.Lk_pad / kAttnKBlk);
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    constexpr int kOHalf = D / 2;             // O columns this warp rescales and stores
+    const uint32_t o_addr = tmem + lane_off + kOCol + hf * kOHalf;
+    const int tail_valid = p.Lk - (n - 1) * kAttnBN;
+    float m = -INFINITY;
+    float2 l2 = make_float2(0.f, 0.f);
+    float ks_cur = ksc[hf];
+    bool ok = true;
+    uint32_t r[64];
+    // both warps of these rows meet here; returns false if the round did not complete
+    auto pair_round = [&](int round) -> bool {
+      mbar_arrive(&pair_bar[quarter]);
+      return mbar_wait(&pair_bar[quarter], round & 1, abort);
+    };
+    for (int j = 0; j < n && ok; ++j) {
+      const int buf = j & 1;
+      const float ks_next = j + 1 < n ? ksc[2 * (j + 1) + hf] : 0.f;
+      ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t s_addr = tmem + lane_off + buf * 128 + hf * 64;
+      tmem_ld32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_wait_ld();
+      const int valid = (j == n - 1) ? tail_valid - 64 * hf : 64;
+      if (valid < 64) mask_tail64(r, valid);
+      const float c = __fmul_rn(cq, ks_cur);
+      const float mt = scaled_max(row_max64(r), c);
+      s_xchg[j & 1][hf][r_local] = mt;
+      ok = pair_round(j);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      const float row_mt = fmaxf(mt, s_xchg[j & 1][hf ^ 1][r_local]);
+      if (j == 0) {
+        m = row_mt;
+      } else if (row_mt > m + kLazyRescale) {
+        // Rare: move the running max up and rescale this warp's half of O once P.V(j - 1) landed.
+        const float alpha = ex2_approx(m - row_mt);
+        l2 = __fmul2_rn(l2, make_float2(alpha, alpha));
+        m = row_mt;
+        ok = mbar_wait(&pv_done, (j - 1) & 1, abort);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int cc = 0; cc < kOHalf; cc += 32) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + cc, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float2 v = __fmul2_rn(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])),
+                                        make_float2(alpha, alpha));
+            o[e] = __float_as_uint(v.x);
+            o[e + 1] = __float_as_uint(v.y);
+          }
+          tmem_st32(o_addr + cc, o);
+        }
+      }
+      float2 lt = make_float2(0.f, 0.f);
+      uint32_t pk[32];
+      if (valid < 64) p_half<BF16, true>(r, c, -__fmaf_rn(kMagicF, c, m), valid, lt, pk);
+      else p_half<BF16, false>(r, c, -__fmaf_rn(kMagicF, c, m), valid, lt, pk);
+      l2 = __fadd2_rn(l2, lt);
+      tmem_st32(tmem + lane_off + buf * 128 + hf * 64, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[buf]);
+      ks_cur = ks_next;
+    }
+    if (ok) {
+      ok = mbar_wait(&pv_done, (n - 1) & 1, abort);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      s_xchg[n & 1][hf][r_local] = __fadd_rn(l2.x, l2.y);
+      ok = pair_round(n);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      const float l_row = __fadd_rn(s_xchg[n & 1][0][r_local], s_xchg[n & 1][1][r_local]);
+      const float inv = __fdiv_rn(1.0f, l_row);
+      const bool row_ok = qrow < p.Lq;
+      uint16_t* dst = reinterpret_cast<uint16_t*>(p.o) + b * p.o_sb + static_cast<int64_t>(qrow) * p.o_sl + h * p.o_sh +
+                      hf * kOHalf;
+#pragma unroll 1
+      for (int cc = 0; cc < kOHalf; cc += 32) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + cc, o);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 w;
+            w.x = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e]), inv), __fmul_rn(__uint_as_float(o[e + 1]), inv));
+            w.y = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e + 2]), inv), __fmul_rn(__uint_as_float(o[e + 3]), inv));
+            w.z = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e + 4]), inv), __fmul_rn(__uint_as_float(o[e + 5]), inv));
+            w.w = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e + 6]), inv), __fmul_rn(__uint_as_float(o[e + 7]), inv));
+            *reinterpret_cast<uint4*>(dst + cc + e) = w;
           }
         }
       }

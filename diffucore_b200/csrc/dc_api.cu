@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -394,6 +395,22 @@ int attn_prep(const void* q, const void* k, int64_t B, int64_t H, int64_t Lq, in
   return DC_OK;
 }
 
+// Which main kernel: both run one CTA per SM (each holds all 512 TMEM columns). The two-tile
+// kernel (256 query rows per CTA) does more work per CTA-time; the single-tile kernel (128 rows,
+// S double-buffered) takes 0.61 of its time per CTA (measured on B200 at B=1, H=24, L=4608:
+// 49 vs 81 us per wave) and so wins when the two-tile grid ends in a poorly filled wave (few
+// heads per GPU, as with a sequence-parallel split). Environment DC_ATTN_KERNEL = "two_tile" or
+// "single_tile" pins one (tests use it to cover both).
+bool use_single_tile_kernel(int64_t ctas_two_tile, int64_t ctas_single_tile) {
+  const char* env = getenv("DC_ATTN_KERNEL");
+  if (env != nullptr && strcmp(env, "two_tile") == 0) return false;
+  if (env != nullptr && strcmp(env, "single_tile") == 0) return true;
+  const int64_t sms = sm_count();
+  const double waves_two = static_cast<double>((ctas_two_tile + sms - 1) / sms);
+  const double waves_single = static_cast<double>((ctas_single_tile + sms - 1) / sms);
+  return 0.61 * waves_single < waves_two;
+}
+
 template <typename T, int D>
 int attn_main(const void* v, int64_t B, int64_t H, int64_t Lq, int64_t Lk, const int64_t* vs, float sm_scale,
               void* o, const int64_t* os, uint8_t* ws, const AttnLayout& a, cudaStream_t st) {
@@ -433,11 +450,20 @@ int attn_main(const void* v, int64_t B, int64_t H, int64_t Lq, int64_t Lk, const
   p.q_scale = reinterpret_cast<const float*>(ws + a.q_scale);
   p.k_scale = reinterpret_cast<const float*>(ws + a.k_scale);
   p.o = o; p.o_sb = os[0]; p.o_sl = os[1]; p.o_sh = os[2];
-  auto kernel = dc::attn_int8_kernel<D, BF16>;
-  int r = set_smem(kernel, SM::kDynamic);
-  if (r) return r;
-  dim3 grid(static_cast<unsigned>(a.Lq_pad / dc::kAttnRows), static_cast<unsigned>(H), static_cast<unsigned>(B));
-  kernel<<<grid, dc::kAttnThreads, SM::kDynamic, st>>>(tq, tk, tv, p);
+  if (use_single_tile_kernel(B * H * (a.Lq_pad / dc::kAttnRows), B * H * (a.Lq_pad / dc::kDbRows))) {
+    using SD = dc::AttnDbSmem<D>;
+    auto kernel = dc::attn_db_kernel<D, BF16>;
+    int r = set_smem(kernel, SD::kDynamic);
+    if (r) return r;
+    dim3 grid(static_cast<unsigned>(a.Lq_pad / dc::kDbRows), static_cast<unsigned>(H), static_cast<unsigned>(B));
+    kernel<<<grid, dc::kAttnThreads, SD::kDynamic, st>>>(tq, tk, tv, p);
+  } else {
+    auto kernel = dc::attn_int8_kernel<D, BF16>;
+    int r = set_smem(kernel, SM::kDynamic);
+    if (r) return r;
+    dim3 grid(static_cast<unsigned>(a.Lq_pad / dc::kAttnRows), static_cast<unsigned>(H), static_cast<unsigned>(B));
+    kernel<<<grid, dc::kAttnThreads, SM::kDynamic, st>>>(tq, tk, tv, p);
+  }
   DC_CHECK_LAUNCH("attention launch");
   return DC_OK;
 }

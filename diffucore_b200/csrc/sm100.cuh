@@ -144,12 +144,17 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc], int8 x int8 -> int32.
+// The MMA issue wrappers carry no "memory" clobber: an MMA reads shared memory and TMEM through
+// the tensor core's own path, ordered by the mbarrier waits and tcgen05 fences around it (volatile
+// asm, which keeps its place among the other volatile asm). A clobber would make the compiler
+// reload every live value around each MMA, and the MMA queue is shallow: an issue that lags
+// the previous MMA's start leaves the tensor core idle.
 __device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                           uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
-      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc], f16/bf16 -> f32.
@@ -158,7 +163,7 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 // D[tmem] (+)= A[tmem] * B[smem desc], f16/bf16 -> f32 (A read from tensor memory).
@@ -167,7 +172,7 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
-      :: "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+      :: "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 // Arrive once on `bar` when every tcgen05.mma issued so far by this thread has completed.

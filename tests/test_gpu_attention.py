@@ -24,6 +24,13 @@ DEV = "cuda"
 MODES = {"ref": _lib.MODE_REF, "block64": _lib.MODE_BLOCK64}
 
 
+@pytest.fixture(params=["two_tile", "single_tile"])
+def kernel(request, monkeypatch):
+    """Pins the main kernel the library would otherwise pick by grid size (DC_ATTN_KERNEL)."""
+    monkeypatch.setenv("DC_ATTN_KERNEL", request.param)
+    return request.param
+
+
 def _inputs(B, Lq, Lk, H, D, dtype, seed=0, k_shift=0.5):
     g = torch.Generator().manual_seed(seed)
     q = torch.randn(B, Lq, H, D, generator=g).to(dtype)
@@ -66,7 +73,7 @@ def _check_against_oracle(q, k, v, out, dtype, mode, sm_scale):
 @pytest.mark.parametrize("mode", ["ref", "block64"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("B,Lq,Lk,H", [(1, 1024, 1024, 4), (2, 1000, 1000, 2), (1, 700, 77, 4), (1, 70, 3953, 2)])
-def test_attention_matches_oracle_and_sdpa(mode, dtype, B, Lq, Lk, H):
+def test_attention_matches_oracle_and_sdpa(mode, dtype, B, Lq, Lk, H, kernel):
     """The reference test's shapes (unaligned lengths exercise query/key tails), K shifted +0.5."""
     q, k, v = _inputs(B, Lq, Lk, H, 128, dtype)
     out = _attention.attention_blhd(q.to(DEV), k.to(DEV), v.to(DEV), "int8_turing", quant_mode=mode)
@@ -81,14 +88,14 @@ def test_attention_matches_oracle_and_sdpa(mode, dtype, B, Lq, Lk, H):
 
 @pytest.mark.parametrize("mode", ["ref", "block64"])
 @pytest.mark.parametrize("B,Lq,Lk,H", [(2, 4096, 4096, 2), (1, 1024, 77, 5), (1, 333, 1500, 3)])
-def test_attention_head_dim_64(mode, B, Lq, Lk, H):
+def test_attention_head_dim_64(mode, B, Lq, Lk, H, kernel):
     """D = 64 (SDXL self-attention); the reference falls back to SDPA there."""
     q, k, v = _inputs(B, Lq, Lk, H, 64, torch.float16, seed=1, k_shift=0.0)
     out = _attention.attention_blhd(q.to(DEV), k.to(DEV), v.to(DEV), "int8_turing", quant_mode=mode)
     _check_against_oracle(q, k, v, out, torch.float16, mode, 64 ** -0.5)
 
 
-def test_bhld_and_packed_strided_inputs():
+def test_bhld_and_packed_strided_inputs(kernel):
     """(B, H, L, D) transposed views and a packed qkv projection (stride(2) = 3 * 128)
     (reference tests/test_attention_dispatch.py:216-226)."""
     g = torch.Generator().manual_seed(0)
@@ -102,7 +109,7 @@ def test_bhld_and_packed_strided_inputs():
     _check_against_oracle(q.cpu(), k.cpu(), v.cpu(), out, torch.float16, "ref", 128 ** -0.5)
 
 
-def test_flat_scores_large_v_stay_finite():
+def test_flat_scores_large_v_stay_finite(kernel):
     """Flat scores with large same-sign V (reference tests/test_attention_dispatch.py:229-238):
     fp32 P.V accumulation keeps every output finite and close."""
     g = torch.Generator().manual_seed(0)
@@ -125,7 +132,7 @@ def test_ineligible_inputs_run_sdpa_exactly():
     assert torch.equal(_attention.attention_blhd(q, q, q, "int8_turing"), _attention.attention_blhd(q, q, q, "sdpa"))
 
 
-def test_null_keys_equal_padded():
+def test_null_keys_equal_padded(kernel):
     g = torch.Generator().manual_seed(0)
     q = torch.randn(1, 300, 4, 128, generator=g).half().to(DEV)
     k = torch.randn(1, 67, 4, 128, generator=g).half().to(DEV)
@@ -137,7 +144,7 @@ def test_null_keys_equal_padded():
 
 
 @pytest.mark.parametrize("mode", ["block64", "ref"])
-def test_config2_full_size_properties(mode):
+def test_config2_full_size_properties(mode, kernel):
     """BASELINE config 2 at full size (B=1, H=24, S=4608, D=128, bf16, N(0,1)): finite, close to
     fp32 attention on the GPU, deterministic run to run, and its codes equal the oracle's."""
     g = torch.Generator().manual_seed(0)
