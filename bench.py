@@ -442,6 +442,37 @@ def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048)) -> dict:
     return out
 
 
+def flux_op_breakdown(dev, side: int = 1024) -> dict:
+    """GPU time per op kind of one FLUX forward at ``side``^2 on one GPU (after two warm-ups)."""
+    import torch
+    from diffucore_b200 import _attention, _lib, flux
+    model = flux.build_flux(flux.FluxConfig(), seed=0, device=dev, group=256)
+    _attention.set_attention_backend(model, "int8_turing")
+    lat = side // 8
+    n_img = (lat // 2) ** 2
+    ops = flux.TimedOps()
+    runner = flux.FluxRunner(model, FLUX_TXT, n_img, device=dev, attn_mode=_lib.MODE_REF, ops=ops)
+    runner.set_positions(flux.img_ids(lat, lat, 2, device=dev), flux.txt_ids(FLUX_TXT, device=dev))
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = flux.patchify(torch.randn(1, 16, lat, lat, generator=g, device=dev)).to(torch.bfloat16)[0]
+    txt = torch.randn(FLUX_TXT, 4096, generator=g, device=dev).to(torch.bfloat16)
+    y = torch.randn(1, 768, generator=g, device=dev).to(torch.bfloat16)
+    t = torch.full((1,), 0.5, device=dev, dtype=torch.bfloat16)
+    for _ in range(2):
+        runner.forward(x, txt, t, y)
+    torch.cuda.synchronize()
+    ops.events.clear()
+    s, e = _events(2)
+    s.record()
+    runner.forward(x, txt, t, y)
+    e.record()
+    rows = ops.summary()
+    total = s.elapsed_time(e)
+    return {"workload": f"FLUX.1 forward, {side}^2 ({FLUX_TXT + n_img} tokens), 1 GPU, eager with events",
+            "forward_ms": round(total, 3), "ops_ms": round(sum(r["ms"] for r in rows), 3),
+            "other_ms_torch_ops": round(total - sum(r["ms"] for r in rows), 3), "ops": rows}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -452,6 +483,8 @@ def main() -> int:
     ap.add_argument("--only", default="all", choices=("all", "gemm", "flux"),
                     help="gemm / flux: time only the config-1 W8A8 linear / the FLUX DiT")
     ap.add_argument("--no-flux", action="store_true", help="skip the FLUX DiT timing")
+    ap.add_argument("--op-breakdown", action="store_true",
+                    help="with --only flux: GPU time per runner op of one 1024^2 forward (CUDA events)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -464,6 +497,11 @@ def main() -> int:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     peaks = _peaks()
+    if args.only == "flux" and args.op_breakdown:
+        res = flux_op_breakdown(dev)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return 0
     if args.only in ("gemm", "flux"):
         res = bench_gemm(args, dev, peaks) if args.only == "gemm" else bench_flux(args, world, rank, dev, peaks)
         if rank == 0:

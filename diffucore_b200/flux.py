@@ -333,6 +333,50 @@ class CudaOps:
             kernels.attn_int8(q, k, v, sm_scale, mode, workspace=workspace, out=out)
 
 
+class TimedOps:
+    """Wraps the runner's ops with CUDA events on the launching stream and sums GPU time per op
+    kind and shape (a profiling aid: events between launches keep the launches in order but add
+    a little time)."""
+
+    def __init__(self, ops=None):
+        self.ops = ops if ops is not None else CudaOps()
+        self.events: list = []
+
+    def _tag(self, name, args, kwargs):
+        if name == "gemm":
+            q, lin = args[0], args[2]
+            extra = " gated" if kwargs.get("gate") is not None else (" gelu" if kwargs.get("gelu") else "")
+            return f"gemm M={q.shape[0]} N={lin.weight.shape[0]} K={lin.weight.shape[1]}{extra}"
+        if name in ("quant", "ln_mod_quant"):
+            return f"{name} K={args[0].shape[1]}"
+        if name == "quant_seg":
+            return "quant_seg"
+        return name
+
+    def __getattr__(self, name):
+        fn = getattr(self.ops, name)
+
+        def timed(*args, **kwargs):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            out = fn(*args, **kwargs)
+            e.record()
+            self.events.append((self._tag(name, args, kwargs), s, e))
+            return out
+        return timed
+
+    def summary(self) -> list[dict]:
+        """[{op, calls, ms, us_per_call}] sorted by total time (synchronizes)."""
+        torch.cuda.synchronize()
+        agg: dict = {}
+        for tag, s, e in self.events:
+            n, ms = agg.get(tag, (0, 0.0))
+            agg[tag] = (n + 1, ms + s.elapsed_time(e))
+        rows = [{"op": k, "calls": n, "ms": round(ms, 3), "us_per_call": round(1e3 * ms / n, 1)}
+                for k, (n, ms) in agg.items()]
+        return sorted(rows, key=lambda r: -r["ms"])
+
+
 def ulysses_qkv_order(hidden: int, heads: int, head_dim: int, P: int) -> torch.Tensor:
     """Output-row order of a fused qkv projection that groups the rows by destination rank:
     new row (p, s, j, d) = old row s * hidden + (p * heads/P + j) * head_dim + d, for q/k/v s,
