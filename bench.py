@@ -473,6 +473,48 @@ def flux_op_breakdown(dev, side: int = 1024) -> dict:
             "other_ms_torch_ops": round(total - sum(r["ms"] for r in rows), 3), "ops": rows}
 
 
+def bench_glue(args, dev, peaks) -> dict:
+    """The FLUX block's HBM-bound glue kernels alone at 1024^2 shapes (4608 rows), GB/s of their
+    algorithmic bytes against the measured HBM peak; inputs rotate over sets larger than L2."""
+    import torch
+    from diffucore_b200 import flux, kernels
+    M, C, F = 4608, 3072, 12288
+    g = torch.Generator(device=dev).manual_seed(3)
+    nset = 3                   # 3 x 141 MB rows of the wide cases; 6 x 28 MB of the narrow ones (> 126 MB L2)
+    xs = [torch.randn(M, C, generator=g, device=dev).to(torch.bfloat16) for _ in range(2 * nset)]
+    big = [torch.randn(M, C + F, generator=g, device=dev).to(torch.bfloat16) for _ in range(nset)]
+    qkv = [torch.randn(M, 3, 24, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(nset)]
+    shift = (0.1 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
+    scale = (0.1 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
+    sc = (1 + 0.1 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
+    pe = flux.rope_table(torch.cat([torch.zeros(512, 3), flux.img_ids(128, 128, 2)[0]]).to(dev), (16, 56, 56), 10_000)
+    q = torch.empty(M, C + F, device=dev, dtype=torch.int8)
+    s = torch.empty(M, device=dev, dtype=torch.float32)
+    cases = {
+        "ln_mod_quant K=3072 group 256": (lambda i: kernels.ln_mod_quant(xs[i % len(xs)], shift, scale, 256, q[:, :C], s),
+                                          M * C * 3 + M * 4),
+        "quant_rows K=15360 group 256": (lambda i: kernels.quant_rows_into(big[i % nset], 256, q, s), M * (C + F) * 3 + M * 4),
+        "quant_rows K=15360 group 0": (lambda i: kernels.quant_rows_into(big[i % nset], 0, q, s), M * (C + F) * 3 + M * 4),
+        "quant_rows K=3072 group 256": (lambda i: kernels.quant_rows_into(xs[i % len(xs)], 256, q[:, :C], s), M * C * 3 + M * 4),
+        "qk_norm_rope 24 heads": (lambda i: kernels.qk_norm_rope(qkv[i % nset], sc, sc, pe), M * 2 * C * 2 * 2),
+    }
+    out = {"rows": M, "unit": "GB/s", "peak_hbm_gbs": peaks["hbm_gbs"]}
+    for name, (fn, nbytes) in cases.items():
+        for i in range(max(3, args.warmup)):
+            fn(i)
+        torch.cuda.synchronize()
+        n = max(10, args.steps)
+        st, en = _events(2)
+        st.record()
+        for i in range(n):
+            fn(i)
+        en.record()
+        torch.cuda.synchronize()
+        us = st.elapsed_time(en) * 1e3 / n
+        out[name] = {"us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / peaks["hbm_gbs"], 3)}
+    return out
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -480,7 +522,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-extras", action="store_true", help="headline attention only (for profiling)")
-    ap.add_argument("--only", default="all", choices=("all", "gemm", "flux"),
+    ap.add_argument("--only", default="all", choices=("all", "gemm", "flux", "glue"),
                     help="gemm / flux: time only the config-1 W8A8 linear / the FLUX DiT")
     ap.add_argument("--no-flux", action="store_true", help="skip the FLUX DiT timing")
     ap.add_argument("--op-breakdown", action="store_true",
@@ -499,6 +541,11 @@ def main() -> int:
     peaks = _peaks()
     if args.only == "flux" and args.op_breakdown:
         res = flux_op_breakdown(dev)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return 0
+    if args.only == "glue":
+        res = bench_glue(args, dev, peaks)
         if rank == 0:
             print(json.dumps(res), flush=True)
         return 0

@@ -18,6 +18,7 @@
 constexpr size_t kNoAllocScratch = static_cast<size_t>(DC_NOALLOC_SCRATCH_BYTES);
 #include "sm100.cuh"
 #include "quant.cuh"
+#include "rowquant.cuh"
 #include "gemm.cuh"
 #include "attn.cuh"
 #include "dit.cuh"
@@ -110,8 +111,61 @@ inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
 // ------------------------------------------------------------------------------ quantizer
 
+// Shared-memory streaming quantizers (rowquant.cuh): K % 256 == 0, 16-bit rows, no GELU.
+constexpr int kRowqWarps = 8;
+
+template <typename T, bool GROUP, bool LNMOD, bool SEG>
+int launch_rowq_warp(const dc::RowSrc& src, int64_t M, int64_t K, const void* shift, const void* scale, int8_t* q,
+                     float* s, cudaStream_t st) {
+  const int nit = static_cast<int>((K / 256 + 1) / 2);
+  const size_t smem = (LNMOD ? 2 * K * sizeof(T) : 0) + static_cast<size_t>(kRowqWarps) * 2 * K * sizeof(T) +
+                      static_cast<size_t>(kRowqWarps) * 2 * dc::kRotScratch * sizeof(float);
+  const int64_t ctas64 = (M + kRowqWarps - 1) / kRowqWarps;
+  const int ctas = static_cast<int>(ctas64 < sm_count() ? ctas64 : sm_count());
+  const T* sh = static_cast<const T*>(shift);
+  const T* sc = static_cast<const T*>(scale);
+  const int Ki = static_cast<int>(K);
+  int r = DC_OK;
+  auto go = [&](auto kernel) {
+    r = set_smem(kernel, static_cast<int>(smem));
+    if (r == DC_OK) kernel<<<ctas, 32 * kRowqWarps, smem, st>>>(src, M, Ki, sh, sc, q, s);
+  };
+  if (nit <= 2) go(dc::rowq_warp_kernel<T, GROUP, LNMOD, SEG, 2>);
+  else if (nit <= 4) go(dc::rowq_warp_kernel<T, GROUP, LNMOD, SEG, 4>);
+  else if (nit <= 6) go(dc::rowq_warp_kernel<T, GROUP, LNMOD, SEG, 6>);
+  else go(dc::rowq_warp_kernel<T, GROUP, LNMOD, SEG, 8>);
+  if (r) return r;
+  DC_CHECK_LAUNCH("quant_rows launch");
+  return DC_OK;
+}
+
+template <typename T, bool GROUP, bool SEG>
+int launch_rowq_cta(const dc::RowSrc& src, int64_t M, int64_t K, int8_t* q, float* s, cudaStream_t st) {
+  const int nit = static_cast<int>((K / 256 + 15) / 16);
+  const size_t smem = 2 * K * sizeof(T) + 16 * dc::kRotScratch * sizeof(float);
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 2;
+  const int ctas = static_cast<int>(M < cap ? M : cap);
+  const int Ki = static_cast<int>(K);
+  int r = DC_OK;
+  auto go = [&](auto kernel) {
+    r = set_smem(kernel, static_cast<int>(smem));
+    if (r == DC_OK) kernel<<<ctas, 256, smem, st>>>(src, M, Ki, q, s);
+  };
+  if (nit <= 2) go(dc::rowq_cta_kernel<T, GROUP, SEG, 2>);
+  else if (nit <= 3) go(dc::rowq_cta_kernel<T, GROUP, SEG, 3>);
+  else go(dc::rowq_cta_kernel<T, GROUP, SEG, 4>);
+  if (r) return r;
+  DC_CHECK_LAUNCH("quant_rows launch");
+  return DC_OK;
+}
+
 template <typename T, bool GROUP, int GELU, bool SEG = false>
 int launch_quant_t(const dc::RowSrc& src, int64_t M, int64_t K, int8_t* q, float* s, bool vec, cudaStream_t st) {
+  if constexpr (GELU == 0 && sizeof(T) == 2) {
+    if (vec && K % 256 == 0 && K <= 16384 && reinterpret_cast<uintptr_t>(q) % 16 == 0)
+      return K <= 4096 ? launch_rowq_warp<T, GROUP, false, SEG>(src, M, K, nullptr, nullptr, q, s, st)
+                       : launch_rowq_cta<T, GROUP, SEG>(src, M, K, q, s, st);
+  }
   if constexpr (!GROUP && GELU == 0 && sizeof(T) == 2) {
     if (vec && K > 4096) {
       const int64_t ctas64 = (M + 3) / 4;
@@ -600,6 +654,15 @@ int dc_ln_mod_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld
     return fail("ln_mod_quant: x, shift, scale must be 16-byte and q 8-byte aligned");
   if (int r = check_sm100()) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K % 256 == 0 && rows_per_mod >= M && reinterpret_cast<uintptr_t>(q) % 16 == 0 &&
+      (x_dtype == DC_DTYPE_BF16 || x_dtype == DC_DTYPE_F16)) {
+    const dc::RowSrc src = dc::plain_rows(x, ldx);
+    if (x_dtype == DC_DTYPE_BF16)
+      return group ? launch_rowq_warp<__nv_bfloat16, true, true, false>(src, M, K, shift, scale, q, s, st)
+                   : launch_rowq_warp<__nv_bfloat16, false, true, false>(src, M, K, shift, scale, q, s, st);
+    return group ? launch_rowq_warp<__half, true, true, false>(src, M, K, shift, scale, q, s, st)
+                 : launch_rowq_warp<__half, false, true, false>(src, M, K, shift, scale, q, s, st);
+  }
   switch (x_dtype) {
     case DC_DTYPE_BF16:
       return group ? launch_ln_mod_quant<__nv_bfloat16, true>(x, M, K, ldx, shift, scale, rows_per_mod, mod_ld, q, s, st)

@@ -58,27 +58,29 @@ ln_mod_quant_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, cons
         for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
       }
     }
-    // mean and biased variance in fp32 (two passes over registers)
-    float acc = 0.0f;
+    // mean and biased variance in fp32 (two passes over registers, four independent sum chains)
+    float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int i = 0; i < VPT; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc += v[i][j];
-    const float mean = __fmul_rn(warp_sum(acc), inv_k);
-    acc = 0.0f;
+      for (int j = 0; j < 8; ++j) a4[j & 3] = __fadd_rn(a4[j & 3], v[i][j]);
+    const float mean = __fmul_rn(warp_sum(__fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]))), inv_k);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) a4[c] = 0.0f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = lane + 32 * i;
       if (vi < nvec) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) { const float d = __fsub_rn(v[i][j], mean); acc = __fmaf_rn(d, d, acc); }
+        for (int j = 0; j < 8; ++j) { const float d = __fsub_rn(v[i][j], mean); a4[j & 3] = __fmaf_rn(d, d, a4[j & 3]); }
       }
     }
-    const float rstd = rsqrtf(__fadd_rn(__fmul_rn(warp_sum(acc), inv_k), 1e-6f));
+    const float var = __fmul_rn(warp_sum(__fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]))), inv_k);
+    const float rstd = rsqrtf(__fadd_rn(var, 1e-6f));
     const int64_t b = row / rows_per_mod;
     const T* shr = shift + b * mod_ld;
     const T* scr = scale + b * mod_ld;
-    float am = 0.0f;
+    float am4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = lane + 32 * i;
@@ -96,8 +98,9 @@ ln_mod_quant_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, cons
       // the 32 lanes at one i hold one 256-wide group; lanes past the row end hold zeros
       if (GROUP) hadamard256_warp(v[i]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(v[i][j]));
+      for (int j = 0; j < 8; ++j) am4[j & 3] = fmaxf(am4[j & 3], fabsf(v[i][j]));
     }
+    float am = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
     const float sc = fmaxf(__fdiv_rn(am, 127.0f), 1e-30f);

@@ -76,11 +76,16 @@ __device__ __forceinline__ float gelu_dtype(float h, int mode) {
     return Vec8<T>::round_trip(__fmul_rn(__fmul_rn(0.5f, h), e));
   }
   if (mode == kGeluTanh) {
-    // 0.5 * h * (1 + tanh(sqrt(2/pi) * (h + 0.044715 * h^3)))
+    // 0.5 * h * (1 + tanh(u)), u = sqrt(2/pi) * (h + 0.044715 * h^3), computed through the
+    // identity 0.5 * (1 + tanh(u)) = 1 / (1 + e^(-2u)): h / (1 + 2^(-2 u log2 e)) with one MUFU
+    // exp2 and one MUFU reciprocal (relative error ~1e-6, no cancellation for negative h), then
+    // rounded to the 16-bit dtype like torch's GELU.
     const float h3 = __fmul_rn(__fmul_rn(h, h), h);
-    const float inner = __fmul_rn(0.7978845608028654f, __fadd_rn(h, __fmul_rn(0.044715f, h3)));
-    const float e = __fadd_rn(1.0f, tanhf(inner));
-    return Vec8<T>::round_trip(__fmul_rn(__fmul_rn(0.5f, h), e));
+    const float u = __fmul_rn(0.7978845608028654f, __fadd_rn(h, __fmul_rn(0.044715f, h3)));
+    float e, r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(-2.8853900817779268f, u)));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.0f, e)));
+    return Vec8<T>::round_trip(__fmul_rn(h, r));
   }
   return h;
 }
@@ -358,7 +363,7 @@ quant_rows_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, fl
   const int nvec = K >> 3;
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     float v[VPT][8];
-    float amax = 0.0f;
+    float am4[4] = {0.0f, 0.0f, 0.0f, 0.0f};     // independent max chains
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = tid + i * kQuantThreads;
@@ -376,8 +381,9 @@ quant_rows_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, fl
       // past the row end hold zeros and are discarded; every lane joins the shuffles.
       if (GROUP) hadamard256_warp(v[i]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+      for (int j = 0; j < 8; ++j) am4[j & 3] = fmaxf(am4[j & 3], fabsf(v[i][j]));
     }
+    float amax = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if ((tid & 31) == 0) red[tid >> 5] = amax;

@@ -1,0 +1,294 @@
+// Per-row int8 quantizers that stream rows through shared memory.
+//
+// Rows arrive by cp.async (16-byte chunks, double-buffered: the next row of a warp or CTA is in
+// flight while the current one is processed), so HBM sees many independent requests per SM and
+// no row is read twice. The 256-wide ConvRot rotation runs as radix-4 stages in registers around
+// one shared-memory transpose instead of warp shuffles (2 shared-memory accesses per element
+// instead of 8 shuffles):
+//   element index in a group e = 64 d3 + 16 d2 + 4 d1 + d0 (base-4 digits, d3 most significant);
+//   layout X: lane L (of 16) holds e = 64 a + 16 b + L (a = d3, b = d2): stages d3, d2 in registers;
+//   transpose through a swizzled scratch (word 16 (e >> 4) + ((e & 15) ^ (e >> 4 & 15)), so both
+//   the stores of X and the loads of Y hit 32 distinct banks);
+//   layout Y: lane L holds e = 16 L + c (c = 4 d1 + d0): stages d1, d0 in registers, then x 1/16.
+// Each stage computes S = (x[d=0] + x[d=1]) + (x[d=2] + x[d=3]) and y = S - 2 x[3 - d], in the
+// order the warp-shuffle butterfly of quant.cuh (and the CPU oracle) uses, so codes and scales are
+// bit-identical to it. Without rotation the same kernels read layout Y directly.
+//
+//   rowq_warp_kernel  one warp per row, K <= 4096 (K % 256 == 0); optionally LayerNorm + AdaLN
+//                     modulation first (one shift/scale vector for all rows)
+//   rowq_cta_kernel   one CTA (16 half-warps) per row, 4096 < K <= 16384 (K % 256 == 0)
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+#include "sm100.cuh"
+#include "quant.cuh"
+
+namespace dc {
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
+// Radix-4 stage over the outer index of x[4 a + b] (digit a), and over the inner index (digit b).
+__device__ __forceinline__ void r4_outer(float (&x)[16]) {
+  float y[16];
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const float s = quad_sum(x[b], x[4 + b], x[8 + b], x[12 + b]);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) y[4 * a + b] = __fsub_rn(s, __fmul_rn(2.0f, x[4 * (3 - a) + b]));
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = y[i];
+}
+__device__ __forceinline__ void r4_inner(float (&x)[16]) {
+  float y[16];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const float s = quad_sum(x[4 * a], x[4 * a + 1], x[4 * a + 2], x[4 * a + 3]);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) y[4 * a + b] = __fsub_rn(s, __fmul_rn(2.0f, x[4 * a + 3 - b]));
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = y[i];
+}
+
+constexpr int kRotScratch = 272;   // floats per half-warp: 256 + 16 so the two halves use other banks
+
+// Rotate one group held in layout X by the 16 lanes of a half-warp (L = lane & 15); returns it in
+// layout Y (times 1/16). Both halves of the warp must call it together (it syncs the warp).
+__device__ __forceinline__ void rotate256_half(float (&x)[16], float* scr, int L) {
+  r4_outer(x);                      // d3
+  r4_inner(x);                      // d2
+#pragma unroll
+  for (int i = 0; i < 16; ++i) scr[16 * i + (L ^ i)] = x[i];       // e >> 4 == i, e & 15 == L
+  __syncwarp();
+#pragma unroll
+  for (int c = 0; c < 16; ++c) x[c] = scr[16 * L + (c ^ L)];
+  __syncwarp();
+  r4_outer(x);                      // d1
+  r4_inner(x);                      // d0
+#pragma unroll
+  for (int c = 0; c < 16; ++c) x[c] = __fmul_rn(x[c], 0.0625f);
+}
+
+template <typename T>
+__device__ __forceinline__ float ld_elem(const T* p) { return Vec8<T>::one(p); }
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// 16 values of group g of a row in shared memory: layout X (rotation) or Y (none).
+template <typename T, bool GROUP>
+__device__ __forceinline__ void load_group(const T* r, int g, int L, float (&x)[16]) {
+  const T* base = r + 256 * g;
+  if (GROUP) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = ld_elem(base + 16 * i + L);   // e = 64 a + 16 b + L, i = 4 a + b
+  } else {
+    float f[8];
+    Vec8<T>::load(base + 16 * L, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = f[j];
+    Vec8<T>::load(base + 16 * L + 8, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[8 + j] = f[j];
+  }
+}
+
+// Column index of value i of group g in the layout load_group used.
+template <bool GROUP>
+__device__ __forceinline__ int group_col(int g, int L, int i) {
+  return 256 * g + (GROUP ? 16 * i + L : 16 * L + i);
+}
+
+// Codes of a group's 16 values (layout Y: 16 consecutive columns) -> one 16-byte store.
+__device__ __forceinline__ void store_codes16(int8_t* dst, const float (&v)[16], float scale, float inv) {
+  float a[8], b[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) { a[j] = v[j]; b[j] = v[8 + j]; }
+  const uint2 lo = quant8(a, scale, inv), hi = quant8(b, scale, inv);
+  *reinterpret_cast<uint4*>(dst) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+}
+
+// Issue this lane's 16-byte chunks of one row (chunk stride = threads taking part).
+template <typename T, bool SEG>
+__device__ __forceinline__ void issue_row(const RowSrc& src, int64_t row, int K, T* dst, int t, int nt) {
+  for (int c = t; c < (K >> 3); c += nt) cp_async16(dst + 8 * c, src_ptr<T, SEG>(src, row, 8 * c));
+}
+
+// One warp per row. NIT >= ceil(K / 512) group pairs (a half-warp per group). Shared memory:
+// [LNMOD: shift, scale: 2 K of T] [per warp: 2 row buffers of K of T] [per warp: 2 x kRotScratch fp32].
+template <typename T, bool GROUP, bool LNMOD, bool SEG, int NIT>
+__global__ void __launch_bounds__(256, 1)
+rowq_warp_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift, const T* __restrict__ mscale,
+                 int8_t* __restrict__ q, float* __restrict__ s) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int half = lane >> 4, L = lane & 15;
+  const int ng = K >> 8;
+  T* smod = reinterpret_cast<T*>(sm);
+  const size_t mod_bytes = LNMOD ? static_cast<size_t>(2 * K) * sizeof(T) : 0;
+  T* rows = reinterpret_cast<T*>(sm + mod_bytes) + static_cast<size_t>(warp) * 2 * K;
+  float* scr = reinterpret_cast<float*>(sm + mod_bytes + static_cast<size_t>(nwarps) * 2 * K * sizeof(T)) +
+               (warp * 2 + half) * kRotScratch;
+  if (LNMOD) {
+    for (int c = threadIdx.x; c < K; c += blockDim.x) { smod[c] = shift[c]; smod[K + c] = mscale[c]; }
+    __syncthreads();
+  }
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * nwarps;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * nwarps + warp;
+  if (first < M) issue_row<T, SEG>(src, first, K, rows, lane, 32);
+  cp_async_commit();
+  if (first + stride < M) issue_row<T, SEG>(src, first + stride, K, rows + K, lane, 32);
+  cp_async_commit();
+  int buf = 0;
+  for (int64_t row = first; row < M; row += stride, buf ^= 1) {
+    cp_async_wait<1>();
+    __syncwarp();
+    const T* r = rows + buf * K;
+    float mean = 0.0f, rstd = 1.0f;
+    if (LNMOD) {
+      const float inv_k = 1.0f / static_cast<float>(K);
+      float a4[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int c = lane; c < (K >> 3); c += 32) {
+        float f[8];
+        Vec8<T>::load(r + 8 * c, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a4[j & 3] = __fadd_rn(a4[j & 3], f[j]);
+      }
+      mean = __fmul_rn(warp_sum_f(__fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]))), inv_k);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) a4[j] = 0.f;
+      for (int c = lane; c < (K >> 3); c += 32) {
+        float f[8];
+        Vec8<T>::load(r + 8 * c, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { const float d = __fsub_rn(f[j], mean); a4[j & 3] = __fmaf_rn(d, d, a4[j & 3]); }
+      }
+      const float var = __fmul_rn(warp_sum_f(__fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]))), inv_k);
+      rstd = rsqrtf(__fadd_rn(var, 1e-6f));
+    }
+    float vals[NIT][16];
+    float am4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int it = 0; it < NIT; ++it) {
+      const int g = 2 * it + half;
+      const bool live = g < ng;
+      float xv[16];
+      if (live) {
+        load_group<T, GROUP>(r, g, L, xv);
+        if (LNMOD) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int col = group_col<GROUP>(g, L, i);
+            const float n = Vec8<T>::round_trip(__fmul_rn(__fsub_rn(xv[i], mean), rstd));
+            const float a = Vec8<T>::round_trip(__fadd_rn(1.0f, ld_elem(smod + K + col)));
+            xv[i] = Vec8<T>::round_trip(__fadd_rn(Vec8<T>::round_trip(__fmul_rn(a, n)), ld_elem(smod + col)));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) xv[i] = 0.0f;
+      }
+      if (GROUP && 2 * it < ng) rotate256_half(xv, scr, L);     // warp-uniform condition
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        vals[it][c] = xv[c];
+        am4[c & 3] = fmaxf(am4[c & 3], fabsf(xv[c]));
+      }
+    }
+    float am = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const float scale = fmaxf(__fdiv_rn(am, 127.0f), 1e-30f);
+    const float inv = __fdiv_rn(1.0f, scale);
+    int8_t* qr = q + row * static_cast<int64_t>(K);
+#pragma unroll
+    for (int it = 0; it < NIT; ++it) {
+      const int g = 2 * it + half;
+      if (g < ng) store_codes16(qr + 256 * g + 16 * L, vals[it], scale, inv);
+    }
+    if (lane == 0) s[row] = scale;
+    __syncwarp();
+    if (row + 2 * stride < M) issue_row<T, SEG>(src, row + 2 * stride, K, rows + buf * K, lane, 32);
+    cp_async_commit();
+  }
+  cp_async_wait<0>();
+}
+
+// One CTA of 256 threads per row; group g goes to half-warp g % 16 at iteration g / 16
+// (NIT >= ceil(K / 4096)). Shared memory: [2 row buffers of K of T] [16 x kRotScratch fp32].
+template <typename T, bool GROUP, bool SEG, int NIT>
+__global__ void __launch_bounds__(256, 2)
+rowq_cta_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, float* __restrict__ s) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  __shared__ float red[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane >> 4, L = lane & 15;
+  const int hw = warp * 2 + half;
+  const int ng = K >> 8;
+  T* rows = reinterpret_cast<T*>(sm);
+  float* scr = reinterpret_cast<float*>(sm + static_cast<size_t>(2 * K) * sizeof(T)) + hw * kRotScratch;
+  const int64_t first = blockIdx.x;
+  if (first < M) issue_row<T, SEG>(src, first, K, rows, threadIdx.x, 256);
+  cp_async_commit();
+  if (first + gridDim.x < M) issue_row<T, SEG>(src, first + gridDim.x, K, rows + K, threadIdx.x, 256);
+  cp_async_commit();
+  int buf = 0;
+  for (int64_t row = first; row < M; row += gridDim.x, buf ^= 1) {
+    cp_async_wait<1>();
+    __syncthreads();
+    const T* r = rows + buf * K;
+    float vals[NIT][16];
+    float am4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int it = 0; it < NIT; ++it) {
+      const int g = 16 * it + hw;
+      float xv[16];
+      if (g < ng) {
+        load_group<T, GROUP>(r, g, L, xv);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) xv[i] = 0.0f;
+      }
+      if (GROUP && 16 * it + 2 * warp < ng) rotate256_half(xv, scr, L);   // warp-uniform
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        vals[it][c] = xv[c];
+        am4[c & 3] = fmaxf(am4[c & 3], fabsf(xv[c]));
+      }
+    }
+    float am = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    if (lane == 0) red[warp] = am;
+    __syncthreads();
+    am = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) am = fmaxf(am, red[w]);
+    const float scale = fmaxf(__fdiv_rn(am, 127.0f), 1e-30f);
+    const float inv = __fdiv_rn(1.0f, scale);
+    int8_t* qr = q + row * static_cast<int64_t>(K);
+#pragma unroll
+    for (int it = 0; it < NIT; ++it) {
+      const int g = 16 * it + hw;
+      if (g < ng) store_codes16(qr + 256 * g + 16 * L, vals[it], scale, inv);
+    }
+    if (threadIdx.x == 0) s[row] = scale;
+    __syncthreads();                     // row buffer and red[] free again
+    if (row + 2 * gridDim.x < M) issue_row<T, SEG>(src, row + 2 * gridDim.x, K, rows + buf * K, threadIdx.x, 256);
+    cp_async_commit();
+  }
+  cp_async_wait<0>();
+}
+
+}  // namespace dc

@@ -74,6 +74,21 @@ def test_quant_rows_strided_and_fp32():
     assert np.array_equal(q.cpu().numpy(), oq) and np.array_equal(s.cpu().numpy(), os_)
 
 
+@pytest.mark.parametrize("group", [0, 256])
+@pytest.mark.parametrize("K", [256, 768, 4352, 12288, 15360, 16384])
+def test_quant_rows_streaming_kernels_bit_exact(group, K):
+    """Rows streamed through shared memory (warp per row up to K = 4096, CTA per row above), the
+    ConvRot butterfly as register stages around a shared-memory transpose: codes and scales equal
+    the oracle's, including an odd number of 256-groups (a half-warp idles) and rows spanning
+    several CTA iterations."""
+    g = torch.Generator().manual_seed(K + group)
+    x = (torch.randn(37, K, generator=g) * torch.rand(37, 1, generator=g) * 4).to(torch.bfloat16)
+    x[5] = 0                                                  # a zero row: scale 1e-30, codes 0
+    q, s = kernels.quant_rows(x.to(DEV), group)
+    oq, os_ = oracle.quant_rows(torch_to_bits(x), "bf16", group)
+    assert np.array_equal(q.cpu().numpy(), oq) and np.array_equal(s.cpu().numpy(), os_)
+
+
 def test_quant_rows_gelu_modes():
     g = torch.Generator().manual_seed(4)
     h = (torch.randn(64, 1024, generator=g) * 3).to(torch.bfloat16)
