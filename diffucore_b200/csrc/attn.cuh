@@ -776,11 +776,15 @@ attn_db_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant_
       const float row_mt = fmaxf(mt, s_xchg[j & 1][hf ^ 1][r_local]);
       if (j == 0) {
         m = row_mt;
-      } else if (row_mt > m + kLazyRescale) {
+      } else if (__any_sync(0xffffffffu, row_mt > m + kLazyRescale)) {
         // Rare: move the running max up and rescale this warp's half of O once P.V(j - 1) landed.
-        const float alpha = ex2_approx(m - row_mt);
+        // The branch is warp-uniform (its body holds warp-collective tcgen05 loads/stores); rows
+        // whose max did not move get alpha = 1. Both warps of these rows see the same row maxima,
+        // so they take the branch together.
+        const float mnew = fmaxf(m, row_mt);
+        const float alpha = ex2_approx(m - mnew);
         l2 = __fmul2_rn(l2, make_float2(alpha, alpha));
-        m = row_mt;
+        m = mnew;
         ok = mbar_wait(&pv_done, (j - 1) & 1, abort);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();

@@ -163,6 +163,25 @@ def test_config2_full_size_properties(mode, kernel):
     assert np.array_equal(got["q_codes"].cpu().numpy(), want["q_codes"])
 
 
+@pytest.mark.parametrize("mode", ["ref", "block64"])
+def test_running_max_moves_every_tile(mode, kernel):
+    """Scores that grow along the keys (K rows scaled up tile after tile) move every row's running
+    max by far more than the lazy-rescale headroom at each 128-key tile, for some rows of a warp
+    and not others: the O rescale path runs, warp-uniformly, and the result still matches the
+    oracle's exact softmax."""
+    g = torch.Generator().manual_seed(9)
+    B, L, H, D = 1, 1024, 2, 128
+    q = torch.randn(B, L, H, D, generator=g)
+    q[:, ::2] *= 0.05                                          # half the rows barely move
+    ramp = torch.linspace(0.2, 24.0, L).view(1, L, 1, 1)   # +9 (log2) per 128 keys for 2-sigma rows
+    base = torch.randn(1, 1, H, D, generator=g)
+    k = (base + 0.3 * torch.randn(B, L, H, D, generator=g)) * ramp
+    v = torch.randn(B, L, H, D, generator=g)
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    out = _attention.attention_blhd(q.to(DEV), k.to(DEV), v.to(DEV), "int8_turing", quant_mode=mode)
+    _check_against_oracle(q, k, v, out, torch.bfloat16, mode, D ** -0.5)
+
+
 def test_fma_pipe_exp2_accuracy():
     """The polynomial exp2 the softmax runs on the FMA pipe for a third of the keys stays within
     1e-4 relative of CUDA's exp2f over the range P takes (arguments <= 8), and is 0 / tiny far below."""
