@@ -442,6 +442,64 @@ def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048)) -> dict:
     return out
 
 
+def bench_sdxl(args, dev, peaks, steps: int = 25) -> dict:
+    """SDXL-architecture UNet, random fp16 weights, attention / FF linears W8A8,
+    INT8 self-attention (head dim 64), CFG batch 2 at 1024^2 (latent 4 x 128 x 128, context
+    [2, 77, 2048], adm [2, 2816]); Euler, 25 steps. s/step = CUDA-event time of a whole 25-step run
+    / 25 after a 3-step warm-up; int8 work per step counted by hooks on one forward."""
+    import torch
+    from diffucore_b200 import _int8, unet
+    t0 = time.perf_counter()
+    model = unet.build_sdxl_unet(seed=0, device=dev)
+    build_s = time.perf_counter() - t0
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(1, 4, 128, 128, generator=g, device=dev).half()
+    ctx = torch.randn(2, 77, 2048, generator=g, device=dev).half()
+    y = torch.randn(2, 2816, generator=g, device=dev).half()
+    work = {"linear_int8_ops": 0, "attn_int8_ops": 0, "attn_f16_ops": 0}
+    hooks = []
+
+    def lin_hook(mod, inp, out):
+        m = inp[0].numel() // inp[0].shape[-1]
+        work["linear_int8_ops"] += 2 * m * mod.in_features * mod.out_features
+
+    def attn_hook(mod, inp, out):
+        b, l, _ = inp[0].shape
+        if mod.is_selfattn and isinstance(mod.to_q, _int8.Int8Linear):
+            # the shared-quantization path calls the three projections' GEMMs directly
+            for lin in (mod.to_q, mod.to_k, mod.to_v):
+                work["linear_int8_ops"] += 2 * b * l * lin.in_features * lin.out_features
+        if mod.attn_backend == "int8_turing":
+            ops = 2 * b * mod.heads * l * l * mod.dim_head
+            work["attn_int8_ops"] += ops
+            work["attn_f16_ops"] += ops
+    for m in model.modules():
+        if isinstance(m, _int8.Int8Linear):
+            hooks.append(m.register_forward_hook(lin_hook))
+        elif isinstance(m, unet.CrossAttention):
+            hooks.append(m.register_forward_hook(attn_hook))
+    with torch.no_grad():
+        model(x.expand(2, -1, -1, -1), torch.full((2,), 500.0, device=dev), ctx, y)
+    for h in hooks:
+        h.remove()
+    unet.euler_cfg_sample(model, x, ctx, y, steps=3)
+    torch.cuda.synchronize()
+    s, e = _events(2)
+    s.record()
+    out = unet.euler_cfg_sample(model, x, ctx, y, steps=steps)
+    e.record()
+    torch.cuda.synchronize()
+    s_step = s.elapsed_time(e) * 1e-3 / steps
+    res = {"model": "SDXL-architecture UNet (320/640/1280, depth 0/2/10, head dim 64, context 2048), random fp16 "
+                    "weights, attention / FF linears W8A8 (group 0), INT8 self-attention",
+           "batch": "CFG 2", "latent": [4, 128, 128], "sampler": "euler", "steps": steps, "build_s": build_s,
+           "s_per_step": s_step, "finite": bool(torch.isfinite(out).all()),
+           "int8_work_per_step_T": {k: v / 1e12 for k, v in work.items()}}
+    del model
+    torch.cuda.empty_cache()
+    return res
+
+
 def flux_op_breakdown(dev, side: int = 1024) -> dict:
     """GPU time per op kind of one FLUX forward at ``side``^2 on one GPU (after two warm-ups)."""
     import torch
@@ -522,7 +580,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-extras", action="store_true", help="headline attention only (for profiling)")
-    ap.add_argument("--only", default="all", choices=("all", "gemm", "flux", "glue"),
+    ap.add_argument("--only", default="all", choices=("all", "gemm", "flux", "glue", "sdxl"),
                     help="gemm / flux: time only the config-1 W8A8 linear / the FLUX DiT")
     ap.add_argument("--no-flux", action="store_true", help="skip the FLUX DiT timing")
     ap.add_argument("--op-breakdown", action="store_true",
@@ -544,8 +602,8 @@ def main() -> int:
         if rank == 0:
             print(json.dumps(res), flush=True)
         return 0
-    if args.only == "glue":
-        res = bench_glue(args, dev, peaks)
+    if args.only in ("glue", "sdxl"):
+        res = bench_glue(args, dev, peaks) if args.only == "glue" else bench_sdxl(args, dev, peaks)
         if rank == 0:
             print(json.dumps(res), flush=True)
         return 0
@@ -601,6 +659,8 @@ def main() -> int:
         del plan, sets
         torch.cuda.empty_cache()
         line["flux_dit"] = bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048) if world == 1 else (2048,))
+        if world == 1:
+            line["sdxl_unet"] = bench_sdxl(args, dev, peaks)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
