@@ -38,7 +38,7 @@ GEMM_OPS = 2 * GEMM_M * GEMM_N * GEMM_K
 METRIC = "INT8 TOPS, INT8 flash attention (BASELINE config 2: B=1, H=24, S=4608, D=128, bf16)"
 # DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, one capture of each
 # kernel on these workloads): attention main kernel, W8A8 GEMM, activation quantizer.
-TRAFFIC_ATTN = 60.65e6
+TRAFFIC_ATTN = 60.71e6
 TRAFFIC_GEMM = 22.09e6
 TRAFFIC_QUANT = 25.21e6
 CONFIG = {"workload": "int8_flash_attention_config2", "batch": B, "heads": H, "seq_len": S, "head_dim": D,
