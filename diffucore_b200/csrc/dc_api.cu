@@ -162,7 +162,10 @@ int launch_rowq_cta(const dc::RowSrc& src, int64_t M, int64_t K, int8_t* q, floa
 template <typename T, bool GROUP, int GELU, bool SEG = false>
 int launch_quant_t(const dc::RowSrc& src, int64_t M, int64_t K, int8_t* q, float* s, bool vec, cudaStream_t st) {
   if constexpr (GELU == 0 && sizeof(T) == 2) {
-    if (vec && K % 256 == 0 && K <= 16384 && reinterpret_cast<uintptr_t>(q) % 16 == 0)
+    // Shared-memory streaming kernels where they pay: with the ConvRot rotation (no warp-shuffle
+    // butterfly), and for wide rows (no second pass over rows L2 has evicted). Plain rows up to
+    // 4096 wide keep the register warp kernel below, which has more rows in flight per SM.
+    if (vec && K % 256 == 0 && K <= 16384 && reinterpret_cast<uintptr_t>(q) % 16 == 0 && (GROUP || K > 4096))
       return K <= 4096 ? launch_rowq_warp<T, GROUP, false, SEG>(src, M, K, nullptr, nullptr, q, s, st)
                        : launch_rowq_cta<T, GROUP, SEG>(src, M, K, q, s, st);
   }
