@@ -108,3 +108,48 @@ def test_ulysses_two_ranks_match_one_rank(tmp_path, group):
     for i in range(len(single)):
         joined = torch.cat([parts[0]["outs"][i], parts[1]["outs"][i]], dim=0)
         assert torch.equal(joined, single[i])
+
+
+WIDE = dict(CFG, hidden_size=1024, num_heads=8, depth=1, depth_single_blocks=1)
+
+
+def _wide_model(group: int) -> flux.Flux:
+    model = flux.Flux(flux.FluxConfig(**WIDE))
+    flux.init_random_(model, seed=1, device="cpu")
+    flux.quantize_linears(model, model.block_linear_names(), "cpu", group=group)
+    return model.eval()
+
+
+def _wide_inputs():
+    g = torch.Generator().manual_seed(13)
+    img = torch.randn(88, 64, generator=g).to(torch.bfloat16)            # 8 x 11 patches
+    txt = torch.randn(40, 64, generator=g).to(torch.bfloat16)
+    y = torch.randn(1, 32, generator=g).to(torch.bfloat16)
+    return img, txt, y, flux.img_ids(16, 22, 2), flux.txt_ids(40)
+
+
+def _wide_worker(rank: int, world: int, port: int, path: str) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        img, txt, y, iid, tid = _wide_inputs()
+        outs, rows = _run(_wide_model(256), img, txt, y, iid, tid, (0.8,), pg=dist.group.WORLD)
+        torch.save({"outs": outs, "rows": rows}, f"{path}.{rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_ulysses_four_and_eight_ranks_match_one_rank(tmp_path, world):
+    """8 heads, 40 text + 88 image tokens split over 4 and 8 gloo ranks (16 rows each at 8 ranks,
+    so three ranks hold text rows and one holds both kinds): same velocity as one rank, bit for bit."""
+    img, txt, y, iid, tid = _wide_inputs()
+    single, _ = _run(_wide_model(256), img, txt, y, iid, tid, (0.8,))
+    path = str(tmp_path / "out")
+    mp.start_processes(_wide_worker, args=(world, _free_port(), path), nprocs=world, join=True,
+                       start_method="spawn")
+    parts = [torch.load(f"{path}.{r}") for r in range(world)]
+    assert parts[0]["rows"][0] == 0 and parts[-1]["rows"][1] == 88
+    joined = torch.cat([p["outs"][0] for p in parts], dim=0)
+    assert torch.equal(joined, single[0])
+
