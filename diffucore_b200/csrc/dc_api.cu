@@ -694,12 +694,12 @@ int dc_qk_norm_rope(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64
   p.q_scale[0] = q_scale0; p.k_scale[0] = k_scale0;
   p.q_scale[1] = q_scale1 ? q_scale1 : q_scale0; p.k_scale[1] = k_scale1 ? k_scale1 : k_scale0;
   p.split_row = split_row; p.pe = pe; p.pe_row0 = pe_row0;
-  const int64_t tasks = L * H * 2;
-  const int64_t ctas64 = (tasks + 7) / 8;
-  const int ctas = static_cast<int>(ctas64 < static_cast<int64_t>(sm_count()) * 16 ? ctas64 : sm_count() * 16);
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  const int ctas = static_cast<int>(L < cap ? L : cap);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == DC_DTYPE_BF16) dc::qk_norm_rope_kernel<__nv_bfloat16><<<ctas, 256, 0, st>>>(p);
-  else if (dtype == DC_DTYPE_F16) dc::qk_norm_rope_kernel<__half><<<ctas, 256, 0, st>>>(p);
+  constexpr int threads = 32 * dc::kRopeWarps;
+  if (dtype == DC_DTYPE_BF16) dc::qk_norm_rope_kernel<__nv_bfloat16><<<ctas, threads, 0, st>>>(p);
+  else if (dtype == DC_DTYPE_F16) dc::qk_norm_rope_kernel<__half><<<ctas, threads, 0, st>>>(p);
   else return fail("qk_norm_rope: dtype must be fp16 or bf16");
   DC_CHECK_LAUNCH("qk_norm_rope launch");
   return DC_OK;

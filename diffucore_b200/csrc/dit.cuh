@@ -125,59 +125,72 @@ struct QkNormRopeParams {
   int64_t pe_row0;           // row r of qkv uses pe row pe_row0 + r
 };
 
-// One warp per (row, head, q|k) vector of 128: lane holds elements 4 lane .. 4 lane + 3, i.e.
-// rotary pairs 2 lane and 2 lane + 1.
+// One CTA per row (grid-stride), 8 warps; warp w takes the row's (head, q|k) vectors w, w + 8, ...
+// (lane holds elements 4 lane .. 4 lane + 3 = rotary pairs 2 lane, 2 lane + 1). The row's RoPE
+// entries are loaded once per warp and all of a warp's vectors are loaded before any is computed.
 template <typename T>
-__global__ void __launch_bounds__(256)
+__device__ __forceinline__ void rms_rope4(uint2& raw, const T* scl, float4 f0, float4 f1) {
+  const uint2 sraw = *reinterpret_cast<const uint2*>(scl);
+  float x[4], g[4];
+  {
+    float tmp[8], stmp[8];
+    Vec8<T>::from_raw(make_uint4(raw.x, raw.y, 0u, 0u), tmp);
+    Vec8<T>::from_raw(make_uint4(sraw.x, sraw.y, 0u, 0u), stmp);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { x[j] = tmp[j]; g[j] = stmp[j]; }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(x[j], x[j]));
+  const float rrms = rsqrtf(__fadd_rn(__fmul_rn(warp_sum(ss), 1.0f / 128.0f), 1e-6f));
+  float y[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) y[j] = rnd<T>(__fmul_rn(rnd<T>(__fmul_rn(x[j], rrms)), g[j]));
+  // pair 0: (y0, y1) with f0 = {f00, f01, f10, f11}; pair 1: (y2, y3) with f1
+  const float o0 = rnd<T>(__fadd_rn(__fmul_rn(f0.x, y[0]), __fmul_rn(f0.y, y[1])));
+  const float o1 = rnd<T>(__fadd_rn(__fmul_rn(f0.z, y[0]), __fmul_rn(f0.w, y[1])));
+  const float o2 = rnd<T>(__fadd_rn(__fmul_rn(f1.x, y[2]), __fmul_rn(f1.y, y[3])));
+  const float o3 = rnd<T>(__fadd_rn(__fmul_rn(f1.z, y[2]), __fmul_rn(f1.w, y[3])));
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    raw.x = pack_bf16x2(o0, o1);
+    raw.y = pack_bf16x2(o2, o3);
+  } else {
+    raw.x = pack_f16x2(o0, o1);
+    raw.y = pack_f16x2(o2, o3);
+  }
+}
+
+constexpr int kRopeWarps = 8;
+constexpr int kRopeBatch = 6;     // vectors per warp loaded together (2 H / 8 for H = 24)
+
+template <typename T>
+__global__ void __launch_bounds__(32 * kRopeWarps)
 qk_norm_rope_kernel(const QkNormRopeParams p) {
-  const int lane = threadIdx.x & 31;
-  const int64_t tasks = p.L * p.H * 2;
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < tasks; t += nwarps) {
-    const int64_t row = t / (2 * p.H);
-    const int rem = static_cast<int>(t - row * 2 * p.H);
-    const int is_k = rem & 1;
-    const int h = rem >> 1;
-    T* base = static_cast<T*>(p.qkv) + row * p.ld_row + (is_k ? p.k_off : p.q_off) + static_cast<int64_t>(h) * 128 + lane * 4;
-    const bool first = row < p.split_row;
-    const void* sv = is_k ? (first ? p.k_scale[0] : p.k_scale[1]) : (first ? p.q_scale[0] : p.q_scale[1]);
-    const T* scl = static_cast<const T*>(sv) + lane * 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nvec = static_cast<int>(2 * p.H);
+  for (int64_t row = blockIdx.x; row < p.L; row += gridDim.x) {
     const float4* pe4 = reinterpret_cast<const float4*>(p.pe + (p.pe_row0 + row) * 256 + lane * 8);
-    const uint2 raw = *reinterpret_cast<const uint2*>(base);
-    const uint2 sraw = *reinterpret_cast<const uint2*>(scl);
     const float4 f0 = pe4[0], f1 = pe4[1];
-    float x[4], g[4];
-    {
-      const uint4 u = make_uint4(raw.x, raw.y, 0u, 0u);
-      const uint4 su = make_uint4(sraw.x, sraw.y, 0u, 0u);
-      float tmp[8], stmp[8];
-      Vec8<T>::from_raw(u, tmp);
-      Vec8<T>::from_raw(su, stmp);
+    const bool first = row < p.split_row;
+    const T* qs = static_cast<const T*>(first ? p.q_scale[0] : p.q_scale[1]) + lane * 4;
+    const T* ks = static_cast<const T*>(first ? p.k_scale[0] : p.k_scale[1]) + lane * 4;
+    T* rbase = static_cast<T*>(p.qkv) + row * p.ld_row + lane * 4;
+    for (int v0 = warp; v0 < nvec; v0 += kRopeWarps * kRopeBatch) {
+      uint2 raw[kRopeBatch];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) { x[j] = tmp[j]; g[j] = stmp[j]; }
+      for (int b = 0; b < kRopeBatch; ++b) {
+        const int v = v0 + b * kRopeWarps;
+        if (v < nvec) raw[b] = *reinterpret_cast<const uint2*>(rbase + ((v & 1) ? p.k_off : p.q_off) + (v >> 1) * 128);
+      }
+#pragma unroll
+      for (int b = 0; b < kRopeBatch; ++b) {
+        const int v = v0 + b * kRopeWarps;
+        if (v < nvec) {
+          rms_rope4<T>(raw[b], (v & 1) ? ks : qs, f0, f1);
+          *reinterpret_cast<uint2*>(rbase + ((v & 1) ? p.k_off : p.q_off) + (v >> 1) * 128) = raw[b];
+        }
+      }
     }
-    float ss = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(x[j], x[j]));
-    const float rrms = rsqrtf(__fadd_rn(__fmul_rn(warp_sum(ss), 1.0f / 128.0f), 1e-6f));
-    float y[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) y[j] = rnd<T>(__fmul_rn(rnd<T>(__fmul_rn(x[j], rrms)), g[j]));
-    // pair 0: (y0, y1) with f0 = {f00, f01, f10, f11}; pair 1: (y2, y3) with f1
-    float o[4];
-    o[0] = rnd<T>(__fadd_rn(__fmul_rn(f0.x, y[0]), __fmul_rn(f0.y, y[1])));
-    o[1] = rnd<T>(__fadd_rn(__fmul_rn(f0.z, y[0]), __fmul_rn(f0.w, y[1])));
-    o[2] = rnd<T>(__fadd_rn(__fmul_rn(f1.x, y[2]), __fmul_rn(f1.y, y[3])));
-    o[3] = rnd<T>(__fadd_rn(__fmul_rn(f1.z, y[2]), __fmul_rn(f1.w, y[3])));
-    uint2 out;
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-      out.x = pack_bf16x2(o[0], o[1]);
-      out.y = pack_bf16x2(o[2], o[3]);
-    } else {
-      out.x = pack_f16x2(o[0], o[1]);
-      out.y = pack_f16x2(o[2], o[3]);
-    }
-    *reinterpret_cast<uint2*>(base) = out;
   }
 }
 

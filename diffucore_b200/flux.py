@@ -422,6 +422,7 @@ class FluxRunner:
         self.sm_scale = self.D ** -0.5
         self._prepare_weights()
         self._allocate()
+        self._pack_modulations()
         self.pe = None
 
     # -- setup ---------------------------------------------------------------------------
@@ -479,6 +480,34 @@ class FluxRunner:
             if lay is not None:
                 self.workspace = torch.empty(lay["total"], device=dev, dtype=torch.uint8)
 
+    def _mod_linears(self) -> list:
+        m = self.model
+        lins = []
+        for blk in m.double_blocks:
+            lins += [blk.img_mod.lin, blk.txt_mod.lin]
+        lins += [blk.modulation.lin for blk in m.single_blocks]
+        lins.append(m.final_layer.adaLN_modulation[1])
+        return lins
+
+    def _pack_modulations(self) -> None:
+        """On CUDA: every block's AdaLN modulation linear (and the final layer's) stacked into one
+        [sum N, hidden] weight, so a forward computes them all in one GEMV over silu(vec) instead of
+        58 small ones (they depend on the timestep and pooled vector only). A copy (~6.5 GB for
+        FLUX.1); the CPU path keeps the per-block linears."""
+        self._mod_w = self._mod_b = None
+        if self.device.type != "cuda":
+            return
+        lins = self._mod_linears()
+        self._mod_w = torch.cat([l.weight.detach() for l in lins]).contiguous()
+        self._mod_b = torch.cat([l.bias.detach() for l in lins]).contiguous()
+        self._mod_sizes = [l.out_features for l in lins]
+
+    def _modulations(self, sv: torch.Tensor) -> list:
+        """Per block (double: img, txt; single; final) the modulation vector lin(silu(vec))."""
+        if self._mod_w is not None:
+            return list(torch.split(F.linear(sv, self._mod_w, self._mod_b)[0], self._mod_sizes))
+        return [lin(sv)[0] for lin in self._mod_linears()]
+
     def set_positions(self, img_ids_: torch.Tensor, txt_ids_: torch.Tensor) -> None:
         """RoPE table for the whole sequence (text ids first), from [1, L*, n_axes] ids."""
         ids = torch.cat([txt_ids_[0], img_ids_[0]], dim=0).to(self.device)
@@ -517,11 +546,11 @@ class FluxRunner:
             self._exchange(self.O_recv, self.O)
 
     # -- blocks --------------------------------------------------------------------------
-    def _double(self, blk: DoubleStreamBlock, w: dict, sv: torch.Tensor) -> None:
+    def _double(self, blk: DoubleStreamBlock, w: dict, img_mod: torch.Tensor, txt_mod: torch.Tensor) -> None:
         ops, X, C, F_, g = self.ops, self.X, self.C, self.F, self.group
         t, i, s = self.t_loc, self.i_loc, self.scales
-        im = blk.img_mod.lin(sv).view(6, C)     # shift1, scale1, gate1, shift2, scale2, gate2
-        tm = blk.txt_mod.lin(sv).view(6, C)
+        im = img_mod.view(6, C)     # shift1, scale1, gate1, shift2, scale2, gate2
+        tm = txt_mod.view(6, C)
         parts = [(0, t, tm, "txt"), (t, i, im, "img")]
         for row0, n, mod, name in parts:
             if n:
@@ -553,9 +582,9 @@ class FluxRunner:
                 xs = X[row0: row0 + n]
                 ops.gemm(self._codes(n, F_, row0), s[row0: row0 + n], w[f"{name}_mlp2"], xs, gate=mod[5], residual=xs)
 
-    def _single(self, blk: SingleStreamBlock, w: dict, sv: torch.Tensor) -> None:
+    def _single(self, blk: SingleStreamBlock, w: dict, modv: torch.Tensor) -> None:
         ops, X, C, F_, g, Lr, s = self.ops, self.X, self.C, self.F, self.group, self.Lr, self.scales
-        mod = blk.modulation.lin(sv).view(3, C)  # shift, scale, gate
+        mod = modv.view(3, C)  # shift, scale, gate
         ops.ln_mod_quant(X, mod[0], mod[1], g, self._codes(Lr, C), s)
         self._qkv_gemm(self._codes(Lr, C), s, w["qkv"], 0)
         ops.gemm(self._codes(Lr, C), s, w["mlp"], self.Cbuf[:, C:], gelu=_lib.GELU_TANH)
@@ -594,12 +623,14 @@ class FluxRunner:
             self.X[:t] = m.txt_in(txt)
         if self.i_loc:
             self.X[t:] = m.img_in(img)
-        for blk, w in zip(m.double_blocks, self.dw):
-            self._double(blk, w, sv)
-        for blk, w in zip(m.single_blocks, self.sw):
-            self._single(blk, w, sv)
+        mods = self._modulations(sv)
+        nd = len(m.double_blocks)
+        for bi, (blk, w) in enumerate(zip(m.double_blocks, self.dw)):
+            self._double(blk, w, mods[2 * bi], mods[2 * bi + 1])
+        for bi, (blk, w) in enumerate(zip(m.single_blocks, self.sw)):
+            self._single(blk, w, mods[2 * nd + bi])
         fl = m.final_layer
-        shift, scale = fl.adaLN_modulation(vec).chunk(2, dim=-1)
+        shift, scale = mods[-1].view(1, -1).chunk(2, dim=-1)
         xi = self.X[t:]
         h = (1 + scale) * F.layer_norm(xi, (C,), eps=1e-6) + shift
         return fl.linear(h)
