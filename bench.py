@@ -583,6 +583,8 @@ def main() -> int:
     ap.add_argument("--only", default="all", choices=("all", "gemm", "flux", "glue", "sdxl"),
                     help="gemm / flux: time only the config-1 W8A8 linear / the FLUX DiT")
     ap.add_argument("--no-flux", action="store_true", help="skip the FLUX DiT timing")
+    ap.add_argument("--clocks-csv-dir", default=None,
+                    help="also write the raw nvidia-smi clock samples of the timed region to this folder")
     ap.add_argument("--op-breakdown", action="store_true",
                     help="with --only flux: GPU time per runner op of one 1024^2 forward (CUDA events)")
     args = ap.parse_args()
@@ -623,8 +625,7 @@ def main() -> int:
         sets.append((q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)))   # (B, L, H, D) views of bhld
     out = torch.empty(B, S, H, D, device=dev, dtype=torch.bfloat16)
     plan = kernels.AttnPlan(B, H, S, S, D, torch.bfloat16, _lib.MODE_BLOCK64, dev)
-    sampler = ClockSampler(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv"
-                           if (ROOT / "gpurun_out").is_dir() else None)
+    sampler = ClockSampler(local, Path(args.clocks_csv_dir) / f"clocks_rank{rank}.csv" if args.clocks_csv_dir else None)
     t = bench_attention(args, world, _lib.MODE_BLOCK64, sets, plan, out, sampler)
     total_s = _max_over_ranks(t["total_ms"] * 1e-3, world)
     value = world * ATTN_OPS * args.steps / total_s / 1e12
