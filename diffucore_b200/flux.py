@@ -34,7 +34,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib, kernels
-from ._int8 import GROUP, Int8Linear, quantize_linears
+from ._int8 import GROUP, Int8Linear, adopt_int8_layers, int8_layers, quantize_linears
 
 
 @dataclass
@@ -269,6 +269,21 @@ def init_random_(model: nn.Module, seed: int = 0, device=None, std: float = 0.02
             vals = std * vals
         p.data = vals.to(device=p.device if p.device.type != "meta" else gen_dev, dtype=dtype)
     return model
+
+
+def from_state_dict(state_dict: dict, config: FluxConfig | None = None, device="cuda") -> Flux:
+    """A ``Flux`` loaded from a FLUX.1 transformer state dict, plain or a ComfyUI ``int8_tensorwise``
+    checkpoint: built on the meta device, every ``comfy_quant``-tagged linear adopted as an
+    :class:`Int8Linear` (its ``weight_scale`` becomes ``scale_bits``), then a strict load, the
+    reference loader's sequence (src/diffucore/bundle.py:301-305 for its DiTs)."""
+    with torch.device("meta"):
+        model = Flux(config)
+    sd = dict(state_dict)
+    layers = int8_layers(sd)
+    if layers:
+        sd = adopt_int8_layers(model, sd, layers)
+    model.load_state_dict(sd, strict=True, assign=True)
+    return model.to(device).eval()
 
 
 def build_flux(cfg: FluxConfig | None = None, seed: int = 0, device="cuda", group: int = GROUP,

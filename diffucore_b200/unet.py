@@ -27,7 +27,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _attention
-from ._int8 import Int8Linear, quantize_activation, quantize_linears
+from ._int8 import Int8Linear, adopt_int8_layers, int8_layers, quantize_activation, quantize_linears
 
 
 @dataclass
@@ -307,6 +307,20 @@ def init_random_(model: nn.Module, seed: int = 0, device=None, dtype: torch.dtyp
             vals = vals / math.sqrt(fan_in)
         p.data = vals.to(device=p.device if p.device.type != "meta" else gen_dev, dtype=dtype)
     return model
+
+
+def from_state_dict(state_dict: dict, config: UNetConfig | None = None, device="cuda") -> UNetModel:
+    """A ``UNetModel`` loaded from a UNet state dict, plain or a ComfyUI ``int8_tensorwise``
+    checkpoint (tagged linears adopted as :class:`Int8Linear`), then a strict load; see
+    :func:`diffucore_b200.flux.from_state_dict`."""
+    with torch.device("meta"):
+        model = UNetModel(config or sdxl_unet_config())
+    sd = dict(state_dict)
+    layers = int8_layers(sd)
+    if layers:
+        sd = adopt_int8_layers(model, sd, layers)
+    model.load_state_dict(sd, strict=True, assign=True)
+    return model.to(device).eval()
 
 
 def build_sdxl_unet(cfg: UNetConfig | None = None, seed: int = 0, device="cuda", init_device=None,
