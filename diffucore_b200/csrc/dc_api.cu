@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -264,12 +265,46 @@ struct GemmEpi {
   int64_t block_stride = 0;
 };
 
-template <int BN, int OUT, bool HAS_BIAS, int GELU, bool GATED>
+// Pair tiles (256 x 256 over a cluster of two CTAs, see gemm.cuh) are opt-in through
+// DC_GEMM_PAIR=1 and need more than one 128-row block of activations.
+bool use_pair_gemm(int64_t M) {
+  const char* env = getenv("DC_GEMM_PAIR");
+  return env != nullptr && strcmp(env, "1") == 0 && M > dc::kGemmBM;
+}
+
+// Largest number of two-CTA clusters of `kernel` resident at once on the current device.
+template <typename Kern>
+int max_pair_clusters(Kern kernel, int smem_bytes, int* clusters) {
+  static std::atomic<int> cache[64];                 // per device ordinal; 0 = not computed
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && cache[dev].load() > 0) { *clusters = cache[dev].load(); return DC_OK; }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * static_cast<unsigned>(sm_count()));
+  cfg.blockDim = dim3(dc::kGemmThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+  if (n <= 0) return fail("gemm: no two-CTA cluster of the pair kernel fits on this device");
+  if (dev >= 0 && dev < 64) cache[dev].store(n);
+  *clusters = n;
+  return DC_OK;
+}
+
+template <int BN, int OUT, bool HAS_BIAS, int GELU, bool GATED, bool PAIR = false>
 int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
                 const void* bias, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K, const GemmEpi& epi,
                 cudaStream_t st) {
-  constexpr int STAGES = BN == 256 ? 4 : 6;
-  using S = dc::GemmSmem<BN, STAGES>;
+  constexpr int STAGES = PAIR ? 6 : (BN == 256 ? 4 : 6);
+  constexpr int kTileM = PAIR ? 2 * dc::kGemmBM : dc::kGemmBM;
+  constexpr int kBoxB = PAIR ? BN / 2 : BN;          // B rows one CTA loads per k-block
+  using S = dc::GemmSmem<kBoxB, STAGES>;
   CUtensorMap ta, tb;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
@@ -281,52 +316,80 @@ int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, cons
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
     const uint64_t strides[1] = {static_cast<uint64_t>(ldw)};
-    const uint32_t box[2] = {dc::kGemmBK, static_cast<uint32_t>(BN)};
+    const uint32_t box[2] = {dc::kGemmBK, static_cast<uint32_t>(kBoxB)};
     int r = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (r) return r;
   }
   dc::GemmParams p;
   p.M = static_cast<int>(M); p.N = static_cast<int>(N); p.K = static_cast<int>(K);
-  p.tiles_m = static_cast<int>((M + dc::kGemmBM - 1) / dc::kGemmBM);
+  p.tiles_m = static_cast<int>((M + kTileM - 1) / kTileM);
   p.tiles_n = static_cast<int>((N + BN - 1) / BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.num_kb = static_cast<int>((K + dc::kGemmBK - 1) / dc::kGemmBK);
   p.sx = sx; p.sw = sw; p.bias = bias; p.out = out; p.ldo = ldo;
   p.gate = epi.gate; p.residual = epi.residual; p.ldr = epi.ldr;
   p.col_block = epi.col_block; p.block_stride = epi.block_stride;
-  auto kernel = dc::gemm_w8a8_kernel<BN, STAGES, OUT, HAS_BIAS, GELU, GATED>;
+  auto kernel = dc::gemm_w8a8_kernel<BN, STAGES, OUT, HAS_BIAS, GELU, GATED, PAIR>;
   int r = set_smem(kernel, S::kDynamic);
   if (r) return r;
-  const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
-  kernel<<<grid, dc::kGemmThreads, S::kDynamic, st>>>(ta, tb, p);
+  if constexpr (PAIR) {
+    int clusters = 0;
+    if ((r = max_pair_clusters(kernel, S::kDynamic, &clusters))) return r;
+    const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * static_cast<unsigned>(pairs));
+    cfg.blockDim = dim3(dc::kGemmThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(S::kDynamic);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, p);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_w8a8 pair launch");
+  } else {
+    const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
+    kernel<<<grid, dc::kGemmThreads, S::kDynamic, st>>>(ta, tb, p);
+  }
   DC_CHECK_LAUNCH("gemm_w8a8 launch");
   return DC_OK;
 }
 
-template <int BN, int OUT>
+template <int BN, int OUT, bool PAIR>
 int dispatch_gemm_epilogue(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx,
                            const float* sw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
                            int64_t K, int gelu, const GemmEpi& epi, cudaStream_t st) {
   if constexpr (OUT == dc::kOutI32) {
-    return launch_gemm<BN, OUT, false, 0, false>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, epi, st);
+    return launch_gemm<BN, OUT, false, 0, false, PAIR>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, epi, st);
   } else {
     const bool b = bias != nullptr;
     if (epi.residual != nullptr) {
-      return b ? launch_gemm<BN, OUT, true, 0, true>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
-               : launch_gemm<BN, OUT, false, 0, true>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
+      return b ? launch_gemm<BN, OUT, true, 0, true, PAIR>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
+               : launch_gemm<BN, OUT, false, 0, true, PAIR>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
     }
     switch (gelu) {
       case DC_GELU_NONE:
-        return b ? launch_gemm<BN, OUT, true, 0, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
-                 : launch_gemm<BN, OUT, false, 0, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
+        return b ? launch_gemm<BN, OUT, true, 0, false, PAIR>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
+                 : launch_gemm<BN, OUT, false, 0, false, PAIR>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
       case DC_GELU_ERF:
-        return b ? launch_gemm<BN, OUT, true, 1, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
-                 : launch_gemm<BN, OUT, false, 1, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
+        return b ? launch_gemm<BN, OUT, true, 1, false, PAIR>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
+                 : launch_gemm<BN, OUT, false, 1, false, PAIR>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
       default:
-        return b ? launch_gemm<BN, OUT, true, 2, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
-                 : launch_gemm<BN, OUT, false, 2, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
+        return b ? launch_gemm<BN, OUT, true, 2, false, PAIR>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st)
+                 : launch_gemm<BN, OUT, false, 2, false, PAIR>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, epi, st);
     }
   }
+}
+
+// 128 x 256 tiles on one SM, or 256 x 256 tiles on a CTA pair.
+template <int OUT>
+int dispatch_gemm_wide(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx,
+                       const float* sw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
+                       int64_t K, int gelu, const GemmEpi& epi, cudaStream_t st) {
+  if (use_pair_gemm(M))
+    return dispatch_gemm_epilogue<256, OUT, true>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st);
+  return dispatch_gemm_epilogue<256, OUT, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st);
 }
 
 int gemm_checked(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
@@ -359,14 +422,14 @@ int gemm_checked(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, con
   if (int r = check_sm100()) return r;
   switch (out_dtype) {
     case DC_DTYPE_BF16:
-      return wide ? dispatch_gemm_epilogue<256, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st)
-                  : dispatch_gemm_epilogue<128, dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st);
+      return wide ? dispatch_gemm_wide<dc::kOutBF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st)
+                  : dispatch_gemm_epilogue<128, dc::kOutBF16, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st);
     case DC_DTYPE_F16:
-      return wide ? dispatch_gemm_epilogue<256, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st)
-                  : dispatch_gemm_epilogue<128, dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st);
+      return wide ? dispatch_gemm_wide<dc::kOutF16>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st)
+                  : dispatch_gemm_epilogue<128, dc::kOutF16, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st);
     case DC_DTYPE_I32:
-      return wide ? dispatch_gemm_epilogue<256, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, epi, st)
-                  : dispatch_gemm_epilogue<128, dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, epi, st);
+      return wide ? dispatch_gemm_wide<dc::kOutI32>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, epi, st)
+                  : dispatch_gemm_epilogue<128, dc::kOutI32, false>(q, ldq, w, ldw, sx, sw, nullptr, out, ldo, M, N, K, 0, epi, st);
     default: return fail("gemm: unsupported output dtype %d", out_dtype);
   }
 }

@@ -7,6 +7,15 @@
 // Accumulators live in TMEM, double-buffered (2 x BN columns) so the epilogue of one tile
 // overlaps the main loop of the next.
 //
+// PAIR runs the same roles in a cluster of two CTAs on one TPC with 256 x BN tiles: each CTA
+// stages its 128 rows of A and half (BN/2 rows) of B per k-block, the even CTA's MMA thread issues
+// `cta_group::2` MMAs that read both CTAs' shared memory and write each CTA's 128 accumulator rows
+// into that CTA's TMEM, and each CTA's epilogue drains its own rows. Per SM that halves the B bytes
+// TMA writes and the tensor core reads per k-block (32 KB instead of 48 KB per 128 x 256 x 128),
+// the shared-memory traffic that limits the one-CTA tile. Barriers: both CTAs' loads of a stage
+// count on the even CTA's `full_bar`; its MMA commits arrive on both CTAs' `empty_bar` and
+// `acc_full`; both CTAs' epilogue warps arrive on the even CTA's `acc_empty`.
+//
 // The epilogue rounds exactly like the reference's `rescale` (src/diffucore/models/_int8.py:313-323):
 //   y = dtype(float(acc) * (sx[m] * sw[n]));  if bias: y = dtype(float(y) + float(bias[n]))
 // and with OUT_I32 it writes the raw accumulator (the reference's `int_mm`, _int8.py:200-207).
@@ -98,12 +107,13 @@ __device__ __forceinline__ float gated_residual(uint32_t res_bits, float gate, f
   return out_round<OUT>(__fadd_rn(rv, out_round<OUT>(__fmul_rn(gate, y))));
 }
 
-template <int BN, int STAGES, int OUT, bool HAS_BIAS, int GELU, bool GATED = false>
+template <int BN, int STAGES, int OUT, bool HAS_BIAS, int GELU, bool GATED = false, bool PAIR = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                  const GemmParams p) {
-  using S = GemmSmem<BN, STAGES>;
+  using S = GemmSmem<PAIR ? BN / 2 : BN, STAGES>;  // B rows staged by this CTA
   constexpr int kHalf = BN / 2;                 // columns per epilogue warp
+  constexpr int kTileM = PAIR ? 2 * kGemmBM : kGemmBM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -119,18 +129,28 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
   __shared__ int abort_flag;
 
   const int warp = warp_id(), lane = lane_id();
+  // PAIR: rank in the pair, the pair's index among all pairs, and the number of pairs.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 32 * kGemmEpiWarps); }
+    // PAIR: one arrival per epilogue warp of both CTAs, on the even CTA's barrier
+    const uint32_t acc_empty_count = PAIR ? 2 * kGemmEpiWarps : 32 * kGemmEpiWarps;
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], acc_empty_count); }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) { tma_prefetch_desc(&tma_a); tma_prefetch_desc(&tma_b); }
-  if (warp == 1) { tmem_alloc(&tmem_base_slot, 2 * BN); tmem_relinquish(); }
+  if (warp == 1) {
+    if constexpr (PAIR) { tmem_alloc_pair(&tmem_base_slot, 2 * BN); tmem_relinquish_pair(); }
+    else { tmem_alloc(&tmem_base_slot, 2 * BN); tmem_relinquish(); }
+  }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_slot;
   volatile int* abort = &abort_flag;
@@ -141,15 +161,23 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (int tile = unit; tile < p.num_tiles && ok; tile += units) {
         const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort)) { ok = false; break; }
           uint8_t* sa = smem + stage * S::kStage;
           uint8_t* sb = sa + S::kA;
-          mbar_arrive_expect_tx(&full_bar[stage], S::kStage);
-          tma_load_2d(sa, &tma_a, &full_bar[stage], kb * kGemmBK, tm * kGemmBM);
-          tma_load_2d(sb, &tma_b, &full_bar[stage], kb * kGemmBK, tn * BN);
+          if constexpr (PAIR) {
+            // both CTAs' halves count on the even CTA's barrier, which expects both
+            const uint32_t bar = cluster_addr(&full_bar[stage], 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * S::kStage);
+            tma_load_2d_pair(sa, &tma_a, bar, kb * kGemmBK, tm * kTileM + static_cast<int>(rank) * kGemmBM);
+            tma_load_2d_pair(sb, &tma_b, bar, kb * kGemmBK, tn * BN + static_cast<int>(rank) * (BN / 2));
+          } else {
+            mbar_arrive_expect_tx(&full_bar[stage], S::kStage);
+            tma_load_2d(sa, &tma_a, &full_bar[stage], kb * kGemmBK, tm * kGemmBM);
+            tma_load_2d(sb, &tma_b, &full_bar[stage], kb * kGemmBK, tn * BN);
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -161,16 +189,18 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (lane 0)
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(kGemmBM, BN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_i8(kTileM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int tile = unit; tile < p.num_tiles && ok; tile += units, ++local) {
         const int buf = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort)) { ok = false; break; }
+        const bool drained = PAIR ? mbar_wait_cluster(&acc_empty[buf], acc_phase ^ 1, abort)
+                                  : mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort);
+        if (!drained) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kb = 0; kb < p.num_kb; ++kb) {
@@ -182,15 +212,26 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
           for (int k = 0; k < kGemmBK / 32; ++k) {
             const uint64_t ad = smem_desc(sa + k * 32, 16, 1024);
             const uint64_t bd = smem_desc(sb + k * 32, 16, 1024);
-            mma_i8_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            if constexpr (PAIR) mma_i8_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            else mma_i8_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          mma_commit(&empty_bar[stage]);
-          if (kb == p.num_kb - 1) mma_commit(&acc_full[buf]);
+          if constexpr (PAIR) {
+            mma_commit_pair(smem_u32(&empty_bar[stage]));
+            mma_commit_pair(cluster_addr(&empty_bar[stage], 1));
+            if (kb == p.num_kb - 1) {
+              mma_commit_pair(smem_u32(&acc_full[buf]));
+              mma_commit_pair(cluster_addr(&acc_full[buf], 1));
+            }
+          } else {
+            mma_commit(&empty_bar[stage]);
+            if (kb == p.num_kb - 1) mma_commit(&acc_full[buf]);
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
       // Every MMA issued above has completed once this commit lands.
-      mma_commit(&drain_bar);
+      if constexpr (PAIR) mma_commit_pair(smem_u32(&drain_bar));
+      else mma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, nullptr, 1000000);
     }
     __syncwarp();
@@ -204,7 +245,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     float* my_bias = col_bias[ew];
     float* my_gate = col_gate[GATED ? ew : 0];
     int local = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = unit; tile < p.num_tiles; tile += units, ++local) {
       const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
@@ -223,7 +264,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       bool ok = mbar_wait(&acc_full[buf], acc_phase, abort);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int row = tm * kGemmBM + row_in_tile;
+      const int row = tm * kTileM + static_cast<int>(rank) * kGemmBM + row_in_tile;
       const bool row_ok = row < p.M;
       const float sxr = (OUT != kOutI32 && row_ok) ? p.sx[row] : 0.0f;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + half * kHalf;
@@ -305,15 +346,22 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
+      if constexpr (PAIR) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(cluster_addr(&acc_empty[buf], 0));
+      } else {
+        mbar_arrive(&acc_empty[buf]);
+      }
     }
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * BN);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, 2 * BN);
+    else tmem_dealloc(tmem_base, 2 * BN);
   }
 }
 

@@ -260,6 +260,102 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool b
        | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// ----------------------------------------------------------------------------- CTA pairs
+// A cluster of two CTAs on the two SMs of a TPC can run one tcgen05.mma of M = 256
+// (`cta_group::2`): each CTA stages half of A (its 128 rows) and half of B in its own shared
+// memory at the same offsets, and holds its 128 rows of the accumulator in its own TMEM at the
+// same columns. One thread of the even CTA issues the MMAs for both.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// Every thread of every CTA in the cluster. Orders the barrier initialisations and TMEM
+// allocation of each CTA before the other's first remote access, and keeps both CTAs alive until
+// neither reads the other's shared memory any more.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier of another CTA in the cluster (`addr` from cluster_addr).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u) : "memory");
+  return ok != 0;
+}
+
+// mbar_wait for a barrier that other CTAs of the cluster arrive on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                  long long limit = kWaitCycleLimit) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (abort != nullptr && *abort) return false;
+    if (clock64() - t0 > limit) {
+      record_error(kErrWaitTimeout);
+      if (abort != nullptr) *abort = 1;
+      return false;
+    }
+  }
+}
+
+// TMA tile load into this CTA's shared memory whose completion is counted on an mbarrier that may
+// sit in either CTA of the pair (`bar_addr` from cluster_addr): both CTAs' loads of a stage count
+// on the even CTA's barrier, which its MMA thread waits on.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* desc, uint32_t bar_addr, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar_addr), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// TMEM allocation for both CTAs of the pair: one warp with the same warp index in each CTA.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+               :: "r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+// D (+)= A . B over the pair: M = 256 rows, each CTA's shared memory supplying its half of A and
+// of B at the descriptors' offsets; no "memory" clobber, as for mma_i8_ss.
+__device__ __forceinline__ void mma_i8_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive once on the mbarrier at `bar_addr` (this CTA's or the peer's) when every pair MMA issued
+// so far by this thread has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(bar_addr) : "memory");
+}
+
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
