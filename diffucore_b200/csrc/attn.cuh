@@ -298,7 +298,10 @@ __device__ __forceinline__ float scaled_max(int mx, float c) {
   return mx == INT_MIN ? -INFINITY : __fmul_rn(static_cast<float>(mx), c);
 }
 
-template <int D, bool BF16>
+// DYN: the MMA thread issues each Q tile's next group (P.V half, then the next Q.K^T) as soon as
+// its inputs are ready, polling the barriers of both tiles, instead of the fixed order tile 0 then
+// tile 1; the order within a tile, and so every result, is the same.
+template <int D, bool BF16, bool DYN = false>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
                  const __grid_constant__ CUtensorMap tma_v, const AttnParams p) {
@@ -412,7 +415,65 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
         issue_s(0, 0); mma_commit(&s_ready[0]);
         issue_s(1, 0); mma_commit(&s_ready[1]);
       }
-      for (int j = 0; j < n && ok; ++j) {
+      if constexpr (DYN) {
+        // Per tile: the step and key half of its next P.V, and whether its next Q.K^T is due.
+        // A stage is released once both tiles issued the second-half P.V of its step; until then
+        // neither tile can reach that stage's next use, so every parity tested below is the one
+        // of the phase in question.
+        int js[2] = {0, 0}, hs[2] = {0, 0};
+        bool s_due[2] = {false, false};
+        uint32_t released = 0;          // 2 bits per stage: tiles done with its current step
+        long long idle_since = clock64();
+        while (ok && (js[0] < n || js[1] < n)) {
+          bool progressed = false;
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int j = js[i];
+            const int st = j % kAttnStages;
+            const uint32_t ph = (j / kAttnStages) & 1;
+            if (s_due[i]) {
+              if (mbar_test(&k_full[st], ph)) {
+                tc_fence_after();
+                issue_s(i, st);
+                mma_commit(&s_ready[i]);
+                s_due[i] = false;
+                progressed = true;
+              }
+            } else if (j < n) {
+              const int hh = hs[i];
+              if (mbar_test(&p_ready[i][hh], j & 1) && mbar_test(&v_full[st], ph)) {
+                tc_fence_after();
+                issue_pv(i, hh, st, j > 0 || hh > 0);
+                mma_commit(&pv_done[i][hh]);
+                if (hh == 0) {
+                  hs[i] = 1;
+                } else {
+                  if (((released >> (2 * st)) & 3u) == 1u) {
+                    mma_commit(&kv_empty[st]);
+                    released &= ~(3u << (2 * st));
+                  } else {
+                    released += 1u << (2 * st);
+                  }
+                  hs[i] = 0;
+                  js[i] = j + 1;
+                  s_due[i] = j + 1 < n;
+                }
+                progressed = true;
+              }
+            }
+          }
+          if (progressed) {
+            idle_since = clock64();
+          } else if (*abort) {
+            ok = false;
+          } else if (clock64() - idle_since > kWaitCycleLimit) {
+            record_error(kErrWaitTimeout);
+            *abort = 1;
+            ok = false;
+          }
+        }
+      }
+      for (int j = 0; j < n && ok && !DYN; ++j) {
         const int st = j % kAttnStages;
         const uint32_t ph = (j / kAttnStages) & 1;
         const int st1 = (j + 1) % kAttnStages;

@@ -578,7 +578,9 @@ int attn_main(const void* v, int64_t B, int64_t H, int64_t Lq, int64_t Lk, const
     dim3 grid(static_cast<unsigned>(a.Lq_pad / dc::kDbRows), static_cast<unsigned>(H), static_cast<unsigned>(B));
     kernel<<<grid, dc::kAttnThreads, SD::kDynamic, st>>>(tq, tk, tv, p);
   } else {
-    auto kernel = dc::attn_int8_kernel<D, BF16>;
+    const char* issue = getenv("DC_ATTN_ISSUE");
+    auto kernel = issue != nullptr && strcmp(issue, "dynamic") == 0 ? dc::attn_int8_kernel<D, BF16, true>
+                                                                     : dc::attn_int8_kernel<D, BF16, false>;
     int r = set_smem(kernel, SM::kDynamic);
     if (r) return r;
     dim3 grid(static_cast<unsigned>(a.Lq_pad / dc::kAttnRows), static_cast<unsigned>(H), static_cast<unsigned>(B));
