@@ -329,6 +329,13 @@ int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, cons
   p.sx = sx; p.sw = sw; p.bias = bias; p.out = out; p.ldo = ldo;
   p.gate = epi.gate; p.residual = epi.residual; p.ldr = epi.ldr;
   p.col_block = epi.col_block; p.block_stride = epi.block_stride;
+  // Vector (16-byte) stores and residual loads only where every such address is 16-byte aligned:
+  // the tile's columns start at multiples of 32 elements, so the base and the row strides decide.
+  const int64_t row_elems = OUT == dc::kOutI32 ? 4 : 8;          // elements per 16 bytes
+  p.out_vec = reinterpret_cast<uintptr_t>(out) % 16 == 0 && ldo % row_elems == 0 &&
+              epi.block_stride % row_elems == 0;
+  p.res_vec = epi.residual != nullptr && reinterpret_cast<uintptr_t>(epi.residual) % 16 == 0 &&
+              epi.ldr % 8 == 0;
   auto kernel = dc::gemm_w8a8_kernel<BN, STAGES, OUT, HAS_BIAS, GELU, GATED, PAIR>;
   int r = set_smem(kernel, S::kDynamic);
   if (r) return r;
@@ -405,6 +412,13 @@ int gemm_checked(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, con
   if (out_dtype != DC_DTYPE_I32 && (sx == nullptr || sw == nullptr)) return fail("gemm: scales are required");
   if (out_dtype == DC_DTYPE_I32 && (bias != nullptr || gelu)) return fail("gemm: int32 output takes no bias or gelu");
   if ((epi.gate == nullptr) != (epi.residual == nullptr)) return fail("gemm: gate and residual go together");
+  {
+    const uintptr_t elem = out_dtype == DC_DTYPE_I32 ? 4 : 2;      // element-aligned pointers
+    if (reinterpret_cast<uintptr_t>(out) % elem || reinterpret_cast<uintptr_t>(bias) % 2 ||
+        reinterpret_cast<uintptr_t>(epi.gate) % 2 || reinterpret_cast<uintptr_t>(epi.residual) % 2 ||
+        reinterpret_cast<uintptr_t>(sx) % 4 || reinterpret_cast<uintptr_t>(sw) % 4)
+      return fail("gemm: out, bias, gate, residual and scales must be aligned to their element size");
+  }
   if (epi.residual != nullptr) {
     if (out_dtype == DC_DTYPE_I32) return fail("gemm: a gated residual needs a 16-bit output");
     if (gelu) return fail("gemm: a gated residual takes no gelu");
@@ -752,6 +766,10 @@ int dc_qk_norm_rope(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64
     return fail("qk_norm_rope: rows and offsets must be 8-byte aligned");
   if (q_scale0 == nullptr || k_scale0 == nullptr || pe == nullptr) return fail("qk_norm_rope: scales and pe are required");
   if (split_row < L && (q_scale1 == nullptr || k_scale1 == nullptr)) return fail("qk_norm_rope: second scales missing");
+  // scales are read 4 elements (8 bytes) per lane, pe 8 floats (two 16-byte loads) per lane
+  for (const void* sp : {q_scale0, k_scale0, q_scale1, k_scale1})
+    if (reinterpret_cast<uintptr_t>(sp) % 8) return fail("qk_norm_rope: scale vectors must be 8-byte aligned");
+  if (reinterpret_cast<uintptr_t>(pe) % 16) return fail("qk_norm_rope: pe must be 16-byte aligned");
   if (pe_row0 < 0) return fail("qk_norm_rope: pe_row0 < 0");
   if (int r = check_sm100()) return r;
   dc::QkNormRopeParams p;

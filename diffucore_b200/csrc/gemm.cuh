@@ -53,6 +53,8 @@ struct GemmParams {
   int64_t ldr;
   int64_t col_block;     // 0: plain [M, N] output; else a multiple of BN (see above)
   int64_t block_stride;  // elements between column blocks
+  int out_vec;           // 16-byte stores allowed: out 16-byte aligned, ldo and block_stride rows of 16 B
+  int res_vec;           // 16-byte residual loads allowed: residual 16-byte aligned, ldr rows of 16 B
 };
 
 template <int BN, int STAGES>
@@ -285,7 +287,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         if (!row_ok || col0 >= p.N) continue;
         if (OUT == kOutI32) {
           int32_t* dst = reinterpret_cast<int32_t*>(p.out) + out_off + (col0 - col_base);
-          if (col0 + 32 <= p.N && (p.ldo & 3) == 0) {
+          if (col0 + 32 <= p.N && p.out_vec) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
               *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
@@ -300,7 +302,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
           uint32_t res[16];
           if (GATED) {
             const uint16_t* rp = reinterpret_cast<const uint16_t*>(p.residual) + static_cast<int64_t>(row) * p.ldr + col0;
-            if (col0 + 32 <= p.N && (p.ldr & 7) == 0) {
+            if (col0 + 32 <= p.N && p.res_vec) {
 #pragma unroll
               for (int j = 0; j < 16; j += 4) {
                 const uint4 u = *reinterpret_cast<const uint4*>(rp + 2 * j);
@@ -334,7 +336,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
             w[j / 2] = OUT == kOutBF16 ? pack_bf16x2(y0, y1) : pack_f16x2(y0, y1);
             w[j / 2 + 1] = OUT == kOutBF16 ? pack_bf16x2(y2, y3) : pack_f16x2(y2, y3);
           }
-          if (col0 + 32 <= p.N && (p.ldo & 7) == 0) {
+          if (col0 + 32 <= p.N && p.out_vec) {
 #pragma unroll
             for (int j = 0; j < 16; j += 4)
               *reinterpret_cast<uint4*>(dst + 2 * j) = make_uint4(w[j], w[j + 1], w[j + 2], w[j + 3]);

@@ -194,6 +194,11 @@ def qk_norm_rope(qkv: torch.Tensor, q_scale0: torch.Tensor, k_scale0: torch.Tens
         raise ValueError("qk_norm_rope expects rows laid out as [3, H, D]")
     if split_row is None:
         split_row = L
+    for sc in (q_scale0, k_scale0, q_scale1, k_scale1):
+        if sc is not None and (sc.dtype != qkv.dtype or sc.numel() != D or not sc.is_contiguous()):
+            raise ValueError(f"qk_norm_rope: scales must be contiguous [{D}] tensors in {qkv.dtype}")
+    if pe.dtype != torch.float32 or not pe.is_contiguous() or pe.numel() < L * D * 2:
+        raise ValueError(f"qk_norm_rope: pe must be a contiguous fp32 table of at least [{L}, {D // 2}, 2, 2]")
     lib = _lib.load()
     _lib.check(lib.dc_qk_norm_rope(_ptr(qkv), _DTYPE[qkv.dtype], L, H, D, qkv.stride(0), 0, H * D, _ptr(q_scale0),
                                    _ptr(k_scale0), _ptr(q_scale1), _ptr(k_scale1), int(split_row), _ptr(pe), 0,

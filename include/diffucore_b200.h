@@ -81,7 +81,9 @@ int dc_gemm_w8a8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, con
  *      out + (n / col_block) * block_stride + m * ldo + n % col_block
  *    i.e. the output is laid out as [N / col_block, M, col_block] blocks, the send layout of an
  *    all-to-all that gives each destination its contiguous block. col_block = 0: plain [M, N]
- *    with row stride ldo (then block_stride must be 0). */
+ *    with row stride ldo (then block_stride must be 0).
+ * Any out / residual alignment is accepted: stores and residual loads are 16 bytes wide where the
+ * base pointer is 16-byte aligned and the row strides keep it so, element-wise otherwise. */
 int dc_gemm_w8a8_ex(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
                     const void* bias, int gelu, const void* gate, const void* residual, int64_t ldr, void* out,
                     int64_t ldo, int64_t col_block, int64_t block_stride, int out_dtype, int64_t M, int64_t N,
@@ -115,7 +117,8 @@ int dc_ln_mod_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld
  *   (y0, y1) of rotary pair i -> dtype(f[i][0][0] y0 + f[i][0][1] y1), dtype(f[i][1][0] y0 + f[i][1][1] y1)
  * with pe fp32 [rows, D/2, 2, 2] (row r uses pe row pe_row0 + r). Rows r < split_row use
  * (q_scale0, k_scale0), the others (q_scale1, k_scale1): the text and image streams of a joint
- * double-stream attention. */
+ * double-stream attention. qkv 8-byte aligned with ld_row, q_off, k_off multiples of 4 elements;
+ * scale vectors (D elements of dtype) 8-byte aligned; pe 16-byte aligned. */
 int dc_qk_norm_rope(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64_t ld_row, int64_t q_off,
                     int64_t k_off, const void* q_scale0, const void* k_scale0, const void* q_scale1,
                     const void* k_scale1, int64_t split_row, const float* pe, int64_t pe_row0, void* stream);

@@ -53,6 +53,25 @@ def test_gemm_gated_residual_in_place_bit_exact(M, N, K):
     assert torch.equal(out, want)
 
 
+@pytest.mark.parametrize("offset", [1, 3, 8])
+def test_gemm_output_and_residual_at_any_alignment(offset):
+    """out / residual views starting `offset` elements past a 16-byte boundary: the epilogue
+    falls back to element-wise stores and loads where 16-byte ones would be misaligned."""
+    g = torch.Generator().manual_seed(offset)
+    M, N, K = 300, 640, 512
+    q, w, sx, sw, bias = _rand_gemm(M, N, K, g)
+    want = kernels.gemm_w8a8(q, w, sx, sw, bias, torch.bfloat16)
+    buf = torch.zeros(M * N + 16, device=DEV, dtype=torch.bfloat16)
+    out = buf[offset: offset + M * N].view(M, N)
+    kernels.gemm_w8a8_into(q, w, sx, sw, bias, out)
+    assert torch.equal(out, want)
+    gate = (torch.randn(N, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16).to(DEV)
+    out.copy_(res)
+    kernels.gemm_w8a8_into(q, w, sx, sw, bias, out, gate=gate, residual=out)
+    assert torch.equal(out, res + gate * want)
+
+
 @pytest.mark.parametrize("P", [2, 4, 8])
 def test_gemm_column_block_layout_bit_exact(P):
     """The qkv projection of 8 heads x 128 written as P per-rank blocks [P, M, 3 * 8/P * 128]."""
