@@ -409,6 +409,7 @@ int gemm_checked(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, con
   if (ldq < K || ldw < K) return fail("gemm: leading dimension smaller than the row");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail("gemm: dimension above 2^31");
   if (gelu < 0 || gelu > 2) return fail("unknown gelu mode %d", gelu);
+  if (q == nullptr || w == nullptr || out == nullptr) return fail("gemm: null operand or output");
   if (out_dtype != DC_DTYPE_I32 && (sx == nullptr || sw == nullptr)) return fail("gemm: scales are required");
   if (out_dtype == DC_DTYPE_I32 && (bias != nullptr || gelu)) return fail("gemm: int32 output takes no bias or gelu");
   if ((epi.gate == nullptr) != (epi.residual == nullptr)) return fail("gemm: gate and residual go together");
@@ -488,6 +489,7 @@ int check_attn_args(int dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk, int
 }
 
 int check_strides(const void* ptr, const int64_t* s, const char* name) {
+  if (ptr == nullptr || s == nullptr) return fail("%s or its strides is null", name);
   if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return fail("%s must be 16-byte aligned", name);
   for (int i = 0; i < 3; ++i)
     if (s[i] % 8 != 0 || s[i] < 0) return fail("%s strides must be non-negative multiples of 8 elements", name);
@@ -663,6 +665,9 @@ int dc_quant_rows(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
   if (group && K % 256) return fail("K=%lld is not a multiple of the ConvRot group 256", (long long)K);
   if (ldx < K) return fail("ldx < K");
   if (gelu < 0 || gelu > 2) return fail("unknown gelu mode %d", gelu);
+  if (x == nullptr || q == nullptr || s == nullptr) return fail("quant_rows: null pointer");
+  if (reinterpret_cast<uintptr_t>(x) % (x_dtype == DC_DTYPE_F32 ? 4 : 2) || reinterpret_cast<uintptr_t>(s) % 4)
+    return fail("quant_rows: x and s must be aligned to their element size");
   if (int r = check_sm100()) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (x_dtype) {
@@ -699,6 +704,8 @@ int dc_quant_rows_seg(const void* x, int x_dtype, int64_t M, int64_t K, int64_t 
                       void* stream) {
   if (M < 0 || K <= 0) return fail("quant_rows_seg: bad shape");
   if (M == 0) return DC_OK;
+  if (x == nullptr || q == nullptr || s == nullptr) return fail("quant_rows_seg: null pointer");
+  if (reinterpret_cast<uintptr_t>(s) % 4) return fail("quant_rows_seg: s must be 4-byte aligned");
   if (group != 0 && group != 256) return fail("ConvRot group must be 0 or 256 (got %d)", group);
   if (group && K % 256) return fail("K=%lld is not a multiple of the ConvRot group 256", (long long)K);
   if (K % 8 || K > 16384) return fail("quant_rows_seg: K must be a multiple of 8 and at most 16384");
@@ -727,6 +734,9 @@ int dc_ln_mod_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld
                     void* stream) {
   if (M < 0 || K <= 0) return fail("ln_mod_quant: bad shape");
   if (M == 0) return DC_OK;
+  if (x == nullptr || shift == nullptr || scale == nullptr || q == nullptr || s == nullptr)
+    return fail("ln_mod_quant: null pointer");
+  if (reinterpret_cast<uintptr_t>(s) % 4) return fail("ln_mod_quant: s must be 4-byte aligned");
   if (group != 0 && group != 256) return fail("ConvRot group must be 0 or 256 (got %d)", group);
   if (group && K % 256) return fail("K=%lld is not a multiple of the ConvRot group 256", (long long)K);
   if (K % 8 || K > 4096) return fail("ln_mod_quant: K must be a multiple of 8 and at most 4096");
@@ -761,6 +771,7 @@ int dc_qk_norm_rope(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64
                     const void* k_scale1, int64_t split_row, const float* pe, int64_t pe_row0, void* stream) {
   if (L < 0 || H <= 0) return fail("qk_norm_rope: bad shape");
   if (L == 0) return DC_OK;
+  if (qkv == nullptr) return fail("qk_norm_rope: null qkv");
   if (D != 128) return fail("qk_norm_rope: head dim must be 128 (got %lld)", (long long)D);
   if (ld_row % 4 || q_off % 4 || k_off % 4 || reinterpret_cast<uintptr_t>(qkv) % 8)
     return fail("qk_norm_rope: rows and offsets must be 8-byte aligned");
@@ -794,6 +805,11 @@ int dc_rescale(const int32_t* acc, int64_t lda, const float* sx, const float* sw
   if (M == 0) return DC_OK;
   if (lda < N || ldo < N) return fail("rescale: leading dimension smaller than the row");
   if (M > INT32_MAX || N > INT32_MAX) return fail("rescale: dimension above 2^31");
+  if (acc == nullptr || sx == nullptr || sw == nullptr || out == nullptr) return fail("rescale: null pointer");
+  if (reinterpret_cast<uintptr_t>(acc) % 4 || reinterpret_cast<uintptr_t>(sx) % 4 ||
+      reinterpret_cast<uintptr_t>(sw) % 4 || reinterpret_cast<uintptr_t>(out) % 2 ||
+      reinterpret_cast<uintptr_t>(bias) % 2)
+    return fail("rescale: pointers must be aligned to their element size");
   if (int r = check_sm100()) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int grid = static_cast<int>(M < 4096 ? M : 4096);

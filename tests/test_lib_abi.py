@@ -56,3 +56,39 @@ def test_argument_validation_without_gpu():
     assert lay[0] == 4608 and lay[1] == 4608 and lay[7] == n.value
     # codes + scales + ksum for config 2
     assert n.value >= 2 * 24 * 4608 * 128 + 24 * 4608 * 4
+
+
+@pytest.mark.skipif(has_b200(), reason="host-side validation only; fake addresses must never reach a GPU")
+def test_pointer_validation_without_gpu():
+    """Null and under-aligned pointers are refused before any launch (addresses here are never
+    dereferenced: every call must fail in the host-side checks)."""
+    lib = _lib.load()
+    a16, odd = 0x10000, 0x10001
+    # GEMM: null operand, odd bf16 output, odd scale pointer
+    assert lib.dc_gemm_w8a8(None, 16, a16, 16, a16, a16, None, a16, 16, _lib.DTYPE_BF16, 4, 16, 16, 0, None) != 0
+    assert b"null" in lib.dc_last_error()
+    assert lib.dc_gemm_w8a8(a16, 16, a16, 16, a16, a16, None, odd, 16, _lib.DTYPE_BF16, 4, 16, 16, 0, None) != 0
+    assert b"aligned" in lib.dc_last_error()
+    assert lib.dc_gemm_w8a8(a16, 16, a16, 16, a16 + 2, a16, None, a16, 16, _lib.DTYPE_BF16, 4, 16, 16, 0,
+                            None) != 0
+    assert b"aligned" in lib.dc_last_error()
+    # quantizer: odd scale output
+    assert lib.dc_quant_rows(a16, _lib.DTYPE_BF16, 4, 16, 16, 0, 0, a16, a16 + 2, None) != 0
+    assert b"aligned" in lib.dc_last_error()
+    # rescale: null scales
+    assert lib.dc_rescale(a16, 16, None, a16, None, a16, 16, _lib.DTYPE_BF16, 4, 16, None) != 0
+    assert b"null" in lib.dc_last_error()
+    # attention: null v
+    strides = _lib.i64_array([4096, 1024, 128])
+    n = ctypes.c_size_t(0)
+    assert lib.dc_attn_workspace_size(1, 8, 32, 32, 128, 0, ctypes.byref(n)) == 0
+    assert lib.dc_attn_int8_fwd(a16, a16, None, _lib.DTYPE_BF16, 1, 8, 32, 32, 128, strides, strides, strides,
+                                0.088, 0, a16, strides, a16, n.value, None) != 0
+    assert b"null" in lib.dc_last_error()
+    # qk_norm_rope: scale vector not 8-byte aligned, pe not 16-byte aligned
+    assert lib.dc_qk_norm_rope(a16, _lib.DTYPE_BF16, 4, 2, 128, 768, 0, 256, a16 + 4, a16, None, None, 4,
+                               a16, 0, None) != 0
+    assert b"8-byte" in lib.dc_last_error()
+    assert lib.dc_qk_norm_rope(a16, _lib.DTYPE_BF16, 4, 2, 128, 768, 0, 256, a16, a16, None, None, 4,
+                               a16 + 8, 0, None) != 0
+    assert b"16-byte" in lib.dc_last_error()
