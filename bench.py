@@ -421,7 +421,35 @@ def bench_gemm(args, dev, peaks):
         "cublaslt_int_mm": {"ms": cublas_ms, "tops": GEMM_OPS / (cublas_ms * 1e-3) / 1e12,
                             "note": "torch._int_mm (cuBLASLt), int32 out, no quantize/rescale: the "
                                     "reference's GEMM on this GPU"},
+        "cpu_baseline": _cpu_linear_baseline(),
     }
+
+
+def _cpu_linear_baseline(reps: int = 3) -> dict:
+    """Config 1 through the reference's CPU path (its torch-op Int8Linear forward, restated in
+    oracle/torch_ref.py and pinned to its output hashes) on all host cores, whole workload."""
+    import torch
+    from oracle import torch_ref
+    threads = os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(GEMM_M, GEMM_K, generator=g).to(torch.bfloat16)
+        w = (torch.randn(GEMM_N, GEMM_K, generator=g) * 0.02).to(torch.bfloat16)
+        b = (torch.randn(GEMM_N, generator=g) * 0.01).to(torch.bfloat16)
+        wq, ws = torch_ref.quantize_weight(w, 0)
+        torch_ref.int8_linear(x, wq, ws, b, 0)                       # warm-up
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            torch_ref.int8_linear(x, wq, ws, b, 0)
+        sec = (time.perf_counter() - t0) / reps
+    finally:
+        torch.set_num_threads(prev)
+    return {"value": GEMM_OPS / sec / 1e12, "unit": "TOPS", "ms_per_call": sec * 1e3, "cores": threads,
+            "kind": "port", "sample": f"whole config 1 (M={GEMM_M}, K=N={GEMM_K}), {reps} calls after one warm-up",
+            "note": "the reference's torch-op Int8Linear forward (quantize rows, torch._int_mm, rescale)",
+            "cpu": _cpu_model()}
 
 
 # ─── FLUX-architecture DiT (BASELINE configs 4 and 5) ────────────────────────────────────

@@ -1,0 +1,75 @@
+"""The reference's CPU (torch-op) path of the W8A8 linear, restated with torch ops — TEST
+INFRASTRUCTURE ONLY (see ``oracle/__init__.py``): the timed CPU baseline of BASELINE config 1 in
+``bench.py`` and a second checker in ``tests/``.
+
+Without a GPU the reference's ``Int8Linear.forward`` runs its torch-op branch
+(src/diffucore/models/_int8.py:158-170 with ``_fast()`` False): ConvRot by an fp32 matmul with the
+normalised Kronecker power of the 4x4 Hadamard (:64-84), per-row symmetric int8 (:87-97),
+``torch._int_mm`` with M <= 16 padded to 32 rows (:200-207), then the rescale rounded to the model
+dtype before the bias is added in that dtype (:313-323). Pinned by the config-1 SHA-256 of the
+reference's own output (``tests/golden/config1_sha256.json``).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+_H4 = ((1, 1, 1, -1), (1, 1, -1, 1), (1, -1, 1, 1), (-1, 1, 1, 1))
+
+
+def hadamard(n: int) -> torch.Tensor:
+    """fp32 [n, n]: the Kronecker power of the 4x4 Hadamard above, divided by sqrt(n)."""
+    h4 = torch.tensor(_H4, dtype=torch.float32)
+    h = h4
+    while h.shape[0] < n:
+        h = torch.kron(h, h4)
+    if h.shape[0] != n:
+        raise ValueError(f"group {n} is not a power of 4")
+    return h / n ** 0.5
+
+
+def rotate(t: torch.Tensor, group: int) -> torch.Tensor:
+    """fp32 ``t @ H`` over each ``group``-wide slice of the last dimension (identity for 0)."""
+    if not group:
+        return t
+    rows = t.reshape(-1, t.shape[-1] // group, group)
+    return (rows @ hadamard(group)).reshape(t.shape)
+
+
+def quantize_rows(t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(int8 codes, fp32 scale per row): scale = max(amax / 127, 1e-30), code = round(x / scale)
+    (half to even) clamped to [-128, 127]."""
+    t = t.float()
+    scale = torch.clamp(t.abs().amax(dim=-1) / 127.0, min=1e-30)
+    codes = torch.clamp(torch.round(t / scale[..., None]), -128, 127).to(torch.int8)
+    return codes, scale
+
+
+def int_mm(q: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """int32 q [M, K] . w [N, K]^T via torch._int_mm (rows padded to 32 when M <= 16)."""
+    m = q.shape[0]
+    if m <= 16:
+        return torch._int_mm(F.pad(q, (0, 0, 0, 32 - m)), w.t())[:m]
+    return torch._int_mm(q, w.t())
+
+
+def rescale(acc: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor, bias: torch.Tensor | None,
+            dtype: torch.dtype) -> torch.Tensor:
+    """dtype(acc * (sx[m] * sw[n])), then + dtype(bias) in dtype."""
+    y = (acc.float() * (sx[:, None] * sw)).to(dtype)
+    return y if bias is None else y + bias.to(dtype)
+
+
+def int8_linear(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, bias: torch.Tensor | None,
+                group: int = 0) -> torch.Tensor:
+    """The torch-op forward of a W8A8 linear with int8 weight ``wq`` [N, K] and fp32 scales ``ws``."""
+    x2 = x.reshape(-1, x.shape[-1])
+    q, sx = quantize_rows(rotate(x2.float(), group))
+    y = rescale(int_mm(q, wq), sx, ws, bias, x.dtype)
+    return y.reshape(*x.shape[:-1], wq.shape[0])
+
+
+def quantize_weight(w: torch.Tensor, group: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-output-channel int8 of a [N, K] weight after the rotation."""
+    return quantize_rows(rotate(w.float(), group))

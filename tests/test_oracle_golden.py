@@ -117,3 +117,35 @@ def test_bits_roundtrip_matches_torch():
         ref = torch.from_numpy(x).to(dt).view(torch.int16).numpy().view(np.uint16)
         assert np.array_equal(oracle.to_bits(x, tag), ref)
         assert np.array_equal(oracle.to_float(ref, tag), bits_to_torch(ref, dt).float().numpy())
+
+
+def test_torch_restatement_reproduces_config1_output_hashes():
+    """The torch-op restatement of the reference's CPU path (oracle/torch_ref.py), the timed CPU
+    baseline of config 1, gives the reference's own int32 accumulator and bf16 output bit for bit
+    at full size (tests/golden/config1_sha256.json)."""
+    from oracle import torch_ref
+    meta = json.loads((GOLDEN / "config1_sha256.json").read_text())
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(4096, 3072, generator=g).to(torch.bfloat16)
+    w = (torch.randn(3072, 3072, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(3072, generator=g) * 0.01).to(torch.bfloat16)
+    h = lambda t: hashlib.sha256(np.ascontiguousarray(t.numpy()).tobytes()).hexdigest()  # noqa: E731
+    wq, ws = torch_ref.quantize_weight(w, 0)
+    assert h(wq) == meta["wq_sha256"] and h(ws) == meta["ws_sha256"]
+    q, sx = torch_ref.quantize_rows(x)
+    assert h(q) == meta["qx_sha256"] and h(sx) == meta["sx_sha256"]
+    assert h(torch_ref.int_mm(q, wq)) == meta["acc_sha256"]
+    y = torch_ref.int8_linear(x, wq, ws, b, 0)
+    assert h(y.view(torch.int16)) == meta["y_sha256"]
+
+
+def test_torch_restatement_rotation_matches_butterfly_within_ties(golden):
+    """group 256: the fp32-matmul rotation of the restatement against the oracle's butterfly
+    (same codes except at rounding ties, as for the reference's own _rotate)."""
+    from oracle import torch_ref
+    xb = golden["qa_bf16_g256_x"]
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16)
+    q, s = torch_ref.quantize_rows(torch_ref.rotate(x.float(), 256))
+    qo, so = oracle.quant_rows(xb, "bf16", 256)
+    assert (q.numpy() != qo).mean() < 2e-3
+    np.testing.assert_allclose(s.numpy(), so, rtol=1e-5)
