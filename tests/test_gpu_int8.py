@@ -204,3 +204,41 @@ def test_config1_full_size_bit_exact_with_reference():
     assert _sha(_int8.int_mm(qx, layer.weight)) == meta["acc_sha256"]
     assert _sha(layer(xd)) == meta["y_sha256"]
 
+
+
+# ─── mirrors of the reference's own module tests (tests/test_int8.py) ───────────────────
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+
+@pytest.mark.parametrize("k,n", [(2048, 2048), (768, 512), (1024, 8192)])
+def test_kernels_match_reference_torch_ops(k, n):
+    """tests/test_int8.py:141-153: the CUDA Int8Linear (default ConvRot group 256, fp16) against
+    the reference's torch-op path (oracle/torch_ref.py, pinned to the reference's output hashes)
+    within 2e-3 relative, and against the float linear within 2e-2."""
+    from oracle import torch_ref
+    torch.manual_seed(4)
+    lin = nn.Linear(k, n, bias=n == 512).half()
+    m = _int8.Int8Linear.from_linear(lin.to(DEV))
+    x = torch.randn(3, 333, k, dtype=torch.float16)
+    y = m(x.to(DEV)).cpu()
+    bias = None if m.bias is None else m.bias.detach().cpu()
+    y_ref = torch_ref.int8_linear(x, m.weight.cpu(), m.scale.cpu(), bias, m.group)
+    assert y.dtype == torch.float16 and _rel(y, y_ref) < 2e-3
+    with torch.no_grad():
+        y_float = lin.cpu().float()(x.float())
+    assert _rel(y, y_float) < 0.02
+
+
+def test_fused_mlp_matches_reference_unfused():
+    """tests/test_int8.py:156-166: int8_mlp against the torch-op l2(gelu(l1(x)))."""
+    from oracle import torch_ref
+    torch.manual_seed(5)
+    l1 = _int8.Int8Linear.from_linear(nn.Linear(1024, 4096, bias=False).half().to(DEV))
+    l2 = _int8.Int8Linear.from_linear(nn.Linear(4096, 1024, bias=False).half().to(DEV))
+    x = torch.randn(2, 500, 1024, dtype=torch.float16)
+    y = _int8.int8_mlp(x.to(DEV), l1, l2).cpu()
+    h = torch_ref.int8_linear(x, l1.weight.cpu(), l1.scale.cpu(), None, l1.group)
+    y_ref = torch_ref.int8_linear(torch.nn.functional.gelu(h), l2.weight.cpu(), l2.scale.cpu(), None, l2.group)
+    assert _rel(y, y_ref) < 2e-3
