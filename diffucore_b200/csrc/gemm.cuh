@@ -14,7 +14,8 @@
 // TMA writes and the tensor core reads per k-block (32 KB instead of 48 KB per 128 x 256 x 128),
 // the shared-memory traffic that limits the one-CTA tile. Barriers: both CTAs' loads of a stage
 // count on the even CTA's `full_bar`; its MMA commits arrive on both CTAs' `empty_bar` and
-// `acc_full`; both CTAs' epilogue warps arrive on the even CTA's `acc_empty`.
+// `acc_full` (one commit with CTA mask 0b11); both CTAs' epilogue warps arrive on the even CTA's
+// `acc_empty`.
 //
 // The epilogue rounds exactly like the reference's `rescale` (src/diffucore/models/_int8.py:313-323):
 //   y = dtype(float(acc) * (sx[m] * sw[n]));  if bias: y = dtype(float(y) + float(bias[n]))
@@ -218,12 +219,8 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
             else mma_i8_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           if constexpr (PAIR) {
-            mma_commit_pair(smem_u32(&empty_bar[stage]));
-            mma_commit_pair(cluster_addr(&empty_bar[stage], 1));
-            if (kb == p.num_kb - 1) {
-              mma_commit_pair(smem_u32(&acc_full[buf]));
-              mma_commit_pair(cluster_addr(&acc_full[buf], 1));
-            }
+            mma_commit_pair_both(&empty_bar[stage]);
+            if (kb == p.num_kb - 1) mma_commit_pair_both(&acc_full[buf]);
           } else {
             mma_commit(&empty_bar[stage]);
             if (kb == p.num_kb - 1) mma_commit(&acc_full[buf]);
@@ -232,7 +229,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         }
       }
       // Every MMA issued above has completed once this commit lands.
-      if constexpr (PAIR) mma_commit_pair(smem_u32(&drain_bar));
+      if constexpr (PAIR) mma_commit_pair(&drain_bar);
       else mma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, nullptr, 1000000);
     }

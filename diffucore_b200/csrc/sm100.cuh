@@ -349,11 +349,19 @@ __device__ __forceinline__ void mma_i8_ss_pair(uint32_t d_tmem, uint64_t a_desc,
       :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
-// Arrive once on the mbarrier at `bar_addr` (this CTA's or the peer's) when every pair MMA issued
-// so far by this thread has completed.
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar_addr) {
+// Arrive once on this CTA's mbarrier `bar` when every pair MMA issued so far by this thread has
+// completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-               :: "r"(bar_addr) : "memory");
+               :: "r"(smem_u32(bar)) : "memory");
+}
+
+// The same, arriving on the mbarrier at `bar`'s offset in both CTAs of the pair (CTA mask 0b11):
+// the signal both CTAs' producers and epilogues wait for.
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar) {
+  const uint16_t both = 0x3;
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               :: "r"(smem_u32(bar)), "h"(both) : "memory");
 }
 
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
