@@ -673,6 +673,97 @@ def flux_op_breakdown(dev, side: int = 1024) -> dict:
             "other_ms_torch_ops": round(total - sum(r["ms"] for r in rows), 3), "ops": rows}
 
 
+def _time_env(fn, env: dict, warmup: int, steps: int) -> float:
+    """Mean device ms of fn(i) over `steps` calls with the environment variables in `env` set
+    (the library reads its kernel switches at each call); restores the environment."""
+    import torch
+    saved = {k: os.environ.get(k) for k in env}
+    try:
+        for k, v in env.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+        for i in range(warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        st, en = _events(2)
+        _cpu_runahead()
+        st.record()
+        for i in range(steps):
+            fn(i)
+        en.record()
+        torch.cuda.synchronize()
+        return st.elapsed_time(en) / steps
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+
+
+def bench_variants(args, dev, peaks) -> dict:
+    """Kernel variants side by side on the same inputs (rotating sets larger than L2): the
+    two-CTA GEMM (DC_GEMM_PAIR=1) against the one-CTA kernel on config 1 and the FLUX block
+    shapes, and the two-tile attention with dynamic MMA issue (DC_ATTN_ISSUE=dynamic) against the
+    fixed order on config 2 in both quant modes. Times are device ms per call."""
+    import torch
+    from diffucore_b200 import _lib, kernels
+    g = torch.Generator(device=dev).manual_seed(11)
+    peak = _int8_peak_tops(peaks)
+    warm, steps = max(3, args.warmup), max(10, min(args.steps, 100))
+    out = {"unit": "ms per call", "peak_int8_tops": peak}
+    gemms = {"config1 4096x3072x3072 bias": (4096, 3072, 3072, _lib.GELU_NONE, False),
+             "flux qkv 4608x9216x3072": (4608, 9216, 3072, _lib.GELU_NONE, False),
+             "flux mlp0 4608x12288x3072 gelu": (4608, 12288, 3072, _lib.GELU_TANH, False),
+             "flux linear2 4608x3072x15360 gated": (4608, 3072, 15360, _lib.GELU_NONE, True)}
+    for name, (M, N, K, gelu, gated) in gemms.items():
+        nset = 3
+        qs = [torch.randint(-127, 128, (M, K), generator=g, device=dev, dtype=torch.int8) for _ in range(nset)]
+        w = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+        sx = torch.rand(M, generator=g, device=dev) * 1e-2 + 1e-4
+        sw = torch.rand(N, generator=g, device=dev) * 1e-3 + 1e-5
+        bias = (torch.randn(N, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        gate = (torch.randn(N, generator=g, device=dev) * 0.5).to(torch.bfloat16) if gated else None
+        ys = [torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16) for _ in range(nset)]
+
+        def fn(i, qs=qs, w=w, sx=sx, sw=sw, bias=bias, gate=gate, ys=ys, gelu=gelu):
+            y = ys[i % len(ys)]
+            kernels.gemm_w8a8_into(qs[i % len(qs)], w, sx, sw, bias, y, gelu=gelu, gate=gate,
+                                   residual=y if gate is not None else None)
+
+        ops = 2 * M * N * K
+        row = {}
+        for tag, env in (("one_cta", {"DC_GEMM_PAIR": None}), ("pair", {"DC_GEMM_PAIR": "1"})):
+            ms = _time_env(fn, env, warm, steps)
+            row[tag] = {"ms": round(ms, 4), "tops": round(ops / ms / 1e9, 1), "frac": round(ops / ms / 1e9 / peak, 3)}
+        out[name] = row
+        del qs, w, ys
+        torch.cuda.empty_cache()
+    sets = []
+    for _ in range(4):
+        q, k, v = (torch.randn(B, H, S, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+        sets.append((q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)))
+    o = torch.empty(B, S, H, D, device=dev, dtype=torch.bfloat16)
+    for mode_name, mode in (("block64", _lib.MODE_BLOCK64), ("ref", _lib.MODE_REF)):
+        plan = kernels.AttnPlan(B, H, S, S, D, torch.bfloat16, mode, dev)
+
+        def fn(i, plan=plan):
+            q, k, v = sets[i % len(sets)]
+            plan(q, k, v, o, D ** -0.5)
+
+        row = {}
+        for tag, env in (("fixed", {"DC_ATTN_KERNEL": "two_tile", "DC_ATTN_ISSUE": None}),
+                         ("dynamic", {"DC_ATTN_KERNEL": "two_tile", "DC_ATTN_ISSUE": "dynamic"}),
+                         ("single_tile", {"DC_ATTN_KERNEL": "single_tile", "DC_ATTN_ISSUE": None})):
+            ms = _time_env(fn, env, warm, steps)
+            row[tag] = {"ms": round(ms, 4), "tops": round(ATTN_OPS / ms / 1e9, 1)}
+        out[f"attention config2 {mode_name} (prep + main)"] = row
+    out["device_error"] = _lib.device_error()
+    return out
+
+
 def bench_glue(args, dev, peaks) -> dict:
     """The FLUX block's HBM-bound glue kernels alone at 1024^2 shapes (4608 rows), GB/s of their
     algorithmic bytes against the measured HBM peak; inputs rotate over sets larger than L2."""
@@ -722,8 +813,9 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-extras", action="store_true", help="headline attention only (for profiling)")
-    ap.add_argument("--only", default="all", choices=("all", "gemm", "flux", "glue", "sdxl"),
-                    help="gemm / flux: time only the config-1 W8A8 linear / the FLUX DiT")
+    ap.add_argument("--only", default="all", choices=("all", "gemm", "flux", "glue", "sdxl", "variants"),
+                    help="gemm / flux: time only the config-1 W8A8 linear / the FLUX DiT; glue: the FLUX glue "
+                         "kernels; sdxl: the UNet; variants: opt-in kernel variants against the defaults")
     ap.add_argument("--no-flux", action="store_true", help="skip the FLUX DiT timing")
     ap.add_argument("--clocks-csv-dir", default=None,
                     help="also write the raw nvidia-smi clock samples of the timed region to this folder")
@@ -746,8 +838,9 @@ def main() -> int:
         if rank == 0:
             print(json.dumps(res), flush=True)
         return 0
-    if args.only in ("glue", "sdxl"):
-        res = bench_glue(args, dev, peaks) if args.only == "glue" else bench_sdxl(args, dev, peaks)
+    if args.only in ("glue", "sdxl", "variants"):
+        fn = {"glue": bench_glue, "sdxl": bench_sdxl, "variants": bench_variants}[args.only]
+        res = fn(args, dev, peaks)
         if rank == 0:
             print(json.dumps(res), flush=True)
         return 0
