@@ -1,6 +1,6 @@
-"""ComfyUI ``int8_tensorwise`` checkpoints load into the FLUX and SDXL backbones (SURVEY's next row
-for the on-disk format next to the path; reference src/diffucore/models/_int8.py:453-481 and the
-loader sequence src/diffucore/bundle.py:301-305). CPU only.
+"""ComfyUI ``int8_tensorwise`` checkpoints, the on-disk format of the W8A8 layers, load into the
+FLUX and SDXL backbones (reference src/diffucore/models/_int8.py:453-481 and the loader sequence
+src/diffucore/bundle.py:301-305). CPU only.
 
 A model whose block linears were quantized in memory is written out in the int8_tensorwise layout
 (int8 ``weight``, fp32 ``weight_scale``, ``comfy_quant`` JSON tag), read back through
