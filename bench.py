@@ -706,8 +706,9 @@ def _time_env(fn, env: dict, warmup: int, steps: int) -> float:
 def bench_variants(args, dev, peaks) -> dict:
     """Kernel variants side by side on the same inputs (rotating sets larger than L2): the
     two-CTA GEMM (DC_GEMM_PAIR=1) against the one-CTA kernel on config 1 and the FLUX block
-    shapes, and the two-tile attention with dynamic MMA issue (DC_ATTN_ISSUE=dynamic) against the
-    fixed order on config 2 in both quant modes. Times are device ms per call."""
+    shapes, the two-tile attention with dynamic MMA issue (DC_ATTN_ISSUE=dynamic) against the
+    fixed order on config 2 in both quant modes, and the packed-pair rotated row quantizers
+    (DC_ROWQ_PAIR=1) on FLUX's 3072-wide rows. Times are device ms per call."""
     import torch
     from diffucore_b200 import _lib, kernels
     g = torch.Generator(device=dev).manual_seed(11)
@@ -760,6 +761,20 @@ def bench_variants(args, dev, peaks) -> dict:
             ms = _time_env(fn, env, warm, steps)
             row[tag] = {"ms": round(ms, 4), "tops": round(ATTN_OPS / ms / 1e9, 1)}
         out[f"attention config2 {mode_name} (prep + main)"] = row
+    M, C = 4608, 3072
+    xs = [torch.randn(M, C, generator=g, device=dev).to(torch.bfloat16) for _ in range(6)]
+    shift = (0.1 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
+    scale = (0.1 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
+    qbuf = torch.empty(M, C, device=dev, dtype=torch.int8)
+    sbuf = torch.empty(M, device=dev, dtype=torch.float32)
+    for name, fn in (("ln_mod_quant 4608x3072 group 256",
+                      lambda i: kernels.ln_mod_quant(xs[i % 6], shift, scale, 256, qbuf, sbuf)),
+                     ("quant_rows 4608x3072 group 256", lambda i: kernels.quant_rows_into(xs[i % 6], 256, qbuf, sbuf))):
+        row = {}
+        for tag, env in (("default", {"DC_ROWQ_PAIR": None}), ("pair", {"DC_ROWQ_PAIR": "1"})):
+            ms = _time_env(fn, env, warm, steps)
+            row[tag] = {"ms": round(ms, 4), "gbs": round((M * C * 3 + M * 4) / ms / 1e6, 1)}
+        out[name] = row
     out["device_error"] = _lib.device_error()
     return out
 

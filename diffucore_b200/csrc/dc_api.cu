@@ -115,9 +115,44 @@ inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 // Shared-memory streaming quantizers (rowquant.cuh): K % 256 == 0, 16-bit rows, no GELU.
 constexpr int kRowqWarps = 8;
 
+// The rotated quantizers computing two groups per half-warp with packed fp32 operations
+// (rowq_pair_kernel) are opt-in through DC_ROWQ_PAIR=1.
+bool use_rowq_pair() {
+  const char* env = getenv("DC_ROWQ_PAIR");
+  return env != nullptr && strcmp(env, "1") == 0;
+}
+
+template <typename T, bool LNMOD, bool SEG>
+int launch_rowq_pair(const dc::RowSrc& src, int64_t M, int64_t K, const void* shift, const void* scale, int8_t* q,
+                     float* s, cudaStream_t st) {
+  const int nit2 = static_cast<int>((K / 256 + 3) / 4);
+  const size_t smem = (LNMOD ? 2 * K * sizeof(float) : 0) + static_cast<size_t>(kRowqWarps) * 2 * K * sizeof(T) +
+                      static_cast<size_t>(kRowqWarps) * 2 * dc::kRotScratch2 * sizeof(float2);
+  const int64_t ctas64 = (M + kRowqWarps - 1) / kRowqWarps;
+  const int ctas = static_cast<int>(ctas64 < sm_count() ? ctas64 : sm_count());
+  const T* sh = static_cast<const T*>(shift);
+  const T* sc = static_cast<const T*>(scale);
+  const int Ki = static_cast<int>(K);
+  int r = DC_OK;
+  auto go = [&](auto kernel) {
+    r = set_smem(kernel, static_cast<int>(smem));
+    if (r == DC_OK) kernel<<<ctas, 32 * kRowqWarps, smem, st>>>(src, M, Ki, sh, sc, q, s);
+  };
+  if (nit2 <= 1) go(dc::rowq_pair_kernel<T, LNMOD, SEG, 1>);
+  else if (nit2 <= 2) go(dc::rowq_pair_kernel<T, LNMOD, SEG, 2>);
+  else if (nit2 <= 3) go(dc::rowq_pair_kernel<T, LNMOD, SEG, 3>);
+  else go(dc::rowq_pair_kernel<T, LNMOD, SEG, 4>);
+  if (r) return r;
+  DC_CHECK_LAUNCH("quant_rows launch");
+  return DC_OK;
+}
+
 template <typename T, bool GROUP, bool LNMOD, bool SEG>
 int launch_rowq_warp(const dc::RowSrc& src, int64_t M, int64_t K, const void* shift, const void* scale, int8_t* q,
                      float* s, cudaStream_t st) {
+  if constexpr (GROUP && !(LNMOD && SEG)) {
+    if (use_rowq_pair()) return launch_rowq_pair<T, LNMOD, SEG>(src, M, K, shift, scale, q, s, st);
+  }
   const int nit = static_cast<int>((K / 256 + 1) / 2);
   const size_t smem = (LNMOD ? 2 * K * sizeof(T) : 0) + static_cast<size_t>(kRowqWarps) * 2 * K * sizeof(T) +
                       static_cast<size_t>(kRowqWarps) * 2 * dc::kRotScratch * sizeof(float);

@@ -21,6 +21,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 #include "sm100.cuh"
 #include "quant.cuh"
 
@@ -286,6 +287,182 @@ rowq_cta_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, floa
     if (threadIdx.x == 0) s[row] = scale;
     __syncthreads();                     // row buffer and red[] free again
     if (row + 2 * gridDim.x < M) issue_row<T, SEG>(src, row + 2 * gridDim.x, K, rows + buf * K, threadIdx.x, 256);
+    cp_async_commit();
+  }
+  cp_async_wait<0>();
+}
+
+// ----------------------------------------------------------------------------- packed pairs
+// rowq_pair_kernel: rowq_warp_kernel with rotation, computing two groups at once per half-warp.
+// Lane L of half h holds value i of group ga = 4 j + h in .x and value i of group gb = ga + 2 in
+// .y of one float2, and every step of the LayerNorm + modulation and of the rotation is a packed
+// fp32 operation (__fadd2_rn / __fmul2_rn: two independent IEEE round-to-nearest operations), so
+// each group receives exactly rowq_warp_kernel's arithmetic in half the instructions. Groups past
+// the row are zero after the modulation, so they add nothing to the amax and are not stored. The
+// modulation vectors are staged once per CTA as fp32: 1 + scale rounded to the row dtype (what the
+// per-element form computes for every row) and the shift.
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+
+// s - 2 x per lane: __fsub_rn(s, __fmul_rn(2, x)) == s + round(-2 x) (negation is exact).
+__device__ __forceinline__ float2 sub_twice2(float2 s, float2 x) { return add2(s, mul2(make_float2(-2.f, -2.f), x)); }
+
+template <typename T>
+__device__ __forceinline__ float2 round_trip2(float2 v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) return __bfloat1622float2(__float22bfloat162_rn(v));
+  else return __half22float2(__float22half2_rn(v));
+}
+
+// r4_outer / r4_inner on pairs (same summation order per lane).
+__device__ __forceinline__ void r4_outer2(float2 (&x)[16]) {
+  float2 y[16];
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const float2 s = add2(add2(x[b], x[4 + b]), add2(x[8 + b], x[12 + b]));
+#pragma unroll
+    for (int a = 0; a < 4; ++a) y[4 * a + b] = sub_twice2(s, x[4 * (3 - a) + b]);
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = y[i];
+}
+__device__ __forceinline__ void r4_inner2(float2 (&x)[16]) {
+  float2 y[16];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const float2 s = add2(add2(x[4 * a], x[4 * a + 1]), add2(x[4 * a + 2], x[4 * a + 3]));
+#pragma unroll
+    for (int b = 0; b < 4; ++b) y[4 * a + b] = sub_twice2(s, x[4 * a + 3 - b]);
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = y[i];
+}
+
+constexpr int kRotScratch2 = 256;   // float2 per half-warp (64-bit accesses: one half-warp per phase)
+
+// rotate256_half on pairs: layout X in, layout Y (times 1/16) out; both halves call it together.
+__device__ __forceinline__ void rotate256_pair(float2 (&x)[16], float2* scr, int L) {
+  r4_outer2(x);                     // d3
+  r4_inner2(x);                     // d2
+#pragma unroll
+  for (int i = 0; i < 16; ++i) scr[16 * i + (L ^ i)] = x[i];
+  __syncwarp();
+#pragma unroll
+  for (int c = 0; c < 16; ++c) x[c] = scr[16 * L + (c ^ L)];
+  __syncwarp();
+  r4_outer2(x);                     // d1
+  r4_inner2(x);                     // d0
+#pragma unroll
+  for (int c = 0; c < 16; ++c) x[c] = mul2(x[c], make_float2(0.0625f, 0.0625f));
+}
+
+// One warp per row, K <= 4096 (K % 256 == 0), rotation always on. NIT2 >= ceil(K / 1024).
+// Shared memory: [LNMOD: 2 K fp32] [per warp: 2 row buffers of K of T] [per warp: 2 x 256 float2].
+template <typename T, bool LNMOD, bool SEG, int NIT2>
+__global__ void __launch_bounds__(256, 1)
+rowq_pair_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift, const T* __restrict__ mscale,
+                 int8_t* __restrict__ q, float* __restrict__ s) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int half = lane >> 4, L = lane & 15;
+  const int ng = K >> 8;
+  float* mod = reinterpret_cast<float*>(sm);          // [0, K): rt(1 + scale); [K, 2K): shift
+  const size_t mod_bytes = LNMOD ? static_cast<size_t>(2 * K) * sizeof(float) : 0;
+  T* rows = reinterpret_cast<T*>(sm + mod_bytes) + static_cast<size_t>(warp) * 2 * K;
+  float2* scr = reinterpret_cast<float2*>(sm + mod_bytes + static_cast<size_t>(nwarps) * 2 * K * sizeof(T)) +
+                (warp * 2 + half) * kRotScratch2;
+  if (LNMOD) {
+    for (int c = threadIdx.x; c < K; c += blockDim.x) {
+      mod[c] = Vec8<T>::round_trip(__fadd_rn(1.0f, ld_elem(mscale + c)));
+      mod[K + c] = ld_elem(shift + c);
+    }
+    __syncthreads();
+  }
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * nwarps;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * nwarps + warp;
+  if (first < M) issue_row<T, SEG>(src, first, K, rows, lane, 32);
+  cp_async_commit();
+  if (first + stride < M) issue_row<T, SEG>(src, first + stride, K, rows + K, lane, 32);
+  cp_async_commit();
+  int buf = 0;
+  for (int64_t row = first; row < M; row += stride, buf ^= 1) {
+    cp_async_wait<1>();
+    __syncwarp();
+    const T* r = rows + buf * K;
+    float mean = 0.0f, rstd = 1.0f;
+    if (LNMOD) {
+      // the same sums, in the same order, as rowq_warp_kernel
+      const float inv_k = 1.0f / static_cast<float>(K);
+      float a4[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int c = lane; c < (K >> 3); c += 32) {
+        float f[8];
+        Vec8<T>::load(r + 8 * c, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a4[j & 3] = __fadd_rn(a4[j & 3], f[j]);
+      }
+      mean = __fmul_rn(warp_sum_f(__fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]))), inv_k);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) a4[j] = 0.f;
+      for (int c = lane; c < (K >> 3); c += 32) {
+        float f[8];
+        Vec8<T>::load(r + 8 * c, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { const float d = __fsub_rn(f[j], mean); a4[j & 3] = __fmaf_rn(d, d, a4[j & 3]); }
+      }
+      const float var = __fmul_rn(warp_sum_f(__fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]))), inv_k);
+      rstd = rsqrtf(__fadd_rn(var, 1e-6f));
+    }
+    float2 vals[NIT2][16];
+    float am4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < NIT2; ++j) {
+      const int ga = 4 * j + half, gb = ga + 2;
+      const bool la = ga < ng, lb = gb < ng;
+      float2 xv[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        // layout X: value i = 4 a + b of a group is element 64 a + 16 b + L = 16 i + L
+        xv[i] = make_float2(la ? ld_elem(r + 256 * ga + 16 * i + L) : 0.0f,
+                            lb ? ld_elem(r + 256 * gb + 16 * i + L) : 0.0f);
+      }
+      if (LNMOD) {
+        const float2 nm = make_float2(-mean, -mean), rs = make_float2(rstd, rstd);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int ca = 256 * (la ? ga : 0) + 16 * i + L;
+          const int cb = 256 * (lb ? gb : 0) + 16 * i + L;
+          const float2 n = round_trip2<T>(mul2(add2(xv[i], nm), rs));
+          const float2 y = round_trip2<T>(mul2(make_float2(mod[ca], mod[cb]), n));
+          const float2 z = round_trip2<T>(add2(y, make_float2(mod[K + ca], mod[K + cb])));
+          xv[i] = make_float2(la ? z.x : 0.0f, lb ? z.y : 0.0f);
+        }
+      }
+      if (4 * j < ng) rotate256_pair(xv, scr, L);        // warp-uniform condition
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        vals[j][c] = xv[c];
+        am4[c & 3] = fmaxf(am4[c & 3], fmaxf(fabsf(xv[c].x), fabsf(xv[c].y)));
+      }
+    }
+    float am = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const float scale = fmaxf(__fdiv_rn(am, 127.0f), 1e-30f);
+    const float inv = __fdiv_rn(1.0f, scale);
+    int8_t* qr = q + row * static_cast<int64_t>(K);
+#pragma unroll
+    for (int j = 0; j < NIT2; ++j) {
+      const int ga = 4 * j + half, gb = ga + 2;
+      float va[16], vb[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) { va[c] = vals[j][c].x; vb[c] = vals[j][c].y; }
+      if (ga < ng) store_codes16(qr + 256 * ga + 16 * L, va, scale, inv);
+      if (gb < ng) store_codes16(qr + 256 * gb + 16 * L, vb, scale, inv);
+    }
+    if (lane == 0) s[row] = scale;
+    __syncwarp();
+    if (row + 2 * stride < M) issue_row<T, SEG>(src, row + 2 * stride, K, rows + buf * K, lane, 32);
     cp_async_commit();
   }
   cp_async_wait<0>();

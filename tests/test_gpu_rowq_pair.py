@@ -1,0 +1,68 @@
+"""The packed-pair rotated row quantizer (DC_ROWQ_PAIR=1, rowq_pair_kernel) against the default
+kernel, bit for bit: plain rows with ConvRot (quant_rows, group 256), LayerNorm + modulation
+(ln_mod_quant), and the segmented rows of an all-to-all receive buffer (quant_rows_seg), over
+widths with a partial last iteration (groups past the row). Opt-in until it has run on a B200:
+set DC_TEST_ROWQ_PAIR=1."""
+
+from __future__ import annotations
+
+import os
+
+import pytest
+import torch
+
+from diffucore_b200 import _lib, kernels
+
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(os.environ.get("DC_TEST_ROWQ_PAIR") != "1",
+                       reason="packed-pair quantizer is opt-in until run on a B200 (DC_TEST_ROWQ_PAIR=1)"),
+]
+DEV = "cuda"
+
+
+def _both(monkeypatch, fn):
+    monkeypatch.delenv("DC_ROWQ_PAIR", raising=False)
+    a = fn()
+    monkeypatch.setenv("DC_ROWQ_PAIR", "1")
+    b = fn()
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    return a, b
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,K", [(4608, 3072), (333, 256), (100, 1280), (77, 4096), (5, 768)])
+def test_quant_rows_group256_bit_exact(monkeypatch, dtype, M, K):
+    g = torch.Generator().manual_seed(M + K)
+    x = (torch.randn(M, K, generator=g) * 2).to(dtype).to(DEV)
+    x[min(3, M - 1)] = 0                                     # a zero row
+    (qa, sa), (qb, sb) = _both(monkeypatch, lambda: kernels.quant_rows(x, 256))
+    assert torch.equal(qa, qb) and torch.equal(sa, sb)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,K", [(4608, 3072), (64, 256), (300, 1280)])
+def test_ln_mod_quant_bit_exact(monkeypatch, dtype, M, K):
+    g = torch.Generator().manual_seed(K)
+    x = (torch.randn(M, K, generator=g) * 3 + 0.5).to(dtype).to(DEV)
+    shift = (torch.randn(K, generator=g) * 0.3).to(dtype).to(DEV)
+    scale = (torch.randn(K, generator=g) * 0.3).to(dtype).to(DEV)
+    (qa, sa), (qb, sb) = _both(monkeypatch, lambda: kernels.ln_mod_quant(x, shift, scale, 256))
+    assert torch.equal(qa, qb) and torch.equal(sa, sb)
+
+
+@pytest.mark.parametrize("P,W", [(2, 1536), (8, 384)])
+def test_quant_rows_seg_bit_exact(monkeypatch, P, W):
+    g = torch.Generator().manual_seed(P)
+    M = 211
+    recv = torch.randn(P, M, W, generator=g).to(torch.bfloat16).to(DEV)
+
+    def run():
+        q = torch.empty(M, P * W, device=DEV, dtype=torch.int8)
+        s = torch.empty(M, device=DEV, dtype=torch.float32)
+        kernels.quant_rows_seg(recv, None, 256, q, s)
+        return q, s
+
+    (qa, sa), (qb, sb) = _both(monkeypatch, run)
+    assert torch.equal(qa, qb) and torch.equal(sa, sb)

@@ -1,0 +1,125 @@
+"""CPU model of the index mapping of ``rowq_pair_kernel`` (diffucore_b200/csrc/rowquant.cuh).
+
+The kernel computes two ConvRot groups per half-warp at once: lane L of half h holds, for
+iteration j, value i of group ga = 4 j + h and of group gb = ga + 2 (layout X: element 16 i + L of
+the group), applies the LayerNorm + modulation by column, rotates through two swizzled scratch
+transposes and stores 16 codes per lane at 256 g + 16 L. This model follows those index formulas
+with numpy float32 arithmetic (every operation IEEE round-to-nearest, as on the GPU) and must
+reproduce the per-group reference: the oracle's butterfly quantizer on the modulated row. It
+checks the mapping on CPU; the GPU test compares the kernel with the default one bit for bit.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+
+F = np.float32
+
+
+def _rt(x: np.ndarray) -> np.ndarray:
+    return oracle.to_float(oracle.to_bits(x.astype(F), "bf16"), "bf16")
+
+
+def _sub_twice(s, x):
+    return (s + (F(-2.0) * x).astype(F)).astype(F)
+
+
+def _r4_outer(x):                     # x: [16, lanes]
+    y = np.empty_like(x)
+    for b in range(4):
+        s = ((x[b] + x[4 + b]).astype(F) + (x[8 + b] + x[12 + b]).astype(F)).astype(F)
+        for a in range(4):
+            y[4 * a + b] = _sub_twice(s, x[4 * (3 - a) + b])
+    return y
+
+
+def _r4_inner(x):
+    y = np.empty_like(x)
+    for a in range(4):
+        s = ((x[4 * a] + x[4 * a + 1]).astype(F) + (x[4 * a + 2] + x[4 * a + 3]).astype(F)).astype(F)
+        for b in range(4):
+            y[4 * a + b] = _sub_twice(s, x[4 * a + 3 - b])
+    return y
+
+
+def _rotate_half_warp(x):
+    """rotate256_pair for one slot (.x or .y) of the 16 lanes: x [16 values, 16 lanes]."""
+    x = _r4_inner(_r4_outer(x))
+    scr = np.zeros(256, dtype=F)
+    for L in range(16):
+        for i in range(16):
+            scr[16 * i + (L ^ i)] = x[i, L]
+    y = np.empty_like(x)
+    for L in range(16):
+        for c in range(16):
+            y[c, L] = scr[16 * L + (c ^ L)]
+    y = _r4_inner(_r4_outer(y))
+    return (y * F(0.0625)).astype(F)
+
+
+def _model_row(row, mod_a, mod_sh, mean, rstd, lnmod):
+    """Codes and scale of one row as rowq_pair_kernel computes them."""
+    K = row.size
+    ng = K // 256
+    nit2 = (ng + 3) // 4
+    vals = {}
+    for j in range(nit2):
+        for h in range(2):
+            ga, gb = 4 * j + h, 4 * j + h + 2
+            slots = []
+            for g in (ga, gb):
+                live = g < ng
+                x = np.zeros((16, 16), dtype=F)           # [value i, lane L]
+                for L in range(16):
+                    for i in range(16):
+                        col = 256 * (g if live else 0) + 16 * i + L
+                        v = row[col] if live else F(0)
+                        if lnmod:
+                            n = _rt(np.array([(v + F(-mean)) * F(rstd)], dtype=F))[0]
+                            y = _rt(np.array([F(mod_a[col]) * n], dtype=F))[0]
+                            v = _rt(np.array([y + F(mod_sh[col])], dtype=F))[0] if live else F(0)
+                        x[i, L] = v
+                slots.append((g, live, x))
+            if 4 * j < ng:
+                slots = [(g, live, _rotate_half_warp(x)) for g, live, x in slots]
+            for g, live, x in slots:
+                if live:
+                    vals[g] = x                            # layout Y: lane L holds 16 L + c
+    amax = max(float(np.abs(v).max()) for v in vals.values())
+    scale = np.float32(max(F(amax) / F(127.0), F(1e-30)))
+    codes = np.zeros(K, dtype=np.int8)
+    for g, x in vals.items():
+        for L in range(16):
+            seg = (x[:, L] / scale).astype(F)
+            codes[256 * g + 16 * L: 256 * g + 16 * L + 16] = np.clip(np.rint(seg), -128, 127).astype(np.int8)
+    return codes, scale
+
+
+@pytest.mark.parametrize("K", [256, 768, 1280, 3072])
+def test_pair_layout_matches_butterfly_quantizer(K):
+    rng = np.random.default_rng(K)
+    x = _rt(rng.standard_normal((2, K)).astype(F) * F(2.0))
+    ref_q, ref_s = oracle.quant_rows(oracle.to_bits(x, "bf16"), "bf16", 256)
+    for m in range(2):
+        q, s = _model_row(x[m], None, None, 0.0, 1.0, False)
+        assert np.array_equal(q, ref_q[m]) and s == ref_s[m]
+
+
+@pytest.mark.parametrize("K", [512, 3072])
+def test_pair_layout_applies_modulation_by_column(K):
+    """The modulation each element receives is its own column's: the model equals the butterfly
+    quantizer on the row modulated element-wise beforehand."""
+    rng = np.random.default_rng(K + 1)
+    x = _rt(rng.standard_normal(K).astype(F) * F(3.0) + F(0.5))
+    scale_v = _rt((rng.standard_normal(K) * 0.3).astype(F))
+    shift_v = _rt((rng.standard_normal(K) * 0.3).astype(F))
+    mod_a = _rt((F(1.0) + scale_v).astype(F))
+    mean, rstd = F(x.mean(dtype=np.float64)), F(1.0 / np.sqrt(x.var(dtype=np.float64) + 1e-6))
+    n = _rt(((x + F(-mean)).astype(F) * rstd).astype(F))
+    y = _rt(_rt((mod_a * n).astype(F)) + shift_v)
+    ref_q, ref_s = oracle.quant_rows(oracle.to_bits(y[None, :], "bf16"), "bf16", 256)
+    q, s = _model_row(x, mod_a, shift_v, mean, rstd, True)
+    assert np.array_equal(q, ref_q[0]) and s == ref_s[0]
