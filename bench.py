@@ -765,15 +765,20 @@ def bench_variants(args, dev, peaks) -> dict:
     xs = [torch.randn(M, C, generator=g, device=dev).to(torch.bfloat16) for _ in range(6)]
     shift = (0.1 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
     scale = (0.1 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
-    qbuf = torch.empty(M, C, device=dev, dtype=torch.int8)
+    W = 15360
+    wide = [torch.randn(M, W, generator=g, device=dev).to(torch.bfloat16) for _ in range(2)]
+    qbuf = torch.empty(M, W, device=dev, dtype=torch.int8)
     sbuf = torch.empty(M, device=dev, dtype=torch.float32)
-    for name, fn in (("ln_mod_quant 4608x3072 group 256",
-                      lambda i: kernels.ln_mod_quant(xs[i % 6], shift, scale, 256, qbuf, sbuf)),
-                     ("quant_rows 4608x3072 group 256", lambda i: kernels.quant_rows_into(xs[i % 6], 256, qbuf, sbuf))):
+    for name, fn, k in (("ln_mod_quant 4608x3072 group 256",
+                         lambda i: kernels.ln_mod_quant(xs[i % 6], shift, scale, 256, qbuf[:, :C], sbuf), C),
+                        ("quant_rows 4608x3072 group 256",
+                         lambda i: kernels.quant_rows_into(xs[i % 6], 256, qbuf[:, :C], sbuf), C),
+                        ("quant_rows 4608x15360 group 256",
+                         lambda i: kernels.quant_rows_into(wide[i % 2], 256, qbuf, sbuf), W)):
         row = {}
         for tag, env in (("default", {"DC_ROWQ_PAIR": None}), ("pair", {"DC_ROWQ_PAIR": "1"})):
             ms = _time_env(fn, env, warm, steps)
-            row[tag] = {"ms": round(ms, 4), "gbs": round((M * C * 3 + M * 4) / ms / 1e6, 1)}
+            row[tag] = {"ms": round(ms, 4), "gbs": round((M * k * 3 + M * 4) / ms / 1e6, 1)}
         out[name] = row
     out["device_error"] = _lib.device_error()
     return out

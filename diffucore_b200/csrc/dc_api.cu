@@ -175,8 +175,30 @@ int launch_rowq_warp(const dc::RowSrc& src, int64_t M, int64_t K, const void* sh
   return DC_OK;
 }
 
+template <typename T, bool SEG>
+int launch_rowq_cta_pair(const dc::RowSrc& src, int64_t M, int64_t K, int8_t* q, float* s, cudaStream_t st) {
+  const int nit2 = static_cast<int>((K / 256 + 31) / 32);
+  const size_t smem = 2 * K * sizeof(T) + 16 * dc::kRotScratch2 * sizeof(float2);
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 2;
+  const int ctas = static_cast<int>(M < cap ? M : cap);
+  const int Ki = static_cast<int>(K);
+  int r = DC_OK;
+  auto go = [&](auto kernel) {
+    r = set_smem(kernel, static_cast<int>(smem));
+    if (r == DC_OK) kernel<<<ctas, 256, smem, st>>>(src, M, Ki, q, s);
+  };
+  if (nit2 <= 1) go(dc::rowq_cta_pair_kernel<T, SEG, 1>);
+  else go(dc::rowq_cta_pair_kernel<T, SEG, 2>);
+  if (r) return r;
+  DC_CHECK_LAUNCH("quant_rows launch");
+  return DC_OK;
+}
+
 template <typename T, bool GROUP, bool SEG>
 int launch_rowq_cta(const dc::RowSrc& src, int64_t M, int64_t K, int8_t* q, float* s, cudaStream_t st) {
+  if constexpr (GROUP) {
+    if (use_rowq_pair()) return launch_rowq_cta_pair<T, SEG>(src, M, K, q, s, st);
+  }
   const int nit = static_cast<int>((K / 256 + 15) / 16);
   const size_t smem = 2 * K * sizeof(T) + 16 * dc::kRotScratch * sizeof(float);
   const int64_t cap = static_cast<int64_t>(sm_count()) * 2;

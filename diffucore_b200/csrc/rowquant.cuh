@@ -468,4 +468,74 @@ rowq_pair_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift
   cp_async_wait<0>();
 }
 
+// One CTA of 256 threads per row, 4096 < K <= 16384 (K % 256 == 0), rotation always on: the
+// packed form of rowq_cta_kernel. Half-warp hw computes groups ga = 32 j + hw and gb = ga + 16 at
+// iteration j (NIT2 >= ceil(K / 8192)). Shared memory: [2 row buffers of K of T] [16 x 256 float2].
+template <typename T, bool SEG, int NIT2>
+__global__ void __launch_bounds__(256, 2)
+rowq_cta_pair_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, float* __restrict__ s) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  __shared__ float red[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane >> 4, L = lane & 15;
+  const int hw = warp * 2 + half;
+  const int ng = K >> 8;
+  T* rows = reinterpret_cast<T*>(sm);
+  float2* scr = reinterpret_cast<float2*>(sm + static_cast<size_t>(2 * K) * sizeof(T)) + hw * kRotScratch2;
+  const int64_t first = blockIdx.x;
+  if (first < M) issue_row<T, SEG>(src, first, K, rows, threadIdx.x, 256);
+  cp_async_commit();
+  if (first + gridDim.x < M) issue_row<T, SEG>(src, first + gridDim.x, K, rows + K, threadIdx.x, 256);
+  cp_async_commit();
+  int buf = 0;
+  for (int64_t row = first; row < M; row += gridDim.x, buf ^= 1) {
+    cp_async_wait<1>();
+    __syncthreads();
+    const T* r = rows + buf * K;
+    float2 vals[NIT2][16];
+    float am4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < NIT2; ++j) {
+      const int ga = 32 * j + hw, gb = ga + 16;
+      const bool la = ga < ng, lb = gb < ng;
+      float2 xv[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        xv[i] = make_float2(la ? ld_elem(r + 256 * ga + 16 * i + L) : 0.0f,
+                            lb ? ld_elem(r + 256 * gb + 16 * i + L) : 0.0f);
+      if (32 * j + 2 * warp < ng) rotate256_pair(xv, scr, L);     // warp-uniform condition
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        vals[j][c] = xv[c];
+        am4[c & 3] = fmaxf(am4[c & 3], fmaxf(fabsf(xv[c].x), fabsf(xv[c].y)));
+      }
+    }
+    float am = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    if (lane == 0) red[warp] = am;
+    __syncthreads();
+    am = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) am = fmaxf(am, red[w]);
+    const float scale = fmaxf(__fdiv_rn(am, 127.0f), 1e-30f);
+    const float inv = __fdiv_rn(1.0f, scale);
+    int8_t* qr = q + row * static_cast<int64_t>(K);
+#pragma unroll
+    for (int j = 0; j < NIT2; ++j) {
+      const int ga = 32 * j + hw, gb = ga + 16;
+      float va[16], vb[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) { va[c] = vals[j][c].x; vb[c] = vals[j][c].y; }
+      if (ga < ng) store_codes16(qr + 256 * ga + 16 * L, va, scale, inv);
+      if (gb < ng) store_codes16(qr + 256 * gb + 16 * L, vb, scale, inv);
+    }
+    if (threadIdx.x == 0) s[row] = scale;
+    __syncthreads();                     // row buffer and red[] free again
+    if (row + 2 * gridDim.x < M) issue_row<T, SEG>(src, row + 2 * gridDim.x, K, rows + buf * K, threadIdx.x, 256);
+    cp_async_commit();
+  }
+  cp_async_wait<0>();
+}
+
 }  // namespace dc

@@ -32,7 +32,8 @@ def _both(monkeypatch, fn):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("M,K", [(4608, 3072), (333, 256), (100, 1280), (77, 4096), (5, 768)])
+@pytest.mark.parametrize("M,K", [(4608, 3072), (333, 256), (100, 1280), (77, 4096), (5, 768), (4608, 15360),
+                                 (300, 12288), (33, 4352), (7, 16384)])
 def test_quant_rows_group256_bit_exact(monkeypatch, dtype, M, K):
     g = torch.Generator().manual_seed(M + K)
     x = (torch.randn(M, K, generator=g) * 2).to(dtype).to(DEV)
@@ -52,16 +53,17 @@ def test_ln_mod_quant_bit_exact(monkeypatch, dtype, M, K):
     assert torch.equal(qa, qb) and torch.equal(sa, sb)
 
 
-@pytest.mark.parametrize("P,W", [(2, 1536), (8, 384)])
-def test_quant_rows_seg_bit_exact(monkeypatch, P, W):
-    g = torch.Generator().manual_seed(P)
+@pytest.mark.parametrize("P,W,K2", [(2, 1536, 0), (8, 384, 0), (8, 384, 12288), (1, 3072, 12288)])
+def test_quant_rows_seg_bit_exact(monkeypatch, P, W, K2):
+    g = torch.Generator().manual_seed(P + K2)
     M = 211
     recv = torch.randn(P, M, W, generator=g).to(torch.bfloat16).to(DEV)
+    x2 = torch.randn(M, K2 + 64, generator=g).to(torch.bfloat16).to(DEV)[:, 64:] if K2 else None
 
     def run():
-        q = torch.empty(M, P * W, device=DEV, dtype=torch.int8)
+        q = torch.empty(M, P * W + K2, device=DEV, dtype=torch.int8)
         s = torch.empty(M, device=DEV, dtype=torch.float32)
-        kernels.quant_rows_seg(recv, None, 256, q, s)
+        kernels.quant_rows_seg(recv, x2, 256, q, s)
         return q, s
 
     (qa, sa), (qb, sb) = _both(monkeypatch, run)

@@ -1,4 +1,5 @@
-"""CPU model of the index mapping of ``rowq_pair_kernel`` (diffucore_b200/csrc/rowquant.cuh).
+"""CPU model of the index mapping of ``rowq_pair_kernel`` and ``rowq_cta_pair_kernel``
+(diffucore_b200/csrc/rowquant.cuh).
 
 The kernel computes two ConvRot groups per half-warp at once: lane L of half h holds, for
 iteration j, value i of group ga = 4 j + h and of group gb = ga + 2 (layout X: element 16 i + L of
@@ -7,6 +8,8 @@ transposes and stores 16 codes per lane at 256 g + 16 L. This model follows thos
 with numpy float32 arithmetic (every operation IEEE round-to-nearest, as on the GPU) and must
 reproduce the per-group reference: the oracle's butterfly quantizer on the modulated row. It
 checks the mapping on CPU; the GPU test compares the kernel with the default one bit for bit.
+The one-CTA-per-row form for wide rows gives half-warp hw of 16 the groups 32 j + hw and
+32 j + hw + 16; every group of a row is computed exactly once under both mappings.
 """
 
 from __future__ import annotations
@@ -123,3 +126,52 @@ def test_pair_layout_applies_modulation_by_column(K):
     ref_q, ref_s = oracle.quant_rows(oracle.to_bits(y[None, :], "bf16"), "bf16", 256)
     q, s = _model_row(x, mod_a, shift_v, mean, rstd, True)
     assert np.array_equal(q, ref_q[0]) and s == ref_s[0]
+
+
+def _model_row_cta(row):
+    """rowq_cta_pair_kernel: half-warp hw of 16 computes groups 32 j + hw and 32 j + hw + 16."""
+    K = row.size
+    ng = K // 256
+    nit2 = (ng + 31) // 32
+    vals = {}
+    for j in range(nit2):
+        for hw in range(16):
+            warp = hw // 2
+            for g in (32 * j + hw, 32 * j + hw + 16):
+                if g >= ng:
+                    continue
+                x = np.zeros((16, 16), dtype=F)
+                for L in range(16):
+                    for i in range(16):
+                        x[i, L] = row[256 * g + 16 * i + L]
+                assert 32 * j + 2 * warp < ng          # the warp-uniform rotate condition holds
+                assert g not in vals
+                vals[g] = _rotate_half_warp(x)
+    assert sorted(vals) == list(range(ng))
+    amax = max(float(np.abs(v).max()) for v in vals.values())
+    scale = np.float32(max(F(amax) / F(127.0), F(1e-30)))
+    codes = np.zeros(K, dtype=np.int8)
+    for g, x in vals.items():
+        for L in range(16):
+            seg = (x[:, L] / scale).astype(F)
+            codes[256 * g + 16 * L: 256 * g + 16 * L + 16] = np.clip(np.rint(seg), -128, 127).astype(np.int8)
+    return codes, scale
+
+
+@pytest.mark.parametrize("K", [4352, 12288, 15360, 16384])
+def test_cta_pair_layout_matches_butterfly_quantizer(K):
+    rng = np.random.default_rng(K)
+    x = _rt(rng.standard_normal((1, K)).astype(F))
+    ref_q, ref_s = oracle.quant_rows(oracle.to_bits(x, "bf16"), "bf16", 256)
+    q, s = _model_row_cta(x[0])
+    assert np.array_equal(q, ref_q[0]) and s == ref_s[0]
+
+
+@pytest.mark.parametrize("ng", range(1, 65))
+def test_pair_mappings_cover_every_group_once(ng):
+    warp_groups = [g for j in range((ng + 3) // 4) for h in range(2) for g in (4 * j + h, 4 * j + h + 2) if g < ng]
+    cta_groups = [g for j in range((ng + 31) // 32) for hw in range(16) for g in (32 * j + hw, 32 * j + hw + 16)
+                  if g < ng]
+    assert sorted(cta_groups) == list(range(ng))
+    if ng <= 16:                                   # the warp kernel serves K <= 4096
+        assert sorted(warp_groups) == list(range(ng))
