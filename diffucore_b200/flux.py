@@ -176,18 +176,24 @@ class Flux(nn.Module):
     def forward(self, img: torch.Tensor, img_ids: torch.Tensor, txt: torch.Tensor, txt_ids: torch.Tensor,
                 timesteps: torch.Tensor, y: torch.Tensor | None = None,
                 guidance: torch.Tensor | None = None) -> torch.Tensor:
-        """Velocity for image tokens ``img`` [1, Li, in_channels] (the reference signature,
-        src/diffucore/models/flux_dit.py:410-447), single GPU."""
-        if img.shape[0] != 1:
-            raise ValueError("FluxRunner runs batch 1")
+        """Velocity for image tokens ``img`` [B, Li, in_channels] (the reference signature,
+        src/diffucore/models/flux_dit.py:410-447), single GPU. The runner takes one sample at a time;
+        a batch runs its samples in turn (the reference's pipelines call it with B = 1)."""
         key = (txt.shape[1], img.shape[1])
         runner = self._runners.get(key)
         if runner is None:
             runner = FluxRunner(self, txt.shape[1], img.shape[1], device=img.device)
             self._runners[key] = runner
-        runner.set_positions(img_ids, txt_ids)
-        out = runner.forward(img[0], txt[0], timesteps, y, guidance)
-        return out.unsqueeze(0)
+
+        def pick(t, b):                 # per-sample slice of a [B, ...] or broadcast [1, ...] tensor
+            return None if t is None else (t[b:b + 1] if t.shape[0] > 1 else t)
+
+        outs = []
+        for b in range(img.shape[0]):
+            runner.set_positions(pick(img_ids, b), pick(txt_ids, b))
+            outs.append(runner.forward(img[b], txt[b if txt.shape[0] > 1 else 0], pick(timesteps, b), pick(y, b),
+                                       pick(guidance, b)))
+        return torch.stack(outs)
 
 
 # ─── embeddings, positions, schedule (functions of the reference pipeline) ───────────────

@@ -213,3 +213,22 @@ def test_flux_full_width_against_torch_restatement():
     # tests/test_attention_dispatch.py:198-213).
     rel = ((got - want).norm() / want.norm()).item()
     assert _cos(got, want) >= 0.999 and rel < 3e-2, (_cos(got, want), rel)
+
+
+def test_flux_backbone_batch_equals_per_sample():
+    """The drop-in backbone signature with B = 2 (the reference's pipelines use B = 1): each sample's
+    velocity equals the single-sample call."""
+    model = flux.Flux(flux.FluxConfig(**TINY))
+    flux.init_random_(model, seed=0, device="cpu")
+    model = model.to(DEV)
+    flux.quantize_linears(model, model.block_linear_names(), DEV, group=256)
+    g = torch.Generator().manual_seed(8)
+    img = torch.randn(2, 96, 64, generator=g).to(torch.bfloat16).to(DEV)
+    txt = torch.randn(2, 40, 64, generator=g).to(torch.bfloat16).to(DEV)
+    y = torch.randn(2, 32, generator=g).to(torch.bfloat16).to(DEV)
+    t = torch.tensor([0.3, 0.8], dtype=torch.bfloat16, device=DEV)
+    iid, tid = flux.img_ids(16, 24, 2).to(DEV), flux.txt_ids(40).to(DEV)
+    both = model(img, iid, txt, tid, t, y)
+    for b in range(2):
+        one = model(img[b:b + 1], iid, txt[b:b + 1], tid, t[b:b + 1], y[b:b + 1])
+        assert torch.equal(both[b:b + 1], one)
