@@ -706,8 +706,9 @@ def _time_env(fn, env: dict, warmup: int, steps: int) -> float:
 def bench_variants(args, dev, peaks) -> dict:
     """Kernel variants side by side on the same inputs (rotating sets larger than L2): the
     two-CTA GEMM (DC_GEMM_PAIR=1) against the one-CTA kernel on config 1 and the FLUX block
-    shapes, the two-tile attention with dynamic MMA issue (DC_ATTN_ISSUE=dynamic) against the
-    fixed order on config 2 in both quant modes, and the packed-pair rotated row quantizers
+    shapes, the two-tile attention with dynamic MMA issue (DC_ATTN_ISSUE=dynamic) and the CTA-pair
+    attention (DC_ATTN_KERNEL=pair) against the fixed-order one-CTA kernel on config 2 in both
+    quant modes, and the packed-pair rotated row quantizers
     (DC_ROWQ_PAIR=1) on FLUX's 3072-wide rows. Times are device ms per call."""
     import torch
     from diffucore_b200 import _lib, kernels
@@ -757,7 +758,8 @@ def bench_variants(args, dev, peaks) -> dict:
         row = {}
         for tag, env in (("fixed", {"DC_ATTN_KERNEL": "two_tile", "DC_ATTN_ISSUE": None}),
                          ("dynamic", {"DC_ATTN_KERNEL": "two_tile", "DC_ATTN_ISSUE": "dynamic"}),
-                         ("single_tile", {"DC_ATTN_KERNEL": "single_tile", "DC_ATTN_ISSUE": None})):
+                         ("single_tile", {"DC_ATTN_KERNEL": "single_tile", "DC_ATTN_ISSUE": None}),
+                         ("cta_pair", {"DC_ATTN_KERNEL": "pair", "DC_ATTN_ISSUE": None})):
             ms = _time_env(fn, env, warm, steps)
             row[tag] = {"ms": round(ms, 4), "tops": round(ATTN_OPS / ms / 1e9, 1)}
         out[f"attention config2 {mode_name} (prep + main)"] = row

@@ -594,6 +594,7 @@ int attn_prep(const void* q, const void* k, int64_t B, int64_t H, int64_t Lq, in
 // 49 vs 81 us per wave) and so wins when the two-tile grid ends in a poorly filled wave (few
 // heads per GPU, as with a sequence-parallel split). Environment DC_ATTN_KERNEL = "two_tile" or
 // "single_tile" pins one (tests use it to cover both).
+// DC_ATTN_KERNEL = "pair" selects the CTA-pair kernel for D = 128 (attn_pair_kernel; opt-in).
 bool use_single_tile_kernel(int64_t ctas_two_tile, int64_t ctas_single_tile) {
   const char* env = getenv("DC_ATTN_KERNEL");
   if (env != nullptr && strcmp(env, "two_tile") == 0) return false;
@@ -643,6 +644,33 @@ int attn_main(const void* v, int64_t B, int64_t H, int64_t Lq, int64_t Lk, const
   p.q_scale = reinterpret_cast<const float*>(ws + a.q_scale);
   p.k_scale = reinterpret_cast<const float*>(ws + a.k_scale);
   p.o = o; p.o_sb = os[0]; p.o_sl = os[1]; p.o_sh = os[2];
+  const char* which = getenv("DC_ATTN_KERNEL");
+  if (D == 128 && which != nullptr && strcmp(which, "pair") == 0) {
+    // CTA-pair kernel (opt-in): K staged in 64-key halves, one per CTA of a pair
+    CUtensorMap tk_half;
+    const uint64_t dims[2] = {static_cast<uint64_t>(D), static_cast<uint64_t>(B * H * a.Lk_pad)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(D)};
+    const uint32_t box[2] = {static_cast<uint32_t>(D), 64};
+    int r = make_map(&tk_half, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, ws + a.k_codes, dims, strides, box, qk_swz);
+    if (r) return r;
+    auto kernel = dc::attn_pair_kernel<BF16>;
+    if ((r = set_smem(kernel, dc::AttnPairSmem::kDynamic))) return r;
+    const int64_t pairs = (a.Lq_pad + dc::kPairRows - 1) / dc::kPairRows;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), static_cast<unsigned>(H), static_cast<unsigned>(B));
+    cfg.blockDim = dim3(dc::kAttnThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(dc::AttnPairSmem::kDynamic);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tq, tk_half, tv, p);
+    if (e != cudaSuccess) return cuda_fail(e, "attention pair launch");
+    DC_CHECK_LAUNCH("attention launch");
+    return DC_OK;
+  }
   if (use_single_tile_kernel(B * H * (a.Lq_pad / dc::kAttnRows), B * H * (a.Lq_pad / dc::kDbRows))) {
     using SD = dc::AttnDbSmem<D>;
     auto kernel = dc::attn_db_kernel<D, BF16>;

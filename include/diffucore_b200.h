@@ -150,6 +150,8 @@ int dc_attn_workspace_layout(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64
  * "single_tile" pins one. Both give the same result within the stated tolerance.
  * DC_ATTN_ISSUE = "dynamic" makes the two-tile kernel's MMA thread issue each tile's next group
  * as soon as its inputs are ready (same arithmetic, bit-identical output; experimental).
+ * DC_ATTN_KERNEL = "pair" (D = 128) runs the two-tile kernel over CTA pairs with cta_group::2 MMAs,
+ * each SM staging half of every K and V tile (experimental).
  * Replaces the pybind `fwd(q, k, v, sm_scale)` of src/diffucore/kernels/int8_attn_sm80.cu:460-497
  * (and int8_attn_sm75.cu:477-514) called from `attention_blhd` / `attention_bhld`
  * (src/diffucore/models/_attention.py:216-217, :268-271). */
