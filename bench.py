@@ -398,8 +398,9 @@ def bench_e2e_pipelined(args, dev):
             "output_matches_serial_call": bool(torch.equal(host_out, ref))}
 
 
-def bench_gemm(args, dev, peaks):
-    """Config 1: W8A8 linear (quantize + tcgen05 GEMM with rescale/bias epilogue)."""
+def bench_gemm(args, dev, peaks, cpu_baseline: bool = True):
+    """Config 1: W8A8 linear (quantize + tcgen05 GEMM with rescale/bias epilogue). With
+    `cpu_baseline` (rank 0 of a one-GPU run only) the reference's CPU path is timed beside it."""
     import torch
     from diffucore_b200 import _int8, kernels
     g = torch.Generator().manual_seed(0)
@@ -461,7 +462,7 @@ def bench_gemm(args, dev, peaks):
         "cublaslt_int_mm": {"ms": cublas_ms, "tops": GEMM_OPS / (cublas_ms * 1e-3) / 1e12,
                             "note": "torch._int_mm (cuBLASLt), int32 out, no quantize/rescale: the "
                                     "reference's GEMM on this GPU"},
-        "cpu_baseline": _cpu_linear_baseline(),
+        **({"cpu_baseline": _cpu_linear_baseline()} if cpu_baseline else {}),
     }
 
 
@@ -867,7 +868,8 @@ def main() -> int:
             print(json.dumps(res), flush=True)
         return 0
     if args.only in ("gemm", "flux"):
-        res = bench_gemm(args, dev, peaks) if args.only == "gemm" else bench_flux(args, world, rank, dev, peaks)
+        res = (bench_gemm(args, dev, peaks, cpu_baseline=rank == 0 and world == 1) if args.only == "gemm"
+               else bench_flux(args, world, rank, dev, peaks))
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:
@@ -909,7 +911,7 @@ def main() -> int:
                             "ms_per_step": r["total_ms"] / args.steps, "prep_ms": r["prep_ms"],
                             "attn_kernel_ms": r["main_ms"]}
         del ref_plan
-        line["w8a8_linear"] = bench_gemm(args, dev, peaks)
+        line["w8a8_linear"] = bench_gemm(args, dev, peaks, cpu_baseline=rank == 0 and world == 1)
         e2e = bench_e2e(args, dev)
         if world > 1:
             # every rank ran the same pipeline on its own GPU: whole-job rate over the slowest rank
