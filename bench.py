@@ -709,8 +709,8 @@ def bench_variants(args, dev, peaks) -> dict:
     two-CTA GEMM (DC_GEMM_PAIR=1) against the one-CTA kernel on config 1 and the FLUX block
     shapes, the two-tile attention with dynamic MMA issue (DC_ATTN_ISSUE=dynamic) and the CTA-pair
     attention (DC_ATTN_KERNEL=pair) against the fixed-order one-CTA kernel on config 2 in both
-    quant modes, and the packed-pair rotated row quantizers
-    (DC_ROWQ_PAIR=1) on FLUX's 3072-wide rows. Times are device ms per call."""
+    quant modes, and the packed-pair rotated row quantizers (the default) against the one-group
+    kernels (DC_ROWQ_PAIR=0) on FLUX's rows. Times are device ms per call."""
     import torch
     from diffucore_b200 import _lib, kernels
     g = torch.Generator(device=dev).manual_seed(11)
@@ -779,7 +779,7 @@ def bench_variants(args, dev, peaks) -> dict:
                         ("quant_rows 4608x15360 group 256",
                          lambda i: kernels.quant_rows_into(wide[i % 2], 256, qbuf, sbuf), W)):
         row = {}
-        for tag, env in (("default", {"DC_ROWQ_PAIR": None}), ("pair", {"DC_ROWQ_PAIR": "1"})):
+        for tag, env in (("one_group", {"DC_ROWQ_PAIR": "0"}), ("pair", {"DC_ROWQ_PAIR": None})):
             ms = _time_env(fn, env, warm, steps)
             row[tag] = {"ms": round(ms, 4), "gbs": round((M * k * 3 + M * 4) / ms / 1e6, 1)}
         out[name] = row

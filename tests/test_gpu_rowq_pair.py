@@ -1,30 +1,24 @@
-"""The packed-pair rotated row quantizer (DC_ROWQ_PAIR=1, rowq_pair_kernel) against the default
-kernel, bit for bit: plain rows with ConvRot (quant_rows, group 256), LayerNorm + modulation
-(ln_mod_quant), and the segmented rows of an all-to-all receive buffer (quant_rows_seg), over
-widths with a partial last iteration (groups past the row). Opt-in until it has run on a B200:
-set DC_TEST_ROWQ_PAIR=1."""
+"""The packed-pair rotated row quantizers (rowq_pair_kernel, rowq_cta_pair_kernel: the default
+for group 256) against the one-group kernels they replaced (DC_ROWQ_PAIR=0), bit for bit: plain
+rows with ConvRot (quant_rows, group 256), LayerNorm + modulation (ln_mod_quant), and the
+segmented rows of an all-to-all receive buffer (quant_rows_seg), over widths with a partial last
+iteration (groups past the row)."""
 
 from __future__ import annotations
-
-import os
 
 import pytest
 import torch
 
 from diffucore_b200 import _lib, kernels
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("DC_TEST_ROWQ_PAIR") != "1",
-                       reason="packed-pair quantizer is opt-in until run on a B200 (DC_TEST_ROWQ_PAIR=1)"),
-]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
 def _both(monkeypatch, fn):
-    monkeypatch.delenv("DC_ROWQ_PAIR", raising=False)
+    monkeypatch.setenv("DC_ROWQ_PAIR", "0")                  # one-group kernels
     a = fn()
-    monkeypatch.setenv("DC_ROWQ_PAIR", "1")
+    monkeypatch.delenv("DC_ROWQ_PAIR", raising=False)        # default: packed pairs
     b = fn()
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
