@@ -764,24 +764,41 @@ def bench_variants(args, dev, peaks) -> dict:
             ms = _time_env(fn, env, warm, steps)
             row[tag] = {"ms": round(ms, 4), "tops": round(ATTN_OPS / ms / 1e9, 1)}
         out[f"attention config2 {mode_name} (prep + main)"] = row
-    M, C = 4608, 3072
+    out["row_quantizers"] = bench_rowq(args, dev, peaks)
+    out["device_error"] = _lib.device_error()
+    return out
+
+
+def bench_rowq(args, dev, peaks) -> dict:
+    """The rotated row quantizers at FLUX row widths (bf16, group 256): the packed-pair kernels (the
+    default) against the one-group kernels (DC_ROWQ_PAIR=0), same inputs rotating over sets larger
+    than L2. Device us per call and GB/s of 2 B read + 1 B written per element."""
+    import torch
+    from diffucore_b200 import _lib, kernels
+    g = torch.Generator(device=dev).manual_seed(11)
+    warm, steps = max(3, args.warmup), max(10, min(args.steps, 100))
+    M, C, W = 4608, 3072, 15360
     xs = [torch.randn(M, C, generator=g, device=dev).to(torch.bfloat16) for _ in range(6)]
     shift = (0.1 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
     scale = (0.1 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
-    W = 15360
     wide = [torch.randn(M, W, generator=g, device=dev).to(torch.bfloat16) for _ in range(2)]
+    mid = [torch.randn(4096, 12288, generator=g, device=dev).to(torch.bfloat16) for _ in range(3)]
     qbuf = torch.empty(M, W, device=dev, dtype=torch.int8)
     sbuf = torch.empty(M, device=dev, dtype=torch.float32)
-    for name, fn, k in (("ln_mod_quant 4608x3072 group 256",
-                         lambda i: kernels.ln_mod_quant(xs[i % 6], shift, scale, 256, qbuf[:, :C], sbuf), C),
-                        ("quant_rows 4608x3072 group 256",
-                         lambda i: kernels.quant_rows_into(xs[i % 6], 256, qbuf[:, :C], sbuf), C),
-                        ("quant_rows 4608x15360 group 256",
-                         lambda i: kernels.quant_rows_into(wide[i % 2], 256, qbuf, sbuf), W)):
+    cases = (("ln_mod_quant 4608x3072 group 256",
+              lambda i: kernels.ln_mod_quant(xs[i % 6], shift, scale, 256, qbuf[:, :C], sbuf), M * C),
+             ("quant_rows 4608x3072 group 256",
+              lambda i: kernels.quant_rows_into(xs[i % 6], 256, qbuf[:, :C], sbuf), M * C),
+             ("quant_rows 4096x12288 group 256",
+              lambda i: kernels.quant_rows_into(mid[i % 3], 256, qbuf[:4096, :12288], sbuf[:4096]), 4096 * 12288),
+             ("quant_rows 4608x15360 group 256",
+              lambda i: kernels.quant_rows_into(wide[i % 2], 256, qbuf, sbuf), M * W))
+    out = {"unit": "us per call", "peak_hbm_gbs": peaks["hbm_gbs"]}
+    for name, fn, elems in cases:
         row = {}
         for tag, env in (("one_group", {"DC_ROWQ_PAIR": "0"}), ("pair", {"DC_ROWQ_PAIR": None})):
             ms = _time_env(fn, env, warm, steps)
-            row[tag] = {"ms": round(ms, 4), "gbs": round((M * k * 3 + M * 4) / ms / 1e6, 1)}
+            row[tag] = {"us": round(ms * 1e3, 2), "gbs": round(elems * 3 / ms / 1e6, 1)}
         out[name] = row
     out["device_error"] = _lib.device_error()
     return out
@@ -836,9 +853,10 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-extras", action="store_true", help="headline attention only (for profiling)")
-    ap.add_argument("--only", default="all", choices=("all", "gemm", "flux", "glue", "sdxl", "variants"),
+    ap.add_argument("--only", default="all", choices=("all", "gemm", "flux", "glue", "sdxl", "variants", "rowq"),
                     help="gemm / flux: time only the config-1 W8A8 linear / the FLUX DiT; glue: the FLUX glue "
-                         "kernels; sdxl: the UNet; variants: opt-in kernel variants against the defaults")
+                         "kernels; sdxl: the UNet; variants: opt-in kernel variants against the defaults; "
+                         "rowq: the packed-pair row quantizers against the one-group kernels")
     ap.add_argument("--no-flux", action="store_true", help="skip the FLUX DiT timing")
     ap.add_argument("--clocks-csv-dir", default=None,
                     help="also write the raw nvidia-smi clock samples of the timed region to this folder")
@@ -861,8 +879,8 @@ def main() -> int:
         if rank == 0:
             print(json.dumps(res), flush=True)
         return 0
-    if args.only in ("glue", "sdxl", "variants"):
-        fn = {"glue": bench_glue, "sdxl": bench_sdxl, "variants": bench_variants}[args.only]
+    if args.only in ("glue", "sdxl", "variants", "rowq"):
+        fn = {"glue": bench_glue, "sdxl": bench_sdxl, "variants": bench_variants, "rowq": bench_rowq}[args.only]
         res = fn(args, dev, peaks)
         if rank == 0:
             print(json.dumps(res), flush=True)
