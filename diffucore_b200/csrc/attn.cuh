@@ -732,6 +732,7 @@ attn_pair_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
       }
       if (!ok) for (int i = 0; i < 1000; ++i) __nanosleep(1000);
     }
+    __syncwarp();                  // whole warp again before the aligned cluster barrier
   } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA issuer (even CTA, lane 0)
     if (lane == 0 && rank == 0) {
@@ -796,6 +797,7 @@ attn_pair_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
       mma_commit_pair(&drain_bar);
       mbar_wait(&drain_bar, 0, nullptr, 1000000);
     }
+    __syncwarp();                  // whole warp again before the aligned cluster barrier
   } else {
     // ------------------------------------------------------------------ softmax warpgroups (both CTAs)
     const int wg = warp >> 2;                 // Q tile 0 or 1
