@@ -77,6 +77,20 @@ def _int8_requirements(policy):
     yield f"INT8 kernel library unavailable: {err}", not err
 
 
+def _fa2_requirements(policy):
+    """(message, satisfied) pairs for FA2-Turing under ``policy`` (_attention.py:117-121): its
+    package is sm75-only and not part of this build, so the first never holds; the rest are
+    listed as the reference lists them, so an explicit request names every unmet one."""
+    dev = torch.device(policy.device)
+    yield "flash_attn_turing is not installed (an sm75-only package, not part of the B200 build)", False
+    yield "device is not CUDA", dev.type == "cuda"
+    yield "GPU is not Turing; the kernel is compiled for sm_75 only", (
+        dev.type == "cuda" and torch.cuda.is_available() and torch.cuda.get_device_capability(dev) == (7, 5))
+    yield "compute dtype is not fp16", policy.compute_dtype == torch.float16
+    yield "incompatible with compile=True (the custom op graph-breaks in every block)", not getattr(
+        policy, "compile", False)
+
+
 def resolve_attention_backend(policy) -> str:
     """``"sdpa"`` as is; ``"auto"`` -> ``"sdpa"`` (FA2-Turing never applies on sm_100); an
     explicit ``"fa2_turing"`` / ``"int8_turing"`` raises on the first unmet requirement, so an
@@ -91,8 +105,8 @@ def resolve_attention_backend(policy) -> str:
         if failures:
             raise ValueError("policy.attention='int8_turing' can't run: " + "; ".join(failures))
         return "int8_turing"
-    raise ValueError("policy.attention='fa2_turing' can't run: flash_attn_turing is an sm75-only "
-                     "package and is not part of the B200 build")
+    failures = [msg for msg, ok in _fa2_requirements(policy) if not ok]
+    raise ValueError("policy.attention='fa2_turing' can't run: " + "; ".join(failures))
 
 
 def set_attention_backend(module: torch.nn.Module, backend: str) -> int:
