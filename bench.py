@@ -508,11 +508,67 @@ def flux_work(L: int, C: int = 3072, F: int = 12288, H: int = 24, Dh: int = 128,
     return {"linear_int8_ops": lin, "attn_int8_ops": att, "attn_bf16_ops": att}
 
 
-def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048)) -> dict:
+def _cpu_flux_baseline() -> dict:
+    """The reference's CPU path for one FLUX.1 step at 1024^2 on all host cores, extrapolated from
+    one block of each kind (a whole step takes minutes on a CPU): a full-width model (hidden 3072,
+    24 heads, RoPE 16/56/56) with one double- and one single-stream block, random bf16 weights,
+    block linears W8A8 with ConvRot 256, 512 text + 4096 image tokens, run by the FLUX runner with
+    the reference's torch ops (oracle/torch_ref.py FluxOps: torch._int_mm W8A8 linears, SDPA
+    attention; pinned to the reference's own FLUX output in tests/test_flux_host.py). Step =
+    19 x double block + 38 x single block + the rest of the forward (embedders, modulations,
+    final layer), each measured in the second of two forwards."""
+    import torch
+    from diffucore_b200 import _lib, flux
+    from oracle.torch_ref import FluxOps
+    threads = os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        t_build = time.perf_counter()
+        model = flux.build_flux(flux.FluxConfig(depth=1, depth_single_blocks=1), seed=0, device="cpu", group=256)
+        t_build = time.perf_counter() - t_build
+        lat, n_img = 128, 4096
+        runner = flux.FluxRunner(model, FLUX_TXT, n_img, device="cpu", attn_mode=_lib.MODE_REF, ops=FluxOps())
+        runner.set_positions(flux.img_ids(lat, lat, 2), flux.txt_ids(FLUX_TXT))
+        g = torch.Generator().manual_seed(1)
+        x = flux.patchify(torch.randn(1, 16, lat, lat, generator=g)).to(torch.bfloat16)[0]
+        txt = torch.randn(FLUX_TXT, 4096, generator=g).to(torch.bfloat16)
+        y = torch.randn(1, 768, generator=g).to(torch.bfloat16)
+        ts = torch.full((1,), 1.0, dtype=torch.bfloat16)
+        runner.forward(x, txt, ts, y)                                     # warm-up
+        secs = {"double": 0.0, "single": 0.0}
+
+        def timed(fn, key):
+            def wrapper(*a, **k):
+                t = time.perf_counter()
+                r = fn(*a, **k)
+                secs[key] += time.perf_counter() - t
+                return r
+            return wrapper
+
+        runner._double = timed(runner._double, "double")
+        runner._single = timed(runner._single, "single")
+        t0 = time.perf_counter()
+        v = runner.forward(x, txt, ts, y)
+        total = time.perf_counter() - t0
+    finally:
+        torch.set_num_threads(prev)
+    rest = total - secs["double"] - secs["single"]
+    step = 19 * secs["double"] + 38 * secs["single"] + rest
+    return {"value": step, "unit": "s/step", "cores": threads, "kind": "port", "extrapolated": True,
+            "s_per_double_block": secs["double"], "s_per_single_block": secs["single"], "s_rest_of_forward": rest,
+            "sample": "one double- and one single-stream block of the full-width FLUX.1 architecture at "
+                      "1024^2 (512 + 4096 tokens), measured; step = 19 x double + 38 x single + rest",
+            "note": "the reference's CPU path: torch-op W8A8 linears (torch._int_mm), SDPA attention, bf16",
+            "finite": bool(torch.isfinite(v).all()), "build_s": t_build, "cpu": _cpu_model()}
+
+
+def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048), cpu_baseline: bool = False) -> dict:
     """Seconds per Euler step of the FLUX.1-architecture DiT (random bf16 weights, block linears
     W8A8 with ConvRot group 256, INT8 attention in the reference's quant mode) at the given image
     sides: 1024 -> 512 text + 4096 image tokens, 2048 -> 512 + 16384. With world > 1 the tokens are
-    split over the ranks (Ulysses all-to-all around every attention)."""
+    split over the ranks (Ulysses all-to-all around every attention). With `cpu_baseline` (rank 0
+    of a one-GPU run) the 1024^2 entry also carries the reference's CPU path, extrapolated."""
     import torch
     import torch.distributed as dist
     from diffucore_b200 import _attention, _lib, flux
@@ -582,6 +638,11 @@ def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048)) -> dict:
         torch.cuda.empty_cache()
     del model
     torch.cuda.empty_cache()
+    if cpu_baseline and "1024px" in out:
+        try:
+            out["1024px"]["cpu_baseline"] = _cpu_flux_baseline()
+        except Exception as exc:                    # keep the GPU numbers; say why it is missing
+            out["1024px"]["cpu_baseline_error"] = f"{type(exc).__name__}: {exc}"[:300]
     return out
 
 
@@ -887,7 +948,7 @@ def main() -> int:
         return 0
     if args.only in ("gemm", "flux"):
         res = (bench_gemm(args, dev, peaks, cpu_baseline=rank == 0 and world == 1) if args.only == "gemm"
-               else bench_flux(args, world, rank, dev, peaks))
+               else bench_flux(args, world, rank, dev, peaks, cpu_baseline=rank == 0 and world == 1))
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:
@@ -943,7 +1004,8 @@ def main() -> int:
     if not args.no_extras and not args.no_flux:
         del plan, sets
         torch.cuda.empty_cache()
-        line["flux_dit"] = bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048) if world == 1 else (2048,))
+        line["flux_dit"] = bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048) if world == 1 else (2048,),
+                                      cpu_baseline=rank == 0 and world == 1)
         if world == 1:
             line["sdxl_unet"] = bench_sdxl(args, dev, peaks)
     if rank == 0:

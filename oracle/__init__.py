@@ -9,7 +9,9 @@ comment); it is pinned to the reference by the golden vectors under ``tests/gold
 running the reference's own torch-op code) and, for the attention prep, by the reference's CUDA
 prep kernels built from its source by ``oracle/build_ref.py`` into ``oracle/_ref/``.
 ``oracle/torch_ref.py`` restates the reference's torch-op (CPU) path of the W8A8 linear, pinned to
-the reference's config-1 output hashes; ``bench.py`` times it as config 1's CPU baseline.
+the reference's config-1 output hashes, and of each step of a FLUX block (``FluxOps``, pinned to
+the reference's own FLUX output); ``bench.py`` times them as the CPU baselines of config 1 and of
+the FLUX step.
 """
 
 from .oracle import *  # noqa: F401,F403

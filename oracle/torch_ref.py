@@ -73,3 +73,70 @@ def int8_linear(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, bias: torch
 def quantize_weight(w: torch.Tensor, group: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-output-channel int8 of a [N, K] weight after the rotation."""
     return quantize_rows(rotate(w.float(), group))
+
+
+class FluxOps:
+    """The reference's CPU path for each step the FLUX runner (``diffucore_b200.flux.FluxRunner``)
+    launches, so the runner can time the reference's arithmetic on the host cores: the FLUX block
+    math of src/diffucore/models/flux_dit.py (LayerNorm + modulation :282, QKNorm :129-151,
+    apply_rope :179-184, SDPA attention :187-190 — the attention dispatch's CPU path, gated
+    residuals :302-305, tanh-GELU MLP :236-239) with every block linear through the W8A8 torch-op
+    path above (``rotate`` + ``quantize_rows``, ``int_mm`` = torch._int_mm, ``rescale``). Each
+    op writes into the buffer layout the runner gives it (strided rows, column blocks, in-place
+    residuals). Used as the timed CPU baseline of the FLUX line in ``bench.py``; ``tests/`` pins
+    it to the reference's own FLUX output."""
+
+    @staticmethod
+    def _quant(x, group, q, s):
+        codes, scale = quantize_rows(rotate(x.float(), group))
+        q.copy_(codes)
+        s.copy_(scale)
+
+    def ln_mod_quant(self, x, shift, scale, group, q, s):
+        self._quant((1 + scale) * F.layer_norm(x, (x.shape[-1],), eps=1e-6) + shift, group, q, s)
+
+    def quant(self, x, group, q, s):
+        self._quant(x, group, q, s)
+
+    def quant_seg(self, recv, x2, group, q, s):
+        parts = list(recv.unbind(0)) + ([x2] if x2 is not None else [])
+        self._quant(torch.cat(parts, dim=1), group, q, s)
+
+    def gemm(self, q, sx, lin, out, *, ldo=None, gelu=0, gate=None, residual=None, col_block=0, block_stride=0):
+        y = rescale(int_mm(q, lin.weight), sx.float(), lin.scale.float(), lin.bias, out.dtype)
+        if gelu == 1:
+            y = F.gelu(y)
+        elif gelu == 2:
+            y = F.gelu(y, approximate="tanh")
+        if residual is not None:
+            y = residual + gate * y
+        M, N = y.shape
+        if col_block:
+            nb = N // col_block
+            out.as_strided((nb, M, col_block), (block_stride, ldo, 1)).copy_(y.view(M, nb, col_block).transpose(0, 1))
+        elif ldo is not None and out.dim() == 1:
+            out.as_strided((M, N), (ldo, 1)).copy_(y)
+        else:
+            out.copy_(y)
+
+    def qk_norm_rope(self, qkv, q0, k0, q1, k1, split_row, pe):
+        L = qkv.shape[0]
+
+        def rms(x, scale):
+            xf = x.float()
+            return (xf * torch.rsqrt(torch.mean(xf ** 2, dim=-1, keepdim=True) + 1e-6)).to(x.dtype) * scale
+
+        def rope(x):
+            xr = x.float().reshape(*x.shape[:-1], -1, 1, 2)
+            f = pe[:, None]
+            return (f[..., 0] * xr[..., 0] + f[..., 1] * xr[..., 1]).reshape(*x.shape).type_as(x)
+
+        for which, (s0, s1) in ((0, (q0, q1)), (1, (k0, k1))):
+            x = qkv[:, which]
+            lo = rms(x[:split_row], s0) if split_row > 0 else x[:0]
+            hi = rms(x[split_row:], s1) if split_row < L else x[:0]
+            qkv[:, which] = rope(torch.cat([lo, hi], dim=0))
+
+    def attention(self, q, k, v, out, sm_scale, backend, mode, workspace):
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), scale=sm_scale)
+        out.copy_(o.transpose(1, 2))

@@ -48,8 +48,9 @@ def _inputs(fx):
     return img, txt, y, torch.from_numpy(fx["img_ids"]), torch.from_numpy(fx["txt_ids"])
 
 
-def _run(model, img, txt, y, iid, tid, times, pg=None):
-    runner = flux.FluxRunner(model, txt.shape[0], img.shape[0], process_group=pg, device="cpu", ops=TorchOps())
+def _run(model, img, txt, y, iid, tid, times, pg=None, ops=None):
+    runner = flux.FluxRunner(model, txt.shape[0], img.shape[0], process_group=pg, device="cpu",
+                             ops=ops if ops is not None else TorchOps())
     runner.set_positions(iid, tid)
     t0, t1 = runner.img_rows
     r0 = runner.rows[0]
@@ -72,6 +73,20 @@ def test_runner_reproduces_reference_flux(group):
         assert got.shape == want.shape
         assert torch.isfinite(got).all()
         # every step rounds where the reference's torch ops round: the velocity is bit-identical
+        assert torch.equal(got.float(), want), (got.float() - want).abs().max().item()
+
+
+@pytest.mark.parametrize("group", [0, 256])
+def test_cpu_baseline_ops_reproduce_reference_flux(group):
+    """The ops bench.py times as the FLUX CPU baseline (oracle/torch_ref.py FluxOps: torch._int_mm
+    for the int32 products, as the reference's torch-op path) give the reference's own velocity
+    bit for bit, so that baseline runs the reference's arithmetic."""
+    from oracle.torch_ref import FluxOps
+    fx = _fixture()
+    img, txt, y, iid, tid = _inputs(fx)
+    outs, _ = _run(_model(group), img, txt, y, iid, tid, fx["times"], ops=FluxOps())
+    for i, got in enumerate(outs):
+        want = bits_to_torch(fx[f"v_g{group}_t{i}"], torch.bfloat16).float()
         assert torch.equal(got.float(), want), (got.float() - want).abs().max().item()
 
 
