@@ -646,11 +646,12 @@ def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048), cpu_baseline: 
     return out
 
 
-def bench_sdxl(args, dev, peaks, steps: int = 25) -> dict:
+def bench_sdxl(args, dev, peaks, steps: int = 25, cpu_baseline: bool = False) -> dict:
     """SDXL-architecture UNet, random fp16 weights, attention / FF linears W8A8,
     INT8 self-attention (head dim 64), CFG batch 2 at 1024^2 (latent 4 x 128 x 128, context
     [2, 77, 2048], adm [2, 2816]); Euler, 25 steps. s/step = CUDA-event time of a whole 25-step run
-    / 25 after a 3-step warm-up; int8 work per step counted by hooks on one forward."""
+    / 25 after a 3-step warm-up; int8 work per step counted by hooks on one forward. With
+    `cpu_baseline` (rank 0 of a one-GPU run) the reference's CPU path for one step sits beside it."""
     import torch
     from diffucore_b200 import _int8, unet
     t0 = time.perf_counter()
@@ -699,9 +700,42 @@ def bench_sdxl(args, dev, peaks, steps: int = 25) -> dict:
            "batch": "CFG 2", "latent": [4, 128, 128], "sampler": "euler", "steps": steps, "build_s": build_s,
            "s_per_step": s_step, "finite": bool(torch.isfinite(out).all()),
            "int8_work_per_step_T": {k: v / 1e12 for k, v in work.items()}}
+    if cpu_baseline:
+        del out
+        try:
+            res["cpu_baseline"] = _cpu_sdxl_baseline(model, x, ctx, y)
+        except Exception as exc:                    # keep the GPU numbers; say why it is missing
+            res["cpu_baseline_error"] = f"{type(exc).__name__}: {exc}"[:300]
     del model
     torch.cuda.empty_cache()
     return res
+
+
+def _cpu_sdxl_baseline(model, x, ctx, y) -> dict:
+    """The reference's CPU path for one Euler step of config 3 on all host cores: the same UNet
+    (the benchmark's own quantized weights) moved to the host in fp32, the reference's compute
+    dtype off the GPU, every W8A8 linear through the reference's torch-op forward
+    (oracle/torch_ref.py CpuInt8Linear: torch._int_mm) and self-attention through SDPA (the
+    attention dispatch's CPU path); one CFG-2 forward is one step's UNet work."""
+    import torch
+    from oracle.torch_ref import cpu_int8_linears_
+    threads = os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        model = model.to("cpu", torch.float32)
+        n = cpu_int8_linears_(model)
+        xc, cc, yc = (t.to("cpu", torch.float32) for t in (x, ctx, y))
+        with torch.no_grad():
+            t0 = time.perf_counter()
+            eps = model(xc.expand(2, -1, -1, -1), torch.full((2,), 500.0), cc, yc)
+            sec = time.perf_counter() - t0
+    finally:
+        torch.set_num_threads(prev)
+    return {"value": sec, "unit": "s/step", "cores": threads, "kind": "port",
+            "sample": f"one CFG-2 UNet forward (one Euler step's model work) at 1024^2, fp32, {n} W8A8 linears",
+            "note": "the reference's CPU path: torch-op W8A8 linears (torch._int_mm), SDPA attention",
+            "finite": bool(torch.isfinite(eps).all()), "cpu": _cpu_model()}
 
 
 def flux_op_breakdown(dev, side: int = 1024) -> dict:
@@ -1007,7 +1041,7 @@ def main() -> int:
         line["flux_dit"] = bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048) if world == 1 else (2048,),
                                       cpu_baseline=rank == 0 and world == 1)
         if world == 1:
-            line["sdxl_unet"] = bench_sdxl(args, dev, peaks)
+            line["sdxl_unet"] = bench_sdxl(args, dev, peaks, cpu_baseline=rank == 0)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -140,3 +140,29 @@ class FluxOps:
     def attention(self, q, k, v, out, sm_scale, backend, mode, workspace):
         o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), scale=sm_scale)
         out.copy_(o.transpose(1, 2))
+
+
+class CpuInt8Linear(torch.nn.Module):
+    """An ``Int8Linear``'s forward off the GPU, as the reference runs it there (its torch-op
+    branch, src/diffucore/models/_int8.py:158-170 with ``_fast()`` False): ``int8_linear`` above
+    on the layer's int8 weight, fp32 scales, bias and ConvRot group."""
+
+    def __init__(self, layer: torch.nn.Module):
+        super().__init__()
+        self.in_features, self.out_features, self.group = layer.in_features, layer.out_features, layer.group
+        self.register_buffer("wq", layer.weight.detach())
+        self.register_buffer("ws", layer.scale.detach().float())
+        self.bias = layer.bias
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return int8_linear(x, self.wq, self.ws, self.bias, self.group)
+
+
+def cpu_int8_linears_(model: torch.nn.Module) -> int:
+    """Replace every ``Int8Linear`` of ``model`` with :class:`CpuInt8Linear`; returns the count."""
+    names = [n for n, m in model.named_modules() if type(m).__name__ == "Int8Linear"]
+    for name in names:
+        head, _, leaf = name.rpartition(".")
+        parent = model.get_submodule(head) if head else model
+        setattr(parent, leaf, CpuInt8Linear(getattr(parent, leaf)))
+    return len(names)
