@@ -26,6 +26,7 @@ state. Weights are random-initialised (no checkpoint is needed for timing or par
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Sequence
 
@@ -412,10 +413,16 @@ class FluxRunner:
 
     ``process_group`` (size P) splits the L = n_txt + n_img tokens (text first) into P contiguous
     ranges of L / P rows; this rank owns ``rows`` = [r L/P, (r+1) L/P), of which the first
-    ``n_txt_local`` are text tokens. Requires L % P == 0 and num_heads % P == 0."""
+    ``n_txt_local`` are text tokens. Requires L % P == 0 and num_heads % P == 0.
+
+    ``overlap_exchange`` (default: the environment variable ``DC_FLUX_OVERLAP=1``; off otherwise)
+    starts a single-stream block's q/k/v all-to-all as soon as its qkv GEMM is done and runs the
+    block's MLP GEMM while it is in flight (the collective runs on the communicator's own stream
+    and the compute stream waits for it before QK-norm + RoPE), instead of exchanging after both
+    GEMMs. Same results either way."""
 
     def __init__(self, model: Flux, n_txt: int, n_img: int, *, process_group=None, device=None,
-                 attn_mode: int = _lib.MODE_REF, ops=None):
+                 attn_mode: int = _lib.MODE_REF, ops=None, overlap_exchange: bool | None = None):
         cfg = model.config
         self.model, self.cfg = model, cfg
         self.ops = ops if ops is not None else CudaOps()
@@ -440,6 +447,9 @@ class FluxRunner:
         self.i_loc = self.Lr - self.t_loc
         self.img_rows = (max(r0 - self.Lt, 0), max(r0 - self.Lt, 0) + self.i_loc)   # image-token indices owned
         self.attn_mode = int(attn_mode)
+        if overlap_exchange is None:
+            overlap_exchange = os.environ.get("DC_FLUX_OVERLAP") == "1"
+        self.overlap_exchange = bool(overlap_exchange) and P > 1
         self.sm_scale = self.D ** -0.5
         self._prepare_weights()
         self._allocate()
@@ -540,9 +550,11 @@ class FluxRunner:
     def _codes(self, rows: int, K: int, row0: int = 0) -> torch.Tensor:
         return self.codes[: self.Lr * K].view(self.Lr, K)[row0: row0 + rows]
 
-    def _exchange(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+    def _exchange(self, out: torch.Tensor, inp: torch.Tensor, async_op: bool = False):
+        """All-to-all of ``inp`` into ``out``; with ``async_op`` the collective's handle (the caller
+        waits on it before reading ``out`` or writing ``inp``)."""
         import torch.distributed as dist
-        dist.all_to_all_single(out, inp, group=self.pg)
+        return dist.all_to_all_single(out, inp, group=self.pg, async_op=async_op)
 
     def _qkv_views(self):
         r4 = self.recv.view(self.L, 3, self.Hp, self.D)
@@ -556,9 +568,10 @@ class FluxRunner:
         else:
             self.ops.gemm(codes, sx, lin, self.send[row0 * Wd:], ldo=Wd)
 
-    def _attend(self, blk, q0, k0, q1, k1, split_row, out4):
-        """Exchange q/k/v, norm + RoPE, attention into ``out4`` (1, L, Hp, D), exchange back."""
-        if self.P > 1:
+    def _attend(self, blk, q0, k0, q1, k1, split_row, out4, exchanged: bool = False):
+        """Exchange q/k/v (unless the caller already did), norm + RoPE, attention into ``out4``
+        (1, L, Hp, D), exchange back."""
+        if self.P > 1 and not exchanged:
             self._exchange(self.recv, self.send)
         r4, q, k, v = self._qkv_views()
         self.ops.qk_norm_rope(r4, q0, k0, q1, k1, split_row, self.pe)
@@ -608,13 +621,19 @@ class FluxRunner:
         mod = modv.view(3, C)  # shift, scale, gate
         ops.ln_mod_quant(X, mod[0], mod[1], g, self._codes(Lr, C), s)
         self._qkv_gemm(self._codes(Lr, C), s, w["qkv"], 0)
+        # The MLP half reads the same codes and writes Cbuf, which the q/k/v exchange (send ->
+        # recv) does not touch, so with overlap_exchange it runs while the exchange is in flight.
+        work = self._exchange(self.recv, self.send, async_op=True) if self.overlap_exchange else None
         ops.gemm(self._codes(Lr, C), s, w["mlp"], self.Cbuf[:, C:], gelu=_lib.GELU_TANH)
+        if work is not None:
+            work.wait()
         if self.P > 1:
             out4 = self.O.view(1, self.L, self.Hp, self.D)
         else:
             out4 = self.Cbuf[:, :C].view(Lr, self.H, self.D).unsqueeze(0)
         nrm = blk.norm
-        self._attend(blk, nrm.query_norm.scale, nrm.key_norm.scale, None, None, self.L, out4)
+        self._attend(blk, nrm.query_norm.scale, nrm.key_norm.scale, None, None, self.L, out4,
+                     exchanged=work is not None)
         if self.P > 1:
             ops.quant_seg(self.O_recv.view(self.P, Lr, self.Hp * self.D), self.Cbuf[:, C:], g,
                           self._codes(Lr, C + F_), s)

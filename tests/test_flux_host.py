@@ -48,9 +48,10 @@ def _inputs(fx):
     return img, txt, y, torch.from_numpy(fx["img_ids"]), torch.from_numpy(fx["txt_ids"])
 
 
-def _run(model, img, txt, y, iid, tid, times, pg=None, ops=None):
+def _run(model, img, txt, y, iid, tid, times, pg=None, ops=None, overlap=False):
     runner = flux.FluxRunner(model, txt.shape[0], img.shape[0], process_group=pg, device="cpu",
-                             ops=ops if ops is not None else TorchOps())
+                             ops=ops if ops is not None else TorchOps(), overlap_exchange=overlap)
+    assert runner.overlap_exchange == (overlap and pg is not None)
     runner.set_positions(iid, tid)
     t0, t1 = runner.img_rows
     r0 = runner.rows[0]
@@ -96,26 +97,29 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _ulysses_worker(rank: int, world: int, port: int, group: int, path: str) -> None:
+def _ulysses_worker(rank: int, world: int, port: int, group: int, path: str, overlap: bool = False) -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         torch.manual_seed(0)
         fx = _fixture()
         img, txt, y, iid, tid = _inputs(fx)
-        outs, (t0, t1) = _run(_model(group), img, txt, y, iid, tid, fx["times"], pg=dist.group.WORLD)
+        outs, (t0, t1) = _run(_model(group), img, txt, y, iid, tid, fx["times"], pg=dist.group.WORLD,
+                              overlap=overlap)
         torch.save({"outs": outs, "rows": (t0, t1)}, f"{path}.{rank}")
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("group", [0, 256])
-def test_ulysses_two_ranks_match_one_rank(tmp_path, group):
+@pytest.mark.parametrize("group,overlap", [(0, False), (256, False), (256, True)])
+def test_ulysses_two_ranks_match_one_rank(tmp_path, group, overlap):
+    """Also with the single-stream blocks' q/k/v exchange started before their MLP GEMM
+    (overlap_exchange): the asynchronous collective changes the schedule, not a bit."""
     fx = _fixture()
     img, txt, y, iid, tid = _inputs(fx)
     single, _ = _run(_model(group), img, txt, y, iid, tid, fx["times"])
     path = str(tmp_path / "out")
-    mp.start_processes(_ulysses_worker, args=(2, _free_port(), group, path), nprocs=2, join=True,
+    mp.start_processes(_ulysses_worker, args=(2, _free_port(), group, path, overlap), nprocs=2, join=True,
                        start_method="spawn")
     parts = [torch.load(f"{path}.{r}") for r in range(2)]
     # rank 0 owns 68 rows: the 40 text tokens and image tokens 0..27; rank 1 image tokens 28..95
