@@ -290,9 +290,12 @@ def bench_attention(args, world, mode_code, sets, plan, out, sampler=None):
     _barrier(world)
     clocks = sampler.stop() if sampler is not None else None
     total = start.elapsed_time(end)
-    prep = sum(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(args.steps))
-    main = sum(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(args.steps))
-    return {"total_ms": total, "prep_ms": prep / args.steps, "main_ms": main / args.steps, "clocks": clocks}
+    preps = [ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(args.steps)]
+    mains = [ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(args.steps)]
+    return {"total_ms": total, "prep_ms": sum(preps) / args.steps, "main_ms": sum(mains) / args.steps,
+            "median_ms": {"prep": statistics.median(preps), "main": statistics.median(mains),
+                          "step": statistics.median(a + b for a, b in zip(preps, mains))},
+            "clocks": clocks}
 
 
 def _e2e_serial(args, dev):
@@ -428,8 +431,9 @@ def bench_gemm(args, dev, peaks, cpu_baseline: bool = True):
         layer.matmul_quantized(q, s, torch.bfloat16)
         ev[3 * i + 2].record()
     torch.cuda.synchronize()
-    quant_ms = sum(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(steps)) / steps
-    gemm_ms = sum(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(steps)) / steps
+    quants = [ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(steps)]
+    gemms = [ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(steps)]
+    quant_ms, gemm_ms = sum(quants) / steps, sum(gemms) / steps
     # the library GEMM bar: cuBLASLt int8 GEMM (torch._int_mm, the reference's GEMM on this GPU)
     ev2 = _events(2)
     qa = [q for q, _ in qs]
@@ -452,6 +456,7 @@ def bench_gemm(args, dev, peaks, cpu_baseline: bool = True):
         "workload": "W8A8 linear, BASELINE config 1: M=4096, K=N=3072, bf16 in/out, bias, group 0",
         "value": GEMM_OPS / ((quant_ms + gemm_ms) * 1e-3) / 1e12, "unit": "TOPS",
         "ms_per_call": quant_ms + gemm_ms,
+        "median_ms": {"quantizer": statistics.median(quants), "gemm": statistics.median(gemms)},
         "gemm": {"ms": gemm_ms, "roofline": {"bound": "tensor", "achieved": tops, "peak": peak, "unit": "TOPS",
                                              "frac": tops / peak, "traffic": TRAFFIC_GEMM,
                                              "peak_source": f"2 x bf16_tflops ({peaks['source']})"}},
@@ -1008,7 +1013,7 @@ def main() -> int:
         "warmup": args.warmup, "ms_per_step": total_s * 1e3 / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 QK^T / bf16 PV",
         "data": "synthetic N(0,1) bf16, seeded", "config": CONFIG,
-        "prep_ms": t["prep_ms"], "attn_kernel_ms": t["main_ms"],
+        "prep_ms": t["prep_ms"], "attn_kernel_ms": t["main_ms"], "median_ms": t["median_ms"],
         "roofline": {"bound": "tensor", "achieved": main_tops, "peak": peak, "unit": "TOPS",
                      "frac": main_tops / peak, "traffic": TRAFFIC_ATTN,
                      "traffic_note": "bytes per launch, ncu dram__bytes_read + write (one capture)",
