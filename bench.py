@@ -8,8 +8,10 @@ One step = the whole attention call (Q/K quantization + the tcgen05 kernel) on o
 value = whole-job INT8 TOPS = 4*B*H*S^2*D ops per step * steps * N / max-over-ranks time.
 The same line carries the W8A8 GEMM of config 1 (M=4096, K=N=3072, bf16 out with bias), the
 activation quantizer's GB/s, the reference-mode attention, the roofline of the dominant kernel,
-the CPU baseline (the oracle port timed on this host), clocks and the end-to-end number through
-the public API with host buffers.
+clocks, the end-to-end number through the public API with host buffers, the FLUX.1 (configs 4
+and 5) and SDXL (config 3) steps, and beside each of them the reference's CPU path timed on this
+host's cores (config 1 and config 2 on rank 0 of a one-GPU run, the FLUX step extrapolated from
+one block of each kind, the SDXL step on one CFG forward).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
