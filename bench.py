@@ -811,8 +811,10 @@ def bench_variants(args, dev, peaks) -> dict:
     two-CTA GEMM (DC_GEMM_PAIR=1) against the one-CTA kernel on config 1 and the FLUX block
     shapes, the two-tile attention with dynamic MMA issue (DC_ATTN_ISSUE=dynamic) and the CTA-pair
     attention (DC_ATTN_KERNEL=pair) against the fixed-order one-CTA kernel on config 2 in both
-    quant modes, and the packed-pair rotated row quantizers (the default) against the one-group
-    kernels (DC_ROWQ_PAIR=0) on FLUX's rows. Times are device ms per call."""
+    quant modes, the key-range split attention (DC_ATTN_SPLIT=auto) against the default dispatch on
+    one rank's share of FLUX's attention at 8 GPUs (3 heads, 4608 and 16896 tokens), and the
+    packed-pair rotated row quantizers (the default) against the one-group kernels
+    (DC_ROWQ_PAIR=0) on FLUX's rows. Times are device ms per call."""
     import torch
     from diffucore_b200 import _lib, kernels
     g = torch.Generator(device=dev).manual_seed(11)
@@ -866,6 +868,27 @@ def bench_variants(args, dev, peaks) -> dict:
             ms = _time_env(fn, env, warm, steps)
             row[tag] = {"ms": round(ms, 4), "tops": round(ATTN_OPS / ms / 1e9, 1)}
         out[f"attention config2 {mode_name} (prep + main)"] = row
+    # one rank's share of FLUX's attention on 8 GPUs (3 heads): default dispatch vs key-range split
+    for L in (4608, 16896):
+        hs = 3
+        fsets = [tuple(torch.randn(1, L, hs, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+                 for _ in range(4)]
+        fo = torch.empty(1, L, hs, D, device=dev, dtype=torch.bfloat16)
+        nbytes = kernels.attn_workspace_layout(1, hs, L, L, D, _lib.MODE_REF)["total"]
+        fws = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+
+        def fn(i, fsets=fsets, fo=fo, fws=fws):
+            q, k, v = fsets[i % len(fsets)]
+            kernels.attn_int8(q, k, v, D ** -0.5, _lib.MODE_REF, workspace=fws, out=fo)
+
+        ops = 4 * hs * L * L * D
+        row = {}
+        for tag, env in (("default", {"DC_ATTN_SPLIT": None, "DC_ATTN_KERNEL": None}),
+                         ("split_auto", {"DC_ATTN_SPLIT": "auto", "DC_ATTN_KERNEL": None})):
+            ms = _time_env(fn, env, warm, steps)
+            row[tag] = {"ms": round(ms, 4), "tops": round(ops / ms / 1e9, 1)}
+        out[f"attention 3 heads x {L} (FLUX rank share at 8 GPUs, mode ref)"] = row
+        del fsets, fws
     out["row_quantizers"] = bench_rowq(args, dev, peaks)
     out["device_error"] = _lib.device_error()
     return out

@@ -55,6 +55,11 @@ _SIGNATURES = {
                                          _c_i64p, _c_i64p, ctypes.c_int, _c_p, ctypes.c_size_t, _c_p]),
     "dc_attn_int8_main": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64p,
                                          ctypes.c_float, ctypes.c_int, _c_p, _c_i64p, _c_p, ctypes.c_size_t, _c_p]),
+    "dc_attn_split_partials_size": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int,
+                                                   ctypes.POINTER(ctypes.c_size_t)]),
+    "dc_attn_int8_main_split": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64p,
+                                               ctypes.c_float, ctypes.c_int, _c_p, _c_i64p, _c_p, ctypes.c_size_t,
+                                               ctypes.c_int, _c_p, ctypes.c_size_t, _c_p]),
     "dc_attn_int8_fwd_noalloc": (ctypes.c_int, [_c_p, _c_p, _c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64,
                                                 _c_i64, _c_i64p, _c_i64p, _c_i64p, ctypes.c_float, ctypes.c_int,
                                                 _c_p, _c_i64p, _c_p]),

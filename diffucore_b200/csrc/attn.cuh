@@ -178,6 +178,12 @@ struct AttnParams {
   const float* k_scale;        // [B*H, Lk_pad / 64] per-block K scale
   void* o;                     // output, (B, Lq, H, D) with the strides below (elements)
   int64_t o_sb, o_sl, o_sh;
+  // Key-range split (attn_int8_kernel<..., SPLIT = true> only): CTA x of the grid takes Q pair
+  // x / nsplit and key tiles [s tiles_per_split, (s + 1) tiles_per_split) for s = x % nsplit, and
+  // writes unnormalized partials for attn_split_combine_kernel instead of O.
+  int nsplit = 1, tiles_per_split = 0, BH = 0;
+  float* part_o = nullptr;     // [nsplit, B*H, Lq_pad, D] fp32: sum of p v over the range
+  float2* part_ml = nullptr;   // [nsplit, B*H, Lq_pad]: (running max m, sum of p) over the range
 };
 
 template <int D>
@@ -301,7 +307,9 @@ __device__ __forceinline__ float scaled_max(int mx, float c) {
 // DYN: the MMA thread issues each Q tile's next group (P.V half, then the next Q.K^T) as soon as
 // its inputs are ready, polling the barriers of both tiles, instead of the fixed order tile 0 then
 // tile 1; the order within a tile, and so every result, is the same.
-template <int D, bool BF16, bool DYN = false>
+// SPLIT: this CTA covers one range of key tiles (see AttnParams) and leaves (O, m, l) of it for
+// attn_split_combine_kernel; everything inside the range runs as without the split.
+template <int D, bool BF16, bool DYN = false, bool SPLIT = false>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
                  const __grid_constant__ CUtensorMap tma_v, const AttnParams p) {
@@ -323,9 +331,12 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
   __shared__ int abort_flag;
 
   const int warp = warp_id(), lane = lane_id();
-  const int qpair = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int split = SPLIT ? static_cast<int>(blockIdx.x) % p.nsplit : 0;
+  const int qpair = SPLIT ? static_cast<int>(blockIdx.x) / p.nsplit : static_cast<int>(blockIdx.x);
+  const int h = blockIdx.y, b = blockIdx.z;
   const int bh = b * p.H + h;
-  const int n = p.n_ktiles;
+  const int j0 = SPLIT ? split * p.tiles_per_split : 0;               // first key tile of this CTA
+  const int n = SPLIT ? min(p.tiles_per_split, p.n_ktiles - j0) : p.n_ktiles;   // key tiles it covers
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
@@ -368,11 +379,11 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
         uint8_t* sk = sstage + st * SM::kStage;
         uint8_t* sv = sk + SM::kKTile;
         mbar_arrive_expect_tx(&k_full[st], SM::kKTile);
-        tma_load_2d(sk, &tma_k, &k_full[st], 0, bh * p.Lk_pad + j * kAttnBN);
+        tma_load_2d(sk, &tma_k, &k_full[st], 0, bh * p.Lk_pad + (j0 + j) * kAttnBN);
         mbar_arrive_expect_tx(&v_full[st], SM::kVTile);
 #pragma unroll
         for (int dh = 0; dh < D / 64; ++dh)
-          tma_load_4d(sv + dh * SM::kVHalf, &tma_v, &v_full[st], dh * 64, j * kAttnBN, h, b);
+          tma_load_4d(sv + dh * SM::kVHalf, &tma_v, &v_full[st], dh * 64, (j0 + j) * kAttnBN, h, b);
       }
       if (!ok) for (int i = 0; i < 1000; ++i) __nanosleep(1000);
     }
@@ -507,11 +518,13 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
     const int r_local = quarter * 32 + lane;
     const int qrow = qpair * kAttnRows + wg * kAttnBM + r_local;    // row in [0, Lq_pad)
     const float cq = __fmul_rn(p.q_scale[static_cast<int64_t>(bh) * p.Lq_pad + qrow], p.scale_log2);
-    const float* ksc = p.k_scale + static_cast<int64_t>(bh) * (p.Lk_pad / kAttnKBlk);
+    // K scales from this CTA's first key tile on (two 64-key blocks per tile)
+    const float* ksc = p.k_scale + static_cast<int64_t>(bh) * (p.Lk_pad / kAttnKBlk) + 2 * j0;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + wg * 128;
     const uint32_t o_addr = tmem + lane_off + kOCol + wg * D;
-    const int tail_valid = p.Lk - (n - 1) * kAttnBN;      // keys in the last tile (1..128)
+    const int tail_valid = p.Lk - (p.n_ktiles - 1) * kAttnBN;      // keys in the last tile (1..128)
+    const bool last_range = j0 + n == p.n_ktiles;                   // this CTA holds that tile
     float m = -INFINITY;
     float2 l2 = make_float2(0.f, 0.f);
     float ks_cur[2] = {ksc[0], ksc[1]};
@@ -546,7 +559,7 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
       ok = mbar_wait(&s_ready[wg], j & 1, abort);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      const bool tail = j == n - 1 && tail_valid < kAttnBN;
+      const bool tail = j == n - 1 && last_range && tail_valid < kAttnBN;
       tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
       tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
       tmem_wait_ld();
@@ -601,7 +614,25 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
       ok = mbar_wait(&pv_done[wg][1], (n - 1) & 1, abort);
       ok = __all_sync(0xffffffffu, ok);
     }
-    if (ok) {
+    if (SPLIT && ok) {
+      // this key range's unnormalized O, running max and sum, for attn_split_combine_kernel
+      tc_fence_after();
+      const bool row_ok = qrow < p.Lq;
+      const int64_t prow = (static_cast<int64_t>(split) * p.BH + bh) * p.Lq_pad + qrow;
+      float* dst = p.part_o + prow * D;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + c, o);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<uint4*>(dst + c + e) = make_uint4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+        }
+      }
+      if (row_ok) p.part_ml[prow] = make_float2(m, __fadd_rn(l2.x, l2.y));
+    } else if (ok) {
       tc_fence_after();
       const float inv = __fdiv_rn(1.0f, __fadd_rn(l2.x, l2.y));
       const bool row_ok = qrow < p.Lq;
@@ -631,6 +662,55 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
   if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// ----------------------------------------------------------------------------- split combine
+// One warp per query row: the key ranges' partials (O_s, m_s, l_s) of attn_int8_kernel<..., SPLIT>
+// merged as o = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s with M = max_s m_s (p was
+// 2^(s c - m_s) in range s), in split order, rounded once to the output dtype. D / 32 consecutive
+// columns per lane.
+template <int D, bool BF16>
+__global__ void __launch_bounds__(256)
+attn_split_combine_kernel(const float* __restrict__ part_o, const float2* __restrict__ part_ml, int nsplit, int BH,
+                          int H, int Lq, int Lq_pad, void* __restrict__ o, int64_t o_sb, int64_t o_sl, int64_t o_sh) {
+  constexpr int kPer = D / 32;
+  const int64_t wrow = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wrow >= static_cast<int64_t>(BH) * Lq) return;
+  const int bh = static_cast<int>(wrow / Lq), row = static_cast<int>(wrow % Lq);
+  const int64_t split_stride = static_cast<int64_t>(BH) * Lq_pad;      // partial rows per split
+  const int64_t base = static_cast<int64_t>(bh) * Lq_pad + row;
+  float mmax = -INFINITY;
+  for (int sp = 0; sp < nsplit; ++sp) mmax = fmaxf(mmax, part_ml[sp * split_stride + base].x);
+  float acc[kPer];
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
+  float den = 0.f;
+  for (int sp = 0; sp < nsplit; ++sp) {
+    const float2 ml = part_ml[sp * split_stride + base];
+    const float w = exp2f(ml.x - mmax);
+    den = __fmaf_rn(w, ml.y, den);
+    const float* src = part_o + (sp * split_stride + base) * D + lane * kPer;
+    float v[kPer];
+    if constexpr (kPer == 4) {
+      const float4 t = *reinterpret_cast<const float4*>(src);
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+      const float2 t = *reinterpret_cast<const float2*>(src);
+      v[0] = t.x; v[1] = t.y;
+    }
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) acc[e] = __fmaf_rn(w, v[e], acc[e]);
+  }
+  const float inv = __fdiv_rn(1.0f, den);
+  const int b = bh / H, h = bh % H;
+  uint16_t* dst = reinterpret_cast<uint16_t*>(o) + b * o_sb + static_cast<int64_t>(row) * o_sl + h * o_sh + lane * kPer;
+  if constexpr (kPer == 4) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(pack_p<BF16>(__fmul_rn(acc[0], inv), __fmul_rn(acc[1], inv)),
+                                                pack_p<BF16>(__fmul_rn(acc[2], inv), __fmul_rn(acc[3], inv)));
+  } else {
+    *reinterpret_cast<uint32_t*>(dst) = pack_p<BF16>(__fmul_rn(acc[0], inv), __fmul_rn(acc[1], inv));
   }
 }
 

@@ -693,6 +693,82 @@ int attn_main(const void* v, int64_t B, int64_t H, int64_t Lq, int64_t Lk, const
   return DC_OK;
 }
 
+// Key ranges of the split attention: tiles_per_split = ceil(n / nsplit) key tiles each, and as many
+// ranges as that takes (every range non-empty).
+inline void split_ranges(int64_t n_ktiles, int nsplit, int* tiles_per_split, int* ranges) {
+  const int64_t tps = (n_ktiles + nsplit - 1) / nsplit;
+  *tiles_per_split = static_cast<int>(tps);
+  *ranges = static_cast<int>((n_ktiles + tps - 1) / tps);
+}
+
+inline size_t split_partial_bytes(int64_t BH, int64_t Lq_pad, int64_t D, int nsplit) {
+  return static_cast<size_t>(nsplit) * static_cast<size_t>(BH * Lq_pad) * (static_cast<size_t>(D) * 4 + 8);
+}
+
+// attn_main with the keys divided into ranges (attn_int8_kernel<..., SPLIT = true>, two Q tiles per
+// CTA, one CTA per (Q pair, key range)) and the ranges merged by attn_split_combine_kernel. The
+// tensor maps are attn_main's.
+template <typename T, int D>
+int attn_main_split(const void* v, int64_t B, int64_t H, int64_t Lq, int64_t Lk, const int64_t* vs, float sm_scale,
+                    void* o, const int64_t* os, uint8_t* ws, const AttnLayout& a, int nsplit, void* partials,
+                    cudaStream_t st) {
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  using SM = dc::AttnSmem<D>;
+  CUtensorMap tq, tk, tv;
+  const CUtensorMapSwizzle qk_swz = D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(D), static_cast<uint64_t>(B * H * a.Lq_pad)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(D)};
+    const uint32_t box[2] = {static_cast<uint32_t>(D), dc::kAttnBM};
+    int r = make_map(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, ws + a.q_codes, dims, strides, box, qk_swz);
+    if (r) return r;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(D), static_cast<uint64_t>(B * H * a.Lk_pad)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(D)};
+    const uint32_t box[2] = {static_cast<uint32_t>(D), dc::kAttnBN};
+    int r = make_map(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, ws + a.k_codes, dims, strides, box, qk_swz);
+    if (r) return r;
+  }
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Lk), static_cast<uint64_t>(H),
+                              static_cast<uint64_t>(B)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(vs[1]) * 2, static_cast<uint64_t>(vs[2]) * 2,
+                                 static_cast<uint64_t>(vs[0]) * 2};
+    const uint32_t box[4] = {64, dc::kAttnBN, 1, 1};
+    int r = make_map(&tv, BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, v, dims,
+                     strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (r) return r;
+  }
+  dc::AttnParams p;
+  p.H = static_cast<int>(H); p.Lq = static_cast<int>(Lq); p.Lk = static_cast<int>(Lk);
+  p.Lq_pad = static_cast<int>(a.Lq_pad); p.Lk_pad = static_cast<int>(a.Lk_pad);
+  p.n_ktiles = static_cast<int>(a.Lk_pad / dc::kAttnBN);
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.q_scale = reinterpret_cast<const float*>(ws + a.q_scale);
+  p.k_scale = reinterpret_cast<const float*>(ws + a.k_scale);
+  p.o = o; p.o_sb = os[0]; p.o_sl = os[1]; p.o_sh = os[2];
+  int ranges = 1;
+  split_ranges(p.n_ktiles, nsplit, &p.tiles_per_split, &ranges);
+  p.nsplit = ranges;
+  p.BH = static_cast<int>(B * H);
+  p.part_o = static_cast<float*>(partials);
+  p.part_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(partials) +
+                                        static_cast<size_t>(ranges) * static_cast<size_t>(B * H * a.Lq_pad) * D * 4);
+  auto kernel = dc::attn_int8_kernel<D, BF16, false, true>;
+  int r = set_smem(kernel, SM::kDynamic);
+  if (r) return r;
+  dim3 grid(static_cast<unsigned>(a.Lq_pad / dc::kAttnRows * ranges), static_cast<unsigned>(H), static_cast<unsigned>(B));
+  kernel<<<grid, dc::kAttnThreads, SM::kDynamic, st>>>(tq, tk, tv, p);
+  DC_CHECK_LAUNCH("split attention launch");
+  const int64_t rows = B * H * Lq;
+  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);          // 8 warps (rows) per block
+  dc::attn_split_combine_kernel<D, BF16><<<blocks, 256, 0, st>>>(p.part_o, p.part_ml, ranges, p.BH, p.H, p.Lq,
+                                                                 p.Lq_pad, o, os[0], os[1], os[2]);
+  DC_CHECK_LAUNCH("split attention combine launch");
+  return DC_OK;
+}
+
 __global__ void selftest_wait_kernel(long long limit, int* status) {
   __shared__ __align__(8) uint64_t bar;
   __shared__ int abort_flag;
@@ -983,6 +1059,52 @@ int dc_attn_int8_prep(const void* q, const void* k, int dtype, int64_t B, int64_
                       size_t workspace_bytes, void* stream) {
   return attn_common(true, false, q, k, nullptr, dtype, B, H, Lq, Lk, D, q_strides, k_strides, nullptr, 1.0f, mode,
                      nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+int dc_attn_split_partials_size(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D, int nsplit, size_t* bytes) {
+  if (bytes == nullptr) return fail("attn_split_partials_size: null output");
+  if (int r = check_attn_args(DC_DTYPE_BF16, B, H, Lq, Lk, D, dc::kModeRef)) return r;
+  const AttnLayout a = attn_layout(B, H, Lq, Lk, D, dc::kModeRef);
+  const int64_t n = a.Lk_pad / dc::kAttnBN;
+  if (nsplit < 1 || nsplit > n) return fail("nsplit=%d must be in [1, %lld] (key tiles of 128)", nsplit, (long long)n);
+  int tps = 0, ranges = 0;
+  split_ranges(n, nsplit, &tps, &ranges);
+  *bytes = split_partial_bytes(B * H, a.Lq_pad, D, ranges);
+  return DC_OK;
+}
+
+int dc_attn_int8_main_split(const void* v, int dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D,
+                            const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
+                            void* workspace, size_t workspace_bytes, int nsplit, void* partials,
+                            size_t partial_bytes, void* stream) {
+  if (int r = check_attn_args(dtype, B, H, Lq, Lk, D, mode)) return r;
+  if (int r = check_strides(v, v_strides, "v")) return r;
+  if (int r = check_strides(o, o_strides, "o")) return r;
+  const AttnLayout a = attn_layout(B, H, Lq, Lk, D, mode);
+  if (workspace == nullptr || workspace_bytes < a.total)
+    return fail("attention workspace too small: need %zu bytes, got %zu", a.total, workspace_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail("attention workspace must be 256-byte aligned");
+  const int64_t n = a.Lk_pad / dc::kAttnBN;
+  if (nsplit < 1 || nsplit > n) return fail("nsplit=%d must be in [1, %lld] (key tiles of 128)", nsplit, (long long)n);
+  if (B * H > INT32_MAX / 2) return fail("split attention: B*H too large");
+  int tps = 0, ranges = 0;
+  split_ranges(n, nsplit, &tps, &ranges);
+  const size_t need = split_partial_bytes(B * H, a.Lq_pad, D, ranges);
+  if (partials == nullptr || partial_bytes < need)
+    return fail("split attention partials too small: need %zu bytes, got %zu", need, partial_bytes);
+  if (reinterpret_cast<uintptr_t>(partials) % 256 != 0) return fail("split attention partials must be 256-byte aligned");
+  if (int r = check_sm100()) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (dtype == DC_DTYPE_BF16)
+    return D == 128 ? attn_main_split<__nv_bfloat16, 128>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a,
+                                                          nsplit, partials, st)
+                    : attn_main_split<__nv_bfloat16, 64>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a,
+                                                         nsplit, partials, st);
+  return D == 128 ? attn_main_split<__half, 128>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a, nsplit,
+                                                 partials, st)
+                  : attn_main_split<__half, 64>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a, nsplit,
+                                                partials, st);
 }
 
 // ---------------------------------------------------------------------------------------------

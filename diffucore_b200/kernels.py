@@ -8,6 +8,7 @@ on sm_100 CUDA tensors only and raise for anything else; there is no CPU impleme
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -234,8 +235,14 @@ def attn_int8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float
               mode: int = _lib.MODE_REF, workspace: torch.Tensor | None = None,
               out: torch.Tensor | None = None) -> torch.Tensor:
     """INT8 attention over ``(B, L, H, D)`` q/k/v (any strides with stride(-1) == 1 and the
-    others multiples of 8) -> contiguous ``(B, Lq, H, D)`` in the input dtype."""
+    others multiples of 8) -> contiguous ``(B, Lq, H, D)`` in the input dtype. With the environment
+    variable ``DC_ATTN_SPLIT=auto`` (opt-in) shapes whose grid fills the GPU poorly run
+    :func:`attn_int8_split` with the key-range count :func:`choose_attn_split` picks."""
     B, Lq, Lk, H, D = _check_attn_inputs(q, k, v)
+    if os.environ.get("DC_ATTN_SPLIT") == "auto":
+        nsplit = choose_attn_split(B, H, Lq, Lk, torch.cuda.get_device_properties(q.device).multi_processor_count)
+        if nsplit > 1:
+            return attn_int8_split(q, k, v, sm_scale, nsplit, mode, workspace=workspace, out=out)
     lib = _lib.load()
     nbytes = ctypes.c_size_t(0)
     _lib.check(lib.dc_attn_workspace_size(B, H, Lq, Lk, D, int(mode), ctypes.byref(nbytes)))
@@ -248,6 +255,61 @@ def attn_int8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float
                                         _blhd_strides(q), _blhd_strides(k), _blhd_strides(v),
                                         float(sm_scale), int(mode), _ptr(out), _blhd_strides(out),
                                         _ptr(workspace), workspace.numel(), _stream(q)))
+    return out
+
+
+def choose_attn_split(B: int, H: int, Lq: int, Lk: int, sms: int = 148, max_split: int = 4) -> int:
+    """Key ranges for :func:`attn_int8_split` (1 = do not split), from a wave-count model: the
+    two-tile kernel runs ceil(Lq / 256) CTAs per head, each for its key tiles of 128 plus about one
+    tile's worth of prologue and epilogue; the single-tile kernel the unsplit call would otherwise
+    choose takes 0.61 of a two-tile CTA's time for 128 rows. A split is chosen only when it saves
+    at least 10 % against the better unsplit kernel (it adds the combine pass)."""
+    qctas = B * H * -(-Lq // 256)
+    n = -(-Lk // 128)
+
+    def waves(ctas: int) -> int:
+        return -(-ctas // sms)
+
+    def cost_split(r: int) -> float:
+        tps = -(-n // r)
+        ranges = -(-n // tps)
+        return waves(qctas * ranges) * (tps + 1)
+
+    unsplit = min(cost_split(1), 0.61 * waves(2 * qctas) * (n + 1))
+    best = min(range(1, min(max_split, n) + 1), key=lambda r: (cost_split(r), r))
+    return best if best > 1 and cost_split(best) < 0.9 * unsplit else 1
+
+
+def attn_split_partials_bytes(B: int, H: int, Lq: int, Lk: int, D: int, nsplit: int) -> int:
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(_lib.load().dc_attn_split_partials_size(B, H, Lq, Lk, D, int(nsplit), ctypes.byref(nbytes)))
+    return int(nbytes.value)
+
+
+def attn_int8_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float, nsplit: int,
+                    mode: int = _lib.MODE_REF, workspace: torch.Tensor | None = None,
+                    partials: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """:func:`attn_int8` with the keys divided into ``nsplit`` ranges (one CTA per 256 query rows and
+    key range, then a merge of the ranges): the same result to rounding, for grids of few heads."""
+    B, Lq, Lk, H, D = _check_attn_inputs(q, k, v)
+    lib = _lib.load()
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(lib.dc_attn_workspace_size(B, H, Lq, Lk, D, int(mode), ctypes.byref(nbytes)))
+    if workspace is None or workspace.numel() < nbytes.value:
+        workspace = torch.empty(nbytes.value, device=q.device, dtype=torch.uint8)
+    pbytes = attn_split_partials_bytes(B, H, Lq, Lk, D, nsplit)
+    if partials is None or partials.numel() < pbytes:
+        partials = torch.empty(pbytes, device=q.device, dtype=torch.uint8)
+    if out is None:
+        out = torch.empty(B, Lq, H, D, device=q.device, dtype=q.dtype)
+    with torch.cuda.device(q.device):
+        _lib.check(lib.dc_attn_int8_prep(_ptr(q), _ptr(k), _DTYPE[q.dtype], B, H, Lq, Lk, D, _blhd_strides(q),
+                                         _blhd_strides(k), int(mode), _ptr(workspace), workspace.numel(),
+                                         _stream(q)))
+        _lib.check(lib.dc_attn_int8_main_split(_ptr(v), _DTYPE[v.dtype], B, H, Lq, Lk, D, _blhd_strides(v),
+                                               float(sm_scale), int(mode), _ptr(out), _blhd_strides(out),
+                                               _ptr(workspace), workspace.numel(), int(nsplit), _ptr(partials),
+                                               partials.numel(), _stream(v)))
     return out
 
 

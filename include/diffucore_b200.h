@@ -174,6 +174,22 @@ int dc_attn_int8_main(const void* v, int dtype, int64_t B, int64_t H, int64_t Lq
                       const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* dc_attn_int8_main with the keys divided into ranges of ceil(n / nsplit) 128-key tiles (n = the
+ * key tiles of Lk; 1 <= nsplit <= n): one CTA per (256 query rows, key range) instead of per 256
+ * query rows, so a grid of few heads (a sequence-parallel rank's share) fills the GPU; each range
+ * leaves its unnormalized output, running max and sum in `partials` (caller-owned, 256-byte
+ * aligned, dc_attn_split_partials_size bytes) and a second kernel merges them and writes o.
+ * Same inputs, workspace (from dc_attn_int8_prep) and output as dc_attn_int8_main; results agree
+ * with it to rounding (the ranges are summed separately). Replaces the same reference call as
+ * dc_attn_int8_fwd (pybind `fwd`, src/diffucore/kernels/int8_attn_sm80.cu:460-497), whose kernel
+ * has no key split. */
+int dc_attn_split_partials_size(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D, int nsplit,
+                                size_t* bytes);
+int dc_attn_int8_main_split(const void* v, int dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D,
+                            const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
+                            void* workspace, size_t workspace_bytes, int nsplit, void* partials,
+                            size_t partial_bytes, void* stream);
+
 /* dc_attn_int8_fwd for callers that cannot allocate device memory — an application whose GPU
  * memory is all owned by its own pool and cannot give this library a workspace, or that runs where
  * cudaMalloc's implicit synchronization is not allowed. Same arguments and results as
