@@ -515,6 +515,27 @@ def flux_work(L: int, C: int = 3072, F: int = 12288, H: int = 24, Dh: int = 128,
     return {"linear_int8_ops": lin, "attn_int8_ops": att, "attn_bf16_ops": att}
 
 
+def _host_gib_available() -> float:
+    """Host memory this process can still use, GiB: the system's available memory, capped by a
+    cgroup (v2) limit when one is set."""
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:                                    # noqa: BLE001  no psutil: assume enough
+        return float("inf")
+    try:
+        limit = Path("/sys/fs/cgroup/memory.max").read_text().strip()
+        used = int(Path("/sys/fs/cgroup/memory.current").read_text().strip())
+        if limit != "max":
+            avail = min(avail, int(limit) - used)
+    except (OSError, ValueError):
+        pass
+    return avail / 2 ** 30
+
+
+HOST_GIB_FOR_CPU_BASELINES = 16.0      # measured peaks: ~6 GiB (SDXL in fp32), ~3 GiB (FLUX blocks)
+
+
 def _cpu_flux_baseline() -> dict:
     """The reference's CPU path for one FLUX.1 step at 1024^2 on all host cores, extrapolated from
     one block of each kind (a whole step takes minutes on a CPU): a full-width model (hidden 3072,
@@ -645,7 +666,9 @@ def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048), cpu_baseline: 
         torch.cuda.empty_cache()
     del model
     torch.cuda.empty_cache()
-    if cpu_baseline and "1024px" in out:
+    if cpu_baseline and "1024px" in out and _host_gib_available() < HOST_GIB_FOR_CPU_BASELINES:
+        out["1024px"]["cpu_baseline_error"] = f"skipped: under {HOST_GIB_FOR_CPU_BASELINES:.0f} GiB of host memory free"
+    elif cpu_baseline and "1024px" in out:
         try:
             out["1024px"]["cpu_baseline"] = _cpu_flux_baseline()
         except Exception as exc:                    # keep the GPU numbers; say why it is missing
@@ -707,7 +730,9 @@ def bench_sdxl(args, dev, peaks, steps: int = 25, cpu_baseline: bool = False) ->
            "batch": "CFG 2", "latent": [4, 128, 128], "sampler": "euler", "steps": steps, "build_s": build_s,
            "s_per_step": s_step, "finite": bool(torch.isfinite(out).all()),
            "int8_work_per_step_T": {k: v / 1e12 for k, v in work.items()}}
-    if cpu_baseline:
+    if cpu_baseline and _host_gib_available() < HOST_GIB_FOR_CPU_BASELINES:
+        res["cpu_baseline_error"] = f"skipped: under {HOST_GIB_FOR_CPU_BASELINES:.0f} GiB of host memory free"
+    elif cpu_baseline:
         del out
         try:
             res["cpu_baseline"] = _cpu_sdxl_baseline(model, x, ctx, y)
