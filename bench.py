@@ -1068,7 +1068,12 @@ def main() -> int:
                      "frac": main_tops / peak, "traffic": TRAFFIC_ATTN,
                      "traffic_note": "bytes per launch, ncu dram__bytes_read + write (one capture)",
                      "peak_source": f"2 x bf16_tflops ({peaks['source']}); nominal dense INT8 4500 TOPS",
-                     "kernel": "attn_int8_kernel<128, bf16>"},
+                     "kernel": "attn_int8_kernel<128, bf16>",
+                     # the kernel's own ceiling: QK^T at the INT8 peak plus P.V at the bf16 peak
+                     "mixed": {"target_ms": (ATTN_OPS / 2 / (peak * 1e12) + ATTN_OPS / 2 / (peaks["bf16_tflops"] * 1e12)) * 1e3,
+                               "frac": (ATTN_OPS / 2 / (peak * 1e12) + ATTN_OPS / 2 / (peaks["bf16_tflops"] * 1e12))
+                               * 1e3 / t["main_ms"],
+                               "note": "half the ops (QK^T) at the INT8 peak, half (P.V) at the bf16 peak"}},
         "clocks": t["clocks"],
         "gpu_launches": 3 * args.steps,
     }
