@@ -34,7 +34,7 @@ def rotate(t: torch.Tensor, group: int) -> torch.Tensor:
     if not group:
         return t
     rows = t.reshape(-1, t.shape[-1] // group, group)
-    return (rows @ hadamard(group)).reshape(t.shape)
+    return (rows @ hadamard(group).to(t.device)).reshape(t.shape)
 
 
 def quantize_rows(t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

@@ -14,28 +14,13 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from diffucore_b200._int8 import _quantize_rows, _rotate
+from oracle.torch_ref import FluxOps
 
 
-def _quant(x: torch.Tensor, group: int, q: torch.Tensor, s: torch.Tensor) -> None:
-    codes, scale = _quantize_rows(_rotate(x.float(), group))
-    q.copy_(codes)
-    s.copy_(scale)
-
-
-class TorchOps:
-    def ln_mod_quant(self, x, shift, scale, group, q, s):
-        y = (1 + scale) * F.layer_norm(x, (x.shape[-1],), eps=1e-6) + shift
-        _quant(y, group, q, s)
-
-    def quant(self, x, group, q, s):
-        _quant(x, group, q, s)
-
-    def quant_seg(self, recv, x2, group, q, s):
-        parts = list(recv.unbind(0))
-        if x2 is not None:
-            parts.append(x2)
-        _quant(torch.cat(parts, dim=1), group, q, s)
+class TorchOps(FluxOps):
+    """The reference's torch ops for every runner step (oracle/torch_ref.py ``FluxOps``) with the
+    int32 products formed in fp64 (exact at these sizes) instead of torch._int_mm, so the same
+    restatement runs on CPU and GPU tensors alike."""
 
     def gemm(self, q, sx, lin, out, *, ldo=None, gelu=0, gate=None, residual=None, col_block=0, block_stride=0):
         acc = (q.double() @ lin.weight.double().T).to(torch.int32)          # exact int32
@@ -58,27 +43,3 @@ class TorchOps:
             out.as_strided((M, N), (ldo, 1)).copy_(y)
         else:
             out.copy_(y)
-
-    def qk_norm_rope(self, qkv, q0, k0, q1, k1, split_row, pe):
-        L = qkv.shape[0]
-
-        def rms(x, scale):
-            xf = x.float()
-            rrms = torch.rsqrt(torch.mean(xf ** 2, dim=-1, keepdim=True) + 1e-6)
-            return (xf * rrms).to(x.dtype) * scale
-
-        def rope(x):
-            xr = x.float().reshape(*x.shape[:-1], -1, 1, 2)
-            f = pe[:, None]                                   # [L, 1, D/2, 2, 2]
-            out = f[..., 0] * xr[..., 0] + f[..., 1] * xr[..., 1]
-            return out.reshape(*x.shape).type_as(x)
-
-        for which, (s0, s1) in ((0, (q0, q1)), (1, (k0, k1))):
-            x = qkv[:, which]
-            lo = rms(x[:split_row], s0) if split_row > 0 else x[:0]
-            hi = rms(x[split_row:], s1) if split_row < L else x[:0]
-            qkv[:, which] = rope(torch.cat([lo, hi], dim=0))
-
-    def attention(self, q, k, v, out, sm_scale, backend, mode, workspace):
-        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), scale=sm_scale)
-        out.copy_(o.transpose(1, 2))
