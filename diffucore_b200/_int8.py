@@ -142,8 +142,10 @@ def fused_gemm_error(device) -> str:
 
 def scaled_mm(q: torch.Tensor, w: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor, dtype: torch.dtype):
     """``dtype(q @ w.T * sx[:, None] * sw)`` in one kernel, rounded exactly like :func:`rescale`
-    (_int8.py:266-276). Returns None only for dtypes the epilogue does not write."""
-    if dtype not in (torch.float16, torch.bfloat16):
+    (_int8.py:266-276). Returns None, as the reference does, when the fused GEMM cannot take the
+    call -- tensors off the GPU, or a dtype its epilogue does not write -- so the caller falls back
+    to :func:`int_mm` + :func:`rescale` (which have no CPU path here and say so)."""
+    if dtype not in (torch.float16, torch.bfloat16) or not q.is_cuda:
         return None
     return kernels.gemm_w8a8(q, w, sx, sw, None, dtype)
 

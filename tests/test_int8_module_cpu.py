@@ -135,3 +135,15 @@ def test_int8_embedding_adopts_a_comfy_table():
     assert isinstance(holder.embed_tokens, _int8.Int8Embedding)
     torch.testing.assert_close(holder.embed_tokens(ids), _int8.dequantize_weight(q, scale, 256)[ids],
                                rtol=1e-5, atol=1e-8)
+
+
+def test_scaled_mm_declines_off_the_gpu():
+    """The reference's scaled_mm returns None when its fused GEMM can't take the call (here: CPU
+    tensors, fp32 output); the int32 path it falls back to then refuses CPU tensors loudly."""
+    q = torch.zeros(32, 64, dtype=torch.int8)
+    w = torch.zeros(16, 64, dtype=torch.int8)
+    sx, sw = torch.ones(32), torch.ones(16)
+    assert _int8.scaled_mm(q, w, sx, sw, torch.float16) is None
+    assert _int8.scaled_mm(q, w, sx, sw, torch.float32) is None
+    with pytest.raises((RuntimeError, ValueError, TypeError)):
+        _int8.int_mm(q, w)
