@@ -2,9 +2,10 @@
 ``diffucore.models._int8`` (src/diffucore/models/_int8.py), re-implemented over the sm_100a
 kernels of this package.
 
-Forward-path functions (``quantize_activation``, ``int_mm``, ``rescale``, ``scaled_mm``,
-``int8_mlp``, ``Int8Linear.forward``) run on CUDA tensors through ``libdiffucore_b200.so`` and
-raise for anything else: there is no CPU or Triton path. Load-time helpers (``quantize_weight``
+Forward-path functions (``quantize_activation``, ``int_mm``, ``rescale``, ``int8_mlp``,
+``Int8Linear.forward``) run on CUDA tensors through ``libdiffucore_b200.so`` and raise for
+anything else: there is no CPU or Triton path. ``scaled_mm`` keeps the reference's contract and
+returns None for a call its fused GEMM cannot take (so off the GPU the caller's int32 path raises). Load-time helpers (``quantize_weight``
 on CPU, ``dequantize_weight``, LoRA's ``add_delta_``, the checkpoint plumbing) are tensor
 bookkeeping done once per layer and use torch ops, as the reference does.
 
