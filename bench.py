@@ -115,6 +115,17 @@ def _dist():
     return world, rank, local
 
 
+def _guarded(fn, *args, **kwargs) -> dict:
+    """fn(*args, **kwargs), or {"error": why} if it raises: a section after the headline that fails
+    (out of memory, a missing optional piece) is reported in the line instead of losing it."""
+    try:
+        return fn(*args, **kwargs)
+    except Exception as exc:                         # noqa: BLE001
+        import traceback
+        traceback.print_exc(file=sys.stderr)
+        return {"error": f"{type(exc).__name__}: {exc}"[:300]}
+
+
 def _max_over_ranks(x: float, world: int) -> float:
     if world == 1:
         return x
@@ -1078,15 +1089,17 @@ def main() -> int:
         "gpu_launches": 3 * args.steps,
     }
     if not args.no_extras:
-        ref_plan = kernels.AttnPlan(B, H, S, S, D, torch.bfloat16, _lib.MODE_REF, dev)
-        r = bench_attention(args, world, _lib.MODE_REF, sets, ref_plan, out)
-        line["ref_mode"] = {"value": ATTN_OPS / (r["total_ms"] / args.steps * 1e-3) / 1e12, "unit": "TOPS",
-                            "ms_per_step": r["total_ms"] / args.steps, "prep_ms": r["prep_ms"],
-                            "attn_kernel_ms": r["main_ms"]}
-        del ref_plan
-        line["w8a8_linear"] = bench_gemm(args, dev, peaks, cpu_baseline=rank == 0 and world == 1)
-        e2e = bench_e2e(args, dev)
-        if world > 1:
+        def ref_mode():
+            ref_plan = kernels.AttnPlan(B, H, S, S, D, torch.bfloat16, _lib.MODE_REF, dev)
+            r = bench_attention(args, world, _lib.MODE_REF, sets, ref_plan, out)
+            return {"value": ATTN_OPS / (r["total_ms"] / args.steps * 1e-3) / 1e12, "unit": "TOPS",
+                    "ms_per_step": r["total_ms"] / args.steps, "prep_ms": r["prep_ms"],
+                    "attn_kernel_ms": r["main_ms"]}
+
+        line["ref_mode"] = _guarded(ref_mode)
+        line["w8a8_linear"] = _guarded(bench_gemm, args, dev, peaks, cpu_baseline=rank == 0 and world == 1)
+        e2e = _guarded(bench_e2e, args, dev)
+        if world > 1 and "error" not in e2e:
             # every rank ran the same pipeline on its own GPU: whole-job rate over the slowest rank
             ms = _max_over_ranks(e2e["ms_per_step"] * 1e-3, world) * 1e3
             e2e.update(value=world * ATTN_OPS / (ms * 1e-3) / 1e12, ms_per_step=ms, ranks=world,
@@ -1094,14 +1107,15 @@ def main() -> int:
                        d2h_bytes_per_step=world * e2e["d2h_bytes_per_step"])
         line["e2e"] = e2e
         if rank == 0 and world == 1:
-            line["cpu_baseline"] = _cpu_baseline()
+            line["cpu_baseline"] = _guarded(_cpu_baseline)
     if not args.no_extras and not args.no_flux:
         del plan, sets
         torch.cuda.empty_cache()
-        line["flux_dit"] = bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048) if world == 1 else (2048,),
-                                      cpu_baseline=rank == 0 and world == 1)
+        line["flux_dit"] = _guarded(bench_flux, args, world, rank, dev, peaks,
+                                    sides=(1024, 2048) if world == 1 else (2048,), cpu_baseline=rank == 0 and world == 1)
         if world == 1:
-            line["sdxl_unet"] = bench_sdxl(args, dev, peaks, cpu_baseline=rank == 0)
+            torch.cuda.empty_cache()
+            line["sdxl_unet"] = _guarded(bench_sdxl, args, dev, peaks, cpu_baseline=rank == 0)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
