@@ -1,6 +1,7 @@
-"""bench.py's reference arm on CPU: the one JSON line the benchmark driver reads (same metric,
-unit, config and direction as the GPU arm; cpu_baseline and a zero-copy e2e), silence on ranks
-other than 0, and the warm-up floor. The GPU arm itself runs only on a B200."""
+"""bench.py on CPU: the reference arm's one JSON line (same metric, unit, config and direction as
+the GPU arm; cpu_baseline and a zero-copy e2e), silence on ranks other than 0, the warm-up floor,
+and the GPU arm's line assembly with its GPU sections faked (the sections themselves run only on a
+B200)."""
 
 from __future__ import annotations
 
@@ -60,3 +61,46 @@ def test_warmup_floor():
 @pytest.mark.parametrize("key", ["bf16_tflops", "hbm_gbs", "source"])
 def test_peaks_have_a_source(key):
     assert key in bench._peaks()
+
+
+def test_main_line_assembles_with_gpu_sections_faked(monkeypatch, capsys):
+    """The GPU arm's line assembly, with every GPU section replaced by a fake (the sections run on
+    a B200): one JSON line with the contract keys, the CPU baselines requested on rank 0 of a
+    one-GPU run, and a section that raises reported as an error entry instead of losing the line."""
+    import torch
+    real_device = torch.device
+    monkeypatch.setattr(torch, "device", lambda *a, **k: real_device("cpu"))
+    monkeypatch.setattr(torch.cuda, "set_device", lambda *a, **k: None)
+    monkeypatch.setattr(torch.cuda, "empty_cache", lambda: None)
+
+    def fake_attention(args, world, mode, sets, plan, out, sampler=None):
+        return {"total_ms": 0.27 * args.steps, "prep_ms": 0.027, "main_ms": 0.246,
+                "median_ms": {"prep": 0.027, "main": 0.246, "step": 0.273}, "clocks": {"sm_mhz": 1965.0}}
+
+    def failing(*a, **k):
+        raise RuntimeError("planted failure")
+
+    monkeypatch.setattr(bench, "bench_attention", fake_attention)
+    monkeypatch.setattr(bench, "bench_gemm", lambda args, dev, peaks, cpu_baseline=True: {"cpu": cpu_baseline})
+    monkeypatch.setattr(bench, "bench_e2e", failing)
+    monkeypatch.setattr(bench, "_cpu_baseline", lambda: {"value": 0.05, "cores": 1})
+    monkeypatch.setattr(bench, "bench_flux", lambda *a, **k: {"cpu": k["cpu_baseline"], "sides": list(k["sides"])})
+    monkeypatch.setattr(bench, "bench_sdxl", lambda *a, **k: {"cpu": k["cpu_baseline"]})
+    monkeypatch.setattr(bench, "ClockSampler", lambda *a, **k: None)
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--steps", "5", "--warmup", "3"])
+    for var in ("WORLD_SIZE", "RANK", "LOCAL_RANK"):
+        monkeypatch.delenv(var, raising=False)
+    assert bench.main() == 0
+    out = [ln for ln in capsys.readouterr().out.splitlines() if ln.strip()]
+    assert len(out) == 1
+    line = json.loads(out[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+                "vs_baseline", "dtype", "data", "config", "roofline", "clocks", "gpu_launches", "e2e", "cpu_baseline"):
+        assert key in line, key
+    assert line["n_gpus"] == 1 and line["steps"] == 5 and line["metric"] == bench.METRIC
+    assert abs(line["value"] - bench.ATTN_OPS * 5 / (0.27 * 5e-3) / 1e12) < 1e-6
+    roof = line["roofline"]
+    assert roof["frac"] == roof["achieved"] / roof["peak"] and 0 < roof["mixed"]["frac"] < 1
+    assert line["e2e"] == {"error": "RuntimeError: planted failure"}
+    assert line["w8a8_linear"] == {"cpu": True} and line["sdxl_unet"] == {"cpu": True}
+    assert line["flux_dit"] == {"cpu": True, "sides": [1024, 2048]}
