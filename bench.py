@@ -1,22 +1,28 @@
 #!/usr/bin/env python
 """Benchmark of the B200 INT8 hot path (BASELINE metric: INT8 TOPS of the W8A8 GEMM and the INT8
-attention vs the B200 dense INT8 peak).
+attention vs the dense INT8 peak; FLUX-DiT s/step at 1024^2 on 1/2/4/8 B200).
 
-Headline workload: INT8 flash attention, B=1, H=24, S=4608, D=128, bf16,
-non-causal, Q and K quantized per 64-token block (mode "block64"), softmax scale 1/sqrt(128).
-One step = the whole attention call (Q/K quantization + the tcgen05 kernel) on one batch.
-value = whole-job INT8 TOPS = 4*B*H*S^2*D ops per step * steps * N / max-over-ranks time.
-The same line carries the W8A8 GEMM of config 1 (M=4096, K=N=3072, bf16 out with bias), the
-activation quantizer's GB/s, the reference-mode attention, the roofline of the dominant kernel,
-clocks, the end-to-end number through the public API with host buffers, the FLUX.1 (configs 4
-and 5) and SDXL (config 3) steps, and beside each of them the reference's CPU path timed on this
-host's cores (config 1 and config 2 on rank 0 of a one-GPU run, the FLUX step extrapolated from
-one block of each kind, the SDXL step on one CFG forward).
+Headline workload (and config 5's Ulysses split at N > 1): a FLUX.1-schnell-
+architecture DiT (19 double + 38 single blocks, hidden 3072, 24 heads of 128, RoPE 16/56/56) with
+seeded random bf16 weights, block linears W8A8 (ConvRot 256) and INT8 attention in the reference's
+quant mode, at 1024^2 (512 text + 4096 image tokens), batch 1. One step = one Euler flow-matching
+step (one forward, CUDA-graph replayed, plus the latent update); the 4-step schedule repeats, the
+latent restarting every 4 steps. At N > 1 the tokens are split over the ranks (Ulysses: an NCCL
+all-to-all of q/k/v before and of the output after every attention), so the total work is fixed
+("strong" scaling); value = s/step of the slowest rank. At N > 1 rank 0 also runs the same seeded
+4-step sample on one GPU and the line reports the N-rank result's distance from it.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+The line also carries the dominant kernel's roofline (the W8A8 GEMMs of one forward, timed per
+launch with CUDA events) with the other hot kernels beside it (attention in the FLUX step and on
+BASELINE config 2, the config-1 W8A8 linear and quantizer), the end-to-end step through the
+public API with host copies, clocks, and compact extras (the 2048^2 step, the SDXL UNet step, the
+reference's own GPU path timed on this GPU). The full per-section details go to stderr as one JSON
+line ("bench details: ..."). Beside the GPU number (rank 0 of a one-GPU run) the reference's CPU
+path for the same step runs on this host's cores, extrapolated from one block of each kind.
 
-N > 1 runs under torch.distributed.run, one rank per GPU, each rank its own batch (weak scaling,
-no data-path collective: attention batches are independent).
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--only SECTION]
+
+N > 1 runs under torch.distributed.run, one rank per GPU.
 """
 
 from __future__ import annotations
@@ -37,15 +43,19 @@ B, H, S, D = 1, 24, 4608, 128
 ATTN_OPS = 4 * B * H * S * S * D                     # QK^T (int8) + PV (bf16), 2 ops per MAC
 GEMM_M, GEMM_N, GEMM_K = 4096, 3072, 3072
 GEMM_OPS = 2 * GEMM_M * GEMM_N * GEMM_K
-METRIC = "INT8 TOPS, INT8 flash attention (BASELINE config 2: B=1, H=24, S=4608, D=128, bf16)"
+ATTN_METRIC = "INT8 TOPS, INT8 flash attention (BASELINE config 2: B=1, H=24, S=4608, D=128, bf16)"
+FLUX_SIDE = 1024
+METRIC = ("FLUX.1-architecture DiT s/step at 1024^2 (512 text + 4096 image tokens, W8A8 linears, INT8 attention), "
+          "Ulysses over the N GPUs")
 # DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, one capture of each
-# kernel on these workloads): attention main kernel, W8A8 GEMM, activation quantizer.
+# kernel on these workloads): attention main kernel (config 2), W8A8 GEMM (config 1), activation
+# quantizer (config 1).
 TRAFFIC_ATTN = 60.71e6
 TRAFFIC_GEMM = 22.09e6
 TRAFFIC_QUANT = 25.21e6
-CONFIG = {"workload": "int8_flash_attention_config2", "batch": B, "heads": H, "seq_len": S, "head_dim": D,
-          "quant": "per-64-token-block Q and K (block64)", "causal": False,
-          "l2": "4 rotating input sets (4 x 85 MB > 126 MB L2)", "parallelism": "replicas (weak scaling)"}
+ATTN_CONFIG = {"workload": "int8_flash_attention_config2", "batch": B, "heads": H, "seq_len": S, "head_dim": D,
+               "quant": "per-64-token-block Q and K (block64)", "causal": False,
+               "l2": "4 rotating input sets (4 x 85 MB > 126 MB L2)"}
 
 
 def _peaks() -> dict:
@@ -215,38 +225,36 @@ def _cpu_sdpa_heads(heads: int, threads: int) -> float:
 
 
 def run_reference(args) -> int:
-    """The reference arm: the reference's own CPU path for this call on this host's cores, rank 0
-    only. Off the GPU the reference's attention dispatch runs torch's
-    scaled_dot_product_attention (src/diffucore/models/_attention.py:278; it has no CPU int8
-    attention), so each step is that call in bf16 over a bounded number of config 2's heads. The
-    oracle's restatement of the int8 arithmetic is timed once beside it (`int8_port`)."""
+    """The reference arm: the reference's CPU path for the headline step on this host's cores, rank
+    0 only (the other ranks of a torchrun launch exit without work). Off the GPU the reference runs
+    its torch-op W8A8 linears (torch._int_mm) and SDPA attention in bf16; `oracle/torch_ref.py`'s
+    FluxOps restates those ops and the FLUX runner drives them (pinned bit for bit to the
+    reference's own FLUX on the tiny fixture, tests/test_flux_host.py). A whole step takes minutes
+    on a CPU, so each timed step is one bounded sample: one forward of the full-width model with one
+    double- and one single-stream block at 1024^2, extrapolated to the 19 + 38 blocks of FLUX.1
+    (value = 19 x double + 38 x single + the rest of the forward, in s/step); ms_per_step is the
+    sample's own wall time."""
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
-    threads = os.cpu_count() or 1
-    _cpu_sdpa_heads(1, threads)
-    t1 = _cpu_sdpa_heads(1, threads)
-    total_budget = 150.0
-    per_step = max(0.05, min(2.0, total_budget / max(1, args.steps + args.warmup)))
-    heads = int(max(1, min(H, per_step / max(t1, 1e-4))))
+    step = CpuFluxStep()
     for _ in range(args.warmup):
-        _cpu_sdpa_heads(heads, threads)
-    secs = 0.0
-    for _ in range(args.steps):
-        secs += _cpu_sdpa_heads(heads, threads)
-    ops = args.steps * ATTN_OPS * heads / H
-    value = ops / secs / 1e12
-    sample = (f"torch CPU scaled_dot_product_attention (the reference's fallback), bf16, {heads} of {H} heads "
-              f"x {S} queries x {S} keys, D={D} per step")
-    t8, ops8 = _cpu_attention_sample(64, threads)
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic N(0,1), seeded", "config": CONFIG,
-            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample,
-                             "cpu": _cpu_model()},
-            "int8_port": {"value": ops8 / t8 / 1e12, "unit": "TOPS",
-                          "sample": f"oracle int8 attention (block64), 1 head x 64 query rows x {S} keys"},
-            "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        step.sample()
+    samples = [step.sample() for _ in range(args.steps)]
+    value = statistics.mean(x["s_step"] for x in samples)
+    wall = statistics.mean(x["wall_s"] for x in samples)
+    sample = ("one forward of a full-width FLUX.1 (hidden 3072, 24 heads) with one double- and one single-stream "
+              "block at 1024^2 (512 + 4096 tokens) per step, extrapolated to 19 + 38 blocks; torch-op W8A8 "
+              "linears (torch._int_mm), SDPA attention, bf16")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "s/step", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1e3,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16 (torch-op int8 GEMMs)",
+            "data": "synthetic: seeded random weights, N(0,1) latent and text", "config": flux_config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": "s/step", "cores": step.threads, "kind": "port",
+                             "sample": sample, "extrapolated": True, "cpu": _cpu_model(),
+                             "s_per_double_block": statistics.mean(x["double"] for x in samples),
+                             "s_per_single_block": statistics.mean(x["single"] for x in samples),
+                             "s_rest_of_forward": statistics.mean(x["rest"] for x in samples)},
+            "e2e": {"value": value, "unit": "s/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -547,59 +555,79 @@ def _host_gib_available() -> float:
 HOST_GIB_FOR_CPU_BASELINES = 16.0      # measured peaks: ~6 GiB (SDXL in fp32), ~3 GiB (FLUX blocks)
 
 
-def _cpu_flux_baseline() -> dict:
+class CpuFluxStep:
     """The reference's CPU path for one FLUX.1 step at 1024^2 on all host cores, extrapolated from
     one block of each kind (a whole step takes minutes on a CPU): a full-width model (hidden 3072,
     24 heads, RoPE 16/56/56) with one double- and one single-stream block, random bf16 weights,
     block linears W8A8 with ConvRot 256, 512 text + 4096 image tokens, run by the FLUX runner with
     the reference's torch ops (oracle/torch_ref.py FluxOps: torch._int_mm W8A8 linears, SDPA
-    attention; pinned to the reference's own FLUX output in tests/test_flux_host.py). Step =
-    19 x double block + 38 x single block + the rest of the forward (embedders, modulations,
-    final layer), each measured in the second of two forwards."""
-    import torch
-    from diffucore_b200 import _lib, flux
-    from oracle.torch_ref import FluxOps
-    threads = os.cpu_count() or 1
-    prev = torch.get_num_threads()
-    torch.set_num_threads(threads)
-    try:
-        t_build = time.perf_counter()
-        model = flux.build_flux(flux.FluxConfig(depth=1, depth_single_blocks=1), seed=0, device="cpu", group=256)
-        t_build = time.perf_counter() - t_build
-        lat, n_img = 128, 4096
-        runner = flux.FluxRunner(model, FLUX_TXT, n_img, device="cpu", attn_mode=_lib.MODE_REF, ops=FluxOps())
-        runner.set_positions(flux.img_ids(lat, lat, 2), flux.txt_ids(FLUX_TXT))
-        g = torch.Generator().manual_seed(1)
-        x = flux.patchify(torch.randn(1, 16, lat, lat, generator=g)).to(torch.bfloat16)[0]
-        txt = torch.randn(FLUX_TXT, 4096, generator=g).to(torch.bfloat16)
-        y = torch.randn(1, 768, generator=g).to(torch.bfloat16)
-        ts = torch.full((1,), 1.0, dtype=torch.bfloat16)
-        runner.forward(x, txt, ts, y)                                     # warm-up
-        secs = {"double": 0.0, "single": 0.0}
+    attention; pinned to the reference's own FLUX output in tests/test_flux_host.py). One
+    :meth:`sample` = one forward of that model; step = 19 x double block + 38 x single block + the
+    rest of the forward (embedders, modulations, final layer)."""
+
+    def __init__(self, threads: int | None = None):
+        import torch
+        from diffucore_b200 import _lib, flux
+        from oracle.torch_ref import FluxOps
+        self.threads = threads or os.cpu_count() or 1
+        prev = torch.get_num_threads()
+        torch.set_num_threads(self.threads)
+        try:
+            t0 = time.perf_counter()
+            model = flux.build_flux(flux.FluxConfig(depth=1, depth_single_blocks=1), seed=0, device="cpu", group=256)
+            self.build_s = time.perf_counter() - t0
+            lat = FLUX_SIDE // 8
+            n_img = (lat // 2) ** 2
+            self.runner = flux.FluxRunner(model, FLUX_TXT, n_img, device="cpu", attn_mode=_lib.MODE_REF, ops=FluxOps())
+            self.runner.set_positions(flux.img_ids(lat, lat, 2), flux.txt_ids(FLUX_TXT))
+            g = torch.Generator().manual_seed(1)
+            self.x = flux.patchify(torch.randn(1, 16, lat, lat, generator=g)).to(torch.bfloat16)[0]
+            self.txt = torch.randn(FLUX_TXT, 4096, generator=g).to(torch.bfloat16)
+            self.y = torch.randn(1, 768, generator=g).to(torch.bfloat16)
+            self.ts = torch.full((1,), 1.0, dtype=torch.bfloat16)
+        finally:
+            torch.set_num_threads(prev)
+        self.secs = {"double": 0.0, "single": 0.0}
 
         def timed(fn, key):
             def wrapper(*a, **k):
                 t = time.perf_counter()
                 r = fn(*a, **k)
-                secs[key] += time.perf_counter() - t
+                self.secs[key] += time.perf_counter() - t
                 return r
             return wrapper
 
-        runner._double = timed(runner._double, "double")
-        runner._single = timed(runner._single, "single")
-        t0 = time.perf_counter()
-        v = runner.forward(x, txt, ts, y)
-        total = time.perf_counter() - t0
-    finally:
-        torch.set_num_threads(prev)
-    rest = total - secs["double"] - secs["single"]
-    step = 19 * secs["double"] + 38 * secs["single"] + rest
-    return {"value": step, "unit": "s/step", "cores": threads, "kind": "port", "extrapolated": True,
-            "s_per_double_block": secs["double"], "s_per_single_block": secs["single"], "s_rest_of_forward": rest,
+        self.runner._double = timed(self.runner._double, "double")
+        self.runner._single = timed(self.runner._single, "single")
+
+    def sample(self) -> dict:
+        import torch
+        prev = torch.get_num_threads()
+        torch.set_num_threads(self.threads)
+        try:
+            self.secs.update(double=0.0, single=0.0)
+            t0 = time.perf_counter()
+            v = self.runner.forward(self.x, self.txt, self.ts, self.y)
+            total = time.perf_counter() - t0
+        finally:
+            torch.set_num_threads(prev)
+        rest = total - self.secs["double"] - self.secs["single"]
+        return {"s_step": 19 * self.secs["double"] + 38 * self.secs["single"] + rest, "wall_s": total,
+                "double": self.secs["double"], "single": self.secs["single"], "rest": rest,
+                "finite": bool(torch.isfinite(v).all())}
+
+
+def _cpu_flux_baseline() -> dict:
+    """:class:`CpuFluxStep` after one warm-up forward, one measured forward (rank 0 of a one-GPU run)."""
+    step = CpuFluxStep()
+    step.sample()
+    r = step.sample()
+    return {"value": r["s_step"], "unit": "s/step", "cores": step.threads, "kind": "port", "extrapolated": True,
+            "s_per_double_block": r["double"], "s_per_single_block": r["single"], "s_rest_of_forward": r["rest"],
             "sample": "one double- and one single-stream block of the full-width FLUX.1 architecture at "
                       "1024^2 (512 + 4096 tokens), measured; step = 19 x double + 38 x single + rest",
             "note": "the reference's CPU path: torch-op W8A8 linears (torch._int_mm), SDPA attention, bf16",
-            "finite": bool(torch.isfinite(v).all()), "build_s": t_build, "cpu": _cpu_model()}
+            "finite": r["finite"], "build_s": step.build_s, "cpu": _cpu_model()}
 
 
 def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048), cpu_baseline: bool = False) -> dict:
@@ -812,6 +840,346 @@ def flux_op_breakdown(dev, side: int = 1024) -> dict:
             "other_ms_torch_ops": round(total - sum(r["ms"] for r in rows), 3), "ops": rows}
 
 
+# ─── the headline: FLUX.1 step at 1024^2, Ulysses over the N ranks ──────────────────────
+
+def flux_config(world: int) -> dict:
+    return {"workload": "flux1_schnell_arch_dit_1024px", "tokens": FLUX_TXT + (FLUX_SIDE // 16) ** 2,
+            "image_tokens": (FLUX_SIDE // 16) ** 2, "text_tokens": FLUX_TXT, "batch": 1, "hidden": 3072, "heads": 24,
+            "head_dim": 128, "blocks": "19 double + 38 single", "linears": "W8A8, ConvRot 256",
+            "attention": "INT8, reference quant mode", "sampler": "euler, 4-step schedule repeated, shift 1",
+            "parallelism": (f"ulysses x{world}: tokens split over the ranks, NCCL all-to-all of q/k/v and of the "
+                            "attention output around every attention" if world > 1 else "one GPU"),
+            "l2": "each step streams ~12 GB of weights (> 126 MB L2)", "graph": "one CUDA graph per forward"}
+
+
+# GPU kernel launches of this library per runner op (attention in the reference's quant mode:
+# k_stats, k_sum, K codes, Q codes, main kernel; one more with the key-range split's combine)
+_LAUNCHES_PER_OP = {"gemm": 1, "quant": 1, "ln_mod_quant": 1, "quant_seg": 1, "qk_norm_rope": 1, "attention": 5}
+
+
+class _EulerSteps:
+    """Euler flow-matching steps (src/diffucore/pipelines/_flux.py:226-236) on a captured forward:
+    step i uses sigma index i % n of the n-step schedule and the latent restarts at x0 whenever
+    i % n == 0, so any number of steps repeats the same sample. Allocation-free per step."""
+
+    def __init__(self, fn, x0, sigmas):
+        import torch
+        self.fn, self.x0 = fn, x0
+        self.x, self.tmp = x0.clone(), torch.empty_like(x0)
+        self.n = len(sigmas) - 1
+        self.ts = [torch.full((1,), float(sigmas[i]), device=x0.device, dtype=x0.dtype) for i in range(self.n)]
+        self.dts = [(sigmas[i + 1] - sigmas[i]).to(x0.dtype).to(x0.device) for i in range(self.n)]
+
+    def step(self, i: int) -> None:
+        import torch
+        k = i % self.n
+        if k == 0:
+            self.x.copy_(self.x0)
+        v = self.fn(self.x, self.ts[k])
+        torch.mul(v, self.dts[k], out=self.tmp)          # x + (sigma_next - sigma) v, rounded as euler_sample
+        self.x.add_(self.tmp)
+
+
+def _gather_rows(x, world: int):
+    """This rank's rows of x [n, C] gathered on every rank in rank order (ranks may own different
+    row counts)."""
+    import torch
+    import torch.distributed as dist
+    n = torch.tensor([x.shape[0]], device=x.device, dtype=torch.int64)
+    counts = [torch.zeros_like(n) for _ in range(world)]
+    dist.all_gather(counts, n)
+    mx = max(int(c) for c in counts)
+    buf = torch.zeros(mx, x.shape[1], device=x.device, dtype=x.dtype)
+    buf[: x.shape[0]] = x
+    bufs = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(bufs, buf)
+    return torch.cat([b[: int(c)] for b, c in zip(bufs, counts)])
+
+
+def bench_flux_headline(args, world, rank, dev, peaks, sampler) -> dict:
+    """The headline step (see the module docstring). Returns the line's headline keys plus
+    `details` (everything measured)."""
+    import torch
+    import torch.distributed as dist
+    from diffucore_b200 import _attention, _lib, flux
+    t0 = time.perf_counter()
+    model = flux.build_flux(flux.FluxConfig(), seed=0, device=dev, group=256)
+    _attention.set_attention_backend(model, "int8_turing")
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    pg = dist.group.WORLD if world > 1 else None
+    lat = FLUX_SIDE // 8
+    n_img = (lat // 2) ** 2
+    L = FLUX_TXT + n_img
+    runner = flux.FluxRunner(model, FLUX_TXT, n_img, process_group=pg, device=dev, attn_mode=_lib.MODE_REF)
+    runner.set_positions(flux.img_ids(lat, lat, 2, device=dev), flux.txt_ids(FLUX_TXT, device=dev))
+    g = torch.Generator(device=dev).manual_seed(1)
+    x_all = flux.patchify(torch.randn(1, 16, lat, lat, generator=g, device=dev)).to(torch.bfloat16)[0]
+    txt_all = torch.randn(FLUX_TXT, 4096, generator=g, device=dev).to(torch.bfloat16)
+    y = torch.randn(1, 768, generator=g, device=dev).to(torch.bfloat16)
+    i0, i1 = runner.img_rows
+    r0 = runner.rows[0]
+    x0, txt = x_all[i0:i1].contiguous(), txt_all[r0: r0 + runner.t_loc].contiguous()
+    sigmas = flux.flow_schedule(FLUX_STEPS, 1.0)
+    graph = flux.FluxGraph(runner, x0, txt, y)
+    eul = _EulerSteps(graph, x0, sigmas)
+    for i in range(args.warmup):
+        eul.step(i)
+    torch.cuda.synchronize()
+    # clock soak: the same steps right before the timed region, sampled with it (a fixed count, so
+    # every rank runs the same collectives)
+    sampler.start()
+    for i in range(16):
+        eul.step(i)
+    torch.cuda.synchronize()
+    start, end = _events(2)
+    _barrier(world)
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(args.steps):
+        eul.step(i)
+    end.record()
+    torch.cuda.synchronize()
+    _barrier(world)
+    clocks = sampler.stop()
+    s_step = _max_over_ranks(start.elapsed_time(end) * 1e-3 / args.steps, world)
+    finite = bool(torch.isfinite(eul.x).all())
+
+    # end to end through the public API: every step copies its latent and text rows in from pinned
+    # host memory and its updated latent back (same stream: each copy-in follows the last copy-out)
+    hx0, hx = x0.cpu().pin_memory(), x0.cpu().pin_memory()
+    htxt = txt.cpu().pin_memory()
+    dx, dtxt = torch.empty_like(x0), torch.empty_like(txt)
+    tmp = torch.empty_like(x0)
+
+    def e2e_step(i):
+        k = i % eul.n
+        dx.copy_(hx0 if k == 0 else hx, non_blocking=True)
+        dtxt.copy_(htxt, non_blocking=True)
+        v = graph(dx, eul.ts[k], dtxt)
+        torch.mul(v, eul.dts[k], out=tmp)
+        dx.add_(tmp)
+        hx.copy_(dx, non_blocking=True)
+
+    for i in range(max(3, args.warmup)):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    es, ee = _events(2)
+    _barrier(world)
+    torch.cuda.synchronize()
+    es.record()
+    for i in range(args.steps):
+        e2e_step(i)
+    ee.record()
+    torch.cuda.synchronize()
+    _barrier(world)
+    e2e_s = _max_over_ranks(es.elapsed_time(ee) * 1e-3 / args.steps, world)
+    bi = (x0.numel() + txt.numel()) * 2
+    bo = x0.numel() * 2
+    if world > 1:
+        tot = torch.tensor([bi, bo], device=dev, dtype=torch.float64)
+        dist.all_reduce(tot)
+        bi, bo = int(tot[0].item()), int(tot[1].item())
+    e2e = {"value": e2e_s, "unit": "s/step", "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
+           "steps": args.steps, "api": "FluxGraph (captured FluxRunner.forward) + Euler update, pinned host latent "
+                                     "and text rows in, updated latent out, every step"}
+
+    # per-op GPU time of one eager forward (events around every runner op): the dominant kernel's
+    # achieved rate, the other hot kernels, and the launches per forward
+    timed = flux.TimedOps()
+    runner.ops = timed
+    t_mid = torch.full((1,), 0.5, device=dev, dtype=torch.bfloat16)
+    runner.forward(x0, txt, t_mid, y)
+    rows = timed.summary()
+    runner.ops = flux.CudaOps()
+    gemm_ops = gemm_ms = attn_ms = 0.0
+    attn_calls = 0
+    launches = 0
+    for r in rows:
+        kind = r["op"].split(" ")[0]
+        launches += _LAUNCHES_PER_OP.get(kind, 1) * r["calls"]
+        if kind == "gemm":
+            dims = dict(t.split("=") for t in r["op"].split(" ")[1:4])
+            gemm_ops += 2.0 * int(dims["M"]) * int(dims["N"]) * int(dims["K"]) * r["calls"]
+            gemm_ms += r["ms"]
+        elif kind == "attention":
+            attn_ms += r["ms"]
+            attn_calls += r["calls"]
+    hp = 24 // world
+    attn_ops = attn_calls * 4.0 * L * L * 128 * hp
+    peak = _int8_peak_tops(peaks)
+    gemm_tops = gemm_ops / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
+    attn_tops = attn_ops / (attn_ms * 1e-3) / 1e12 if attn_ms else None
+    w = flux_work(L)
+    compute_s = (w["linear_int8_ops"] + w["attn_int8_ops"]) / (peak * 1e12) + w["attn_bf16_ops"] / (peaks["bf16_tflops"] * 1e12)
+    roof = compute_s / world
+    a2a = 0.0
+    if world > 1:
+        Lr = L // world
+        a2a = 57 * (Lr * 3 * 3072 + Lr * 3072) * 2 * (world - 1) / world / 770e9    # bytes sent per rank / peer copy
+        roof = max(roof, a2a)
+
+    # parity of the N-rank sample with one GPU's (rank 0 runs the same seeded 4-step sample alone)
+    parity = None
+    if world > 1:
+        xs = flux.euler_sample(graph, x0, txt, y, sigmas)
+        full = _gather_rows(xs, world)
+        if rank == 0:
+            one = flux.FluxRunner(model, FLUX_TXT, n_img, process_group=None, device=dev, attn_mode=_lib.MODE_REF)
+            one.set_positions(flux.img_ids(lat, lat, 2, device=dev), flux.txt_ids(FLUX_TXT, device=dev))
+            ref = flux.euler_sample(one, x_all, txt_all, y, sigmas).float()
+            got = full.float()
+            cos = torch.nn.functional.cosine_similarity(got.flatten().double(), ref.flatten().double(), dim=0).item()
+            mad = (got - ref).abs().max().item()
+            parity = {"max_abs": mad, "cos": cos, "ok": bool(mad <= 2e-2 and cos >= 0.999),
+                      "what": "final latent of the seeded 4-step sample, N ranks vs one GPU (tolerance max-abs 2e-2, "
+                              "cos 0.999)"}
+            del one, ref
+        _barrier(world)
+    del graph, runner
+    torch.cuda.empty_cache()
+    head = {
+        "value": s_step, "ms_per_step": s_step * 1e3, "clocks": clocks, "e2e": e2e,
+        "gpu_launches": launches * args.steps,
+        "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": peak, "unit": "TOPS",
+                     "frac": gemm_tops / peak if gemm_tops else None, "traffic": None,
+                     "kernel": "gemm_w8a8_kernel: every W8A8 block GEMM of one forward, ops-weighted (events per launch)",
+                     "peak_source": f"2 x bf16_tflops ({peaks['source']}); nominal dense INT8 4500 TOPS",
+                     "step": {"roofline_s": roof, "frac": roof / s_step,
+                              "note": "int8 ops at the INT8 peak + P.V at the bf16 peak, / N; at N > 1 at least the "
+                                      "all-to-all bytes at 770 GB/s"}},
+        "parity_vs_1gpu": parity, "finite": finite,
+    }
+    head["roofline"]["kernels"] = {"attention_flux": {
+        "achieved": attn_tops, "frac": attn_tops / peak if attn_tops else None, "unit": "TOPS",
+        "ms_per_call": attn_ms / max(attn_calls, 1), "heads_per_gpu": hp, "tokens": L}}
+    head["details"] = {"build_s": build_s, "op_breakdown": rows, "roofline_s_per_step": roof,
+                       "a2a_s_per_step_at_770GBps": a2a, "work_per_step_T": {k: v / 1e12 for k, v in w.items()}}
+    return head
+
+
+def bench_reference_gpu(args, dev) -> dict:
+    """The reference's own GPU path for the two hot calls, timed on this GPU beside this library's:
+    its W8A8 linear (Triton `_rot_quant_kernel` -> torch._int_mm (cuBLASLt) -> Triton
+    `_rescale_kernel`, src/diffucore/models/_int8.py:158-168, :299-323) on config 1, and its INT8
+    attention `fwd` (src/diffucore/kernels/int8_attn_sm80.cu:460-497, mma.sync, fp16 only) on
+    config 2's shape in fp16, against this library's attention in the same (reference) quant mode.
+    Both are the reference's unchanged code, staged / compiled into oracle/_ref/ by the checker
+    recipe (oracle/build_ref.py); they are bars to compare with, never part of this library."""
+    import torch
+    from oracle import build_ref
+    from diffucore_b200 import _int8, _lib, kernels
+    out = {}
+    warm, steps = max(3, args.warmup), max(10, min(args.steps, 50))
+
+    def timeit(fn):
+        for i in range(warm):
+            fn(i)
+        torch.cuda.synchronize()
+        s, e = _events(2)
+        _cpu_runahead()
+        s.record()
+        for i in range(steps):
+            fn(i)
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / steps
+
+    if build_ref.int8_available():
+        ref = build_ref.load_int8()
+        g = torch.Generator().manual_seed(0)
+        lin = torch.nn.Linear(GEMM_K, GEMM_N, bias=True).to(torch.bfloat16)
+        with torch.no_grad():
+            lin.weight.copy_((torch.randn(GEMM_N, GEMM_K, generator=g) * 0.02).to(torch.bfloat16))
+            lin.bias.copy_((torch.randn(GEMM_N, generator=g) * 0.01).to(torch.bfloat16))
+        lin = lin.to(dev)
+        ref_layer = ref.Int8Linear.from_linear(lin, group=0)
+        our_layer = _int8.Int8Linear.from_linear(lin, group=0)
+        xs = [torch.randn(GEMM_M, GEMM_K, generator=g).to(torch.bfloat16).to(dev) for _ in range(6)]
+        with torch.no_grad():
+            same = bool(torch.equal(ref_layer(xs[0]), our_layer(xs[0])))
+            ref_ms = timeit(lambda i: ref_layer(xs[i % 6]))
+            our_ms = timeit(lambda i: our_layer(xs[i % 6]))
+        out["w8a8_linear_config1"] = {"reference_ms": ref_ms, "ours_ms": our_ms, "speedup": ref_ms / our_ms,
+                                      "outputs_bit_identical": same,
+                                      "reference_path": "Triton _rot_quant_kernel + torch._int_mm + Triton _rescale_kernel"}
+        del xs
+    else:
+        out["w8a8_linear_config1"] = {"error": "reference _int8.py not staged in oracle/_ref"}
+    if build_ref.available():
+        mod = build_ref.load()
+        g = torch.Generator(device=dev).manual_seed(2)
+        sets = [tuple(torch.randn(B, S, H, D, generator=g, device=dev).half() for _ in range(3)) for _ in range(4)]
+        plan = kernels.AttnPlan(B, H, S, S, D, torch.float16, _lib.MODE_REF, dev)
+        o = torch.empty(B, S, H, D, device=dev, dtype=torch.float16)
+        ref_ms = timeit(lambda i: mod.fwd(*sets[i % 4], D ** -0.5))
+        our_ms = timeit(lambda i: plan(*sets[i % 4], o, D ** -0.5))
+        a = mod.fwd(*sets[0], D ** -0.5).float().reshape(B, S, H, D)
+        plan(*sets[0], o, D ** -0.5)
+        cos = torch.nn.functional.cosine_similarity(a.flatten().double(), o.float().flatten().double(), dim=0).item()
+        out["attention_config2_fp16_ref_mode"] = {
+            "reference_ms": ref_ms, "ours_ms": our_ms, "speedup": ref_ms / our_ms,
+            "reference_tops": ATTN_OPS / ref_ms / 1e9, "ours_tops": ATTN_OPS / our_ms / 1e9,
+            "max_abs_vs_reference": (a - o.float()).abs().max().item(), "cos_vs_reference": cos,
+            "reference_path": "int8_attn_sm80.cu fwd (mma.sync, compute_100 build)"}
+        del sets
+    else:
+        out["attention_config2_fp16_ref_mode"] = {"error": "reference attention not built in oracle/_ref"}
+    torch.cuda.empty_cache()
+    return out
+
+
+def bench_attention_config2(args, world, dev, peaks) -> dict:
+    """BASELINE config 2 on its own: the INT8 attention (B=1, H=24, S=4608, D=128, bf16, block64),
+    Q/K quantization + main kernel per step over rotating input sets; TOPS of the whole call and of
+    the main kernel, its roofline against the INT8 peak and against its mixed ceiling (QK^T at the
+    INT8 peak plus P.V at the bf16 peak), the reference quant mode's step, and the same call end to
+    end with host buffers."""
+    import torch
+    from diffucore_b200 import _lib, kernels
+    g = torch.Generator().manual_seed(0)
+    sets = []
+    for _ in range(4):
+        q, k, v = (torch.randn(B, H, S, D, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+        sets.append((q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)))   # (B, L, H, D) views of bhld
+    out = torch.empty(B, S, H, D, device=dev, dtype=torch.bfloat16)
+    plan = kernels.AttnPlan(B, H, S, S, D, torch.bfloat16, _lib.MODE_BLOCK64, dev)
+    t = bench_attention(args, world, _lib.MODE_BLOCK64, sets, plan, out)
+    ref_plan = kernels.AttnPlan(B, H, S, S, D, torch.bfloat16, _lib.MODE_REF, dev)
+    r = bench_attention(args, world, _lib.MODE_REF, sets, ref_plan, out)
+    peak = _int8_peak_tops(peaks)
+    main_tops = ATTN_OPS / (t["main_ms"] * 1e-3) / 1e12
+    mixed_ms = (ATTN_OPS / 2 / (peak * 1e12) + ATTN_OPS / 2 / (peaks["bf16_tflops"] * 1e12)) * 1e3
+    del sets, plan, ref_plan
+    torch.cuda.empty_cache()
+    return {"metric": ATTN_METRIC, "config": ATTN_CONFIG,
+            "tops": ATTN_OPS / (t["total_ms"] / args.steps * 1e-3) / 1e12, "ms_per_call": t["total_ms"] / args.steps,
+            "prep_ms": t["prep_ms"], "kernel_ms": t["main_ms"], "median_ms": t["median_ms"],
+            "roofline": {"bound": "tensor", "achieved": main_tops, "peak": peak, "unit": "TOPS", "frac": main_tops / peak,
+                         "traffic": TRAFFIC_ATTN, "kernel": "attn_int8_kernel<128, bf16>",
+                         "mixed": {"target_ms": mixed_ms, "frac": mixed_ms / t["main_ms"]}},
+            "ref_mode": {"ms_per_call": r["total_ms"] / args.steps, "prep_ms": r["prep_ms"], "kernel_ms": r["main_ms"],
+                         "tops": ATTN_OPS / (r["total_ms"] / args.steps * 1e-3) / 1e12},
+            "e2e": _guarded(bench_e2e, args, dev)}
+
+
+def _compact(d, keys):
+    """A few rounded numbers of a section dict (the long form goes to stderr)."""
+    if not isinstance(d, dict):
+        return d
+    if "error" in d:
+        return {"error": d["error"]}
+    out = {}
+    for k in keys:
+        v = d
+        for part in k.split("."):
+            v = v.get(part) if isinstance(v, dict) else None
+        if isinstance(v, float):
+            v = round(v, 5 if abs(v) < 1 else 2)
+        out[k.replace(".", "_")] = v
+    return out
+
+
 def _time_env(fn, env: dict, warmup: int, steps: int) -> float:
     """Mean device ms of fn(i) over `steps` calls with the environment variables in `env` set
     (the library reads its kernel switches at each call); restores the environment."""
@@ -844,13 +1212,13 @@ def _time_env(fn, env: dict, warmup: int, steps: int) -> float:
 
 def bench_variants(args, dev, peaks) -> dict:
     """Kernel variants side by side on the same inputs (rotating sets larger than L2): the
-    two-CTA GEMM (DC_GEMM_PAIR=1) against the one-CTA kernel on config 1 and the FLUX block
-    shapes, the two-tile attention with dynamic MMA issue (DC_ATTN_ISSUE=dynamic) and the CTA-pair
-    attention (DC_ATTN_KERNEL=pair) against the fixed-order one-CTA kernel on config 2 in both
-    quant modes, the key-range split attention (DC_ATTN_SPLIT=auto) against the default dispatch on
-    one rank's share of FLUX's attention at 8 GPUs (3 heads, 4608 and 16896 tokens), and the
-    packed-pair rotated row quantizers (the default) against the one-group kernels
-    (DC_ROWQ_PAIR=0) on FLUX's rows. Times are device ms per call."""
+    two-CTA GEMM (the default for wide GEMMs of 512+ rows without GELU) against the one-CTA kernel
+    (DC_GEMM_PAIR=0) on config 1 and the FLUX block shapes, the two-tile attention against the
+    single-tile one on config 2 in both quant modes, the key-range split attention (the default
+    routing) against the unsplit dispatch (DC_ATTN_SPLIT=0) on one rank's share of FLUX's attention
+    at 8 GPUs (3 heads, 4608 and 16896 tokens), and the packed-pair rotated row quantizers (the
+    default) against the one-group kernels (DC_ROWQ_PAIR=0) on FLUX's rows. Times are device ms per
+    call."""
     import torch
     from diffucore_b200 import _lib, kernels
     g = torch.Generator(device=dev).manual_seed(11)
@@ -878,7 +1246,7 @@ def bench_variants(args, dev, peaks) -> dict:
 
         ops = 2 * M * N * K
         row = {}
-        for tag, env in (("one_cta", {"DC_GEMM_PAIR": None}), ("pair", {"DC_GEMM_PAIR": "1"})):
+        for tag, env in (("one_cta", {"DC_GEMM_PAIR": "0"}), ("pair", {"DC_GEMM_PAIR": "1"})):
             ms = _time_env(fn, env, warm, steps)
             row[tag] = {"ms": round(ms, 4), "tops": round(ops / ms / 1e9, 1), "frac": round(ops / ms / 1e9 / peak, 3)}
         out[name] = row
@@ -897,10 +1265,8 @@ def bench_variants(args, dev, peaks) -> dict:
             plan(q, k, v, o, D ** -0.5)
 
         row = {}
-        for tag, env in (("fixed", {"DC_ATTN_KERNEL": "two_tile", "DC_ATTN_ISSUE": None}),
-                         ("dynamic", {"DC_ATTN_KERNEL": "two_tile", "DC_ATTN_ISSUE": "dynamic"}),
-                         ("single_tile", {"DC_ATTN_KERNEL": "single_tile", "DC_ATTN_ISSUE": None}),
-                         ("cta_pair", {"DC_ATTN_KERNEL": "pair", "DC_ATTN_ISSUE": None})):
+        for tag, env in (("two_tile", {"DC_ATTN_KERNEL": "two_tile"}),
+                         ("single_tile", {"DC_ATTN_KERNEL": "single_tile"})):
             ms = _time_env(fn, env, warm, steps)
             row[tag] = {"ms": round(ms, 4), "tops": round(ATTN_OPS / ms / 1e9, 1)}
         out[f"attention config2 {mode_name} (prep + main)"] = row
@@ -919,8 +1285,8 @@ def bench_variants(args, dev, peaks) -> dict:
 
         ops = 4 * hs * L * L * D
         row = {}
-        for tag, env in (("default", {"DC_ATTN_SPLIT": None, "DC_ATTN_KERNEL": None}),
-                         ("split_auto", {"DC_ATTN_SPLIT": "auto", "DC_ATTN_KERNEL": None})):
+        for tag, env in (("unsplit", {"DC_ATTN_SPLIT": "0", "DC_ATTN_KERNEL": None}),
+                         ("default", {"DC_ATTN_SPLIT": None, "DC_ATTN_KERNEL": None})):
             ms = _time_env(fn, env, warm, steps)
             row[tag] = {"ms": round(ms, 4), "tops": round(ops / ms / 1e9, 1)}
         out[f"attention 3 heads x {L} (FLUX rank share at 8 GPUs, mode ref)"] = row
@@ -1010,15 +1376,16 @@ def bench_glue(args, dev, peaks) -> dict:
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
-    ap.add_argument("--no-extras", action="store_true", help="headline attention only (for profiling)")
-    ap.add_argument("--only", default="all", choices=("all", "gemm", "flux", "glue", "sdxl", "variants", "rowq"),
-                    help="gemm / flux: time only the config-1 W8A8 linear / the FLUX DiT; glue: the FLUX glue "
-                         "kernels; sdxl: the UNet; variants: opt-in kernel variants against the defaults; "
-                         "rowq: the packed-pair row quantizers against the one-group kernels")
-    ap.add_argument("--no-flux", action="store_true", help="skip the FLUX DiT timing")
+    ap.add_argument("--no-extras", action="store_true", help="the headline FLUX step only")
+    ap.add_argument("--only", default="all",
+                    choices=("all", "attention", "gemm", "flux", "glue", "sdxl", "variants", "rowq", "refgpu"),
+                    help="attention: BASELINE config 2 alone; gemm / flux: the config-1 W8A8 linear / the FLUX DiT "
+                         "at 1024^2 and 2048^2; glue: the FLUX glue kernels; sdxl: the UNet; variants: kernel "
+                         "variants against the defaults; rowq: the row quantizers; refgpu: the reference's own GPU "
+                         "path against this library's")
     ap.add_argument("--clocks-csv-dir", default=None,
                     help="also write the raw nvidia-smi clock samples of the timed region to this folder")
     ap.add_argument("--op-breakdown", action="store_true",
@@ -1030,25 +1397,12 @@ def main() -> int:
         return run_reference(args)
 
     import torch
-    from diffucore_b200 import _lib, kernels
     world, rank, local = _dist()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     peaks = _peaks()
-    if args.only == "flux" and args.op_breakdown:
-        res = flux_op_breakdown(dev)
-        if rank == 0:
-            print(json.dumps(res), flush=True)
-        return 0
-    if args.only in ("glue", "sdxl", "variants", "rowq"):
-        fn = {"glue": bench_glue, "sdxl": bench_sdxl, "variants": bench_variants, "rowq": bench_rowq}[args.only]
-        res = fn(args, dev, peaks)
-        if rank == 0:
-            print(json.dumps(res), flush=True)
-        return 0
-    if args.only in ("gemm", "flux"):
-        res = (bench_gemm(args, dev, peaks, cpu_baseline=rank == 0 and world == 1) if args.only == "gemm"
-               else bench_flux(args, world, rank, dev, peaks, cpu_baseline=rank == 0 and world == 1))
+
+    def finish(res) -> int:
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:
@@ -1056,72 +1410,69 @@ def main() -> int:
             dist.destroy_process_group()
         return 0
 
-    g = torch.Generator().manual_seed(0)
-    sets = []
-    for _ in range(4):
-        q, k, v = (torch.randn(B, H, S, D, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
-        sets.append((q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)))   # (B, L, H, D) views of bhld
-    out = torch.empty(B, S, H, D, device=dev, dtype=torch.bfloat16)
-    plan = kernels.AttnPlan(B, H, S, S, D, torch.bfloat16, _lib.MODE_BLOCK64, dev)
-    sampler = ClockSampler(local, Path(args.clocks_csv_dir) / f"clocks_rank{rank}.csv" if args.clocks_csv_dir else None)
-    t = bench_attention(args, world, _lib.MODE_BLOCK64, sets, plan, out, sampler)
-    total_s = _max_over_ranks(t["total_ms"] * 1e-3, world)
-    value = world * ATTN_OPS * args.steps / total_s / 1e12
-    main_tops = ATTN_OPS / (t["main_ms"] * 1e-3) / 1e12
-    peak = _int8_peak_tops(peaks)
-    line = {
-        "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": total_s * 1e3 / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8 QK^T / bf16 PV",
-        "data": "synthetic N(0,1) bf16, seeded", "config": CONFIG,
-        "prep_ms": t["prep_ms"], "attn_kernel_ms": t["main_ms"], "median_ms": t["median_ms"],
-        "roofline": {"bound": "tensor", "achieved": main_tops, "peak": peak, "unit": "TOPS",
-                     "frac": main_tops / peak, "traffic": TRAFFIC_ATTN,
-                     "traffic_note": "bytes per launch, ncu dram__bytes_read + write (one capture)",
-                     "peak_source": f"2 x bf16_tflops ({peaks['source']}); nominal dense INT8 4500 TOPS",
-                     "kernel": "attn_int8_kernel<128, bf16>",
-                     # the kernel's own ceiling: QK^T at the INT8 peak plus P.V at the bf16 peak
-                     "mixed": {"target_ms": (ATTN_OPS / 2 / (peak * 1e12) + ATTN_OPS / 2 / (peaks["bf16_tflops"] * 1e12)) * 1e3,
-                               "frac": (ATTN_OPS / 2 / (peak * 1e12) + ATTN_OPS / 2 / (peaks["bf16_tflops"] * 1e12))
-                               * 1e3 / t["main_ms"],
-                               "note": "half the ops (QK^T) at the INT8 peak, half (P.V) at the bf16 peak"}},
-        "clocks": t["clocks"],
-        "gpu_launches": 3 * args.steps,
-    }
-    if not args.no_extras:
-        def ref_mode():
-            ref_plan = kernels.AttnPlan(B, H, S, S, D, torch.bfloat16, _lib.MODE_REF, dev)
-            r = bench_attention(args, world, _lib.MODE_REF, sets, ref_plan, out)
-            return {"value": ATTN_OPS / (r["total_ms"] / args.steps * 1e-3) / 1e12, "unit": "TOPS",
-                    "ms_per_step": r["total_ms"] / args.steps, "prep_ms": r["prep_ms"],
-                    "attn_kernel_ms": r["main_ms"]}
+    if args.only == "flux" and args.op_breakdown:
+        return finish(flux_op_breakdown(dev))
+    if args.only in ("glue", "sdxl", "variants", "rowq"):
+        fn = {"glue": bench_glue, "sdxl": bench_sdxl, "variants": bench_variants, "rowq": bench_rowq}[args.only]
+        return finish(fn(args, dev, peaks))
+    if args.only == "refgpu":
+        return finish(bench_reference_gpu(args, dev))
+    if args.only == "attention":
+        return finish(bench_attention_config2(args, world, dev, peaks))
+    if args.only in ("gemm", "flux"):
+        return finish(bench_gemm(args, dev, peaks, cpu_baseline=rank == 0 and world == 1) if args.only == "gemm"
+                      else bench_flux(args, world, rank, dev, peaks, cpu_baseline=rank == 0 and world == 1))
 
-        line["ref_mode"] = _guarded(ref_mode)
-        line["w8a8_linear"] = _guarded(bench_gemm, args, dev, peaks, cpu_baseline=rank == 0 and world == 1)
-        e2e = _guarded(bench_e2e, args, dev)
-        if world > 1 and "error" not in e2e:
-            # every rank ran the same pipeline on its own GPU: whole-job rate over the slowest rank
-            ms = _max_over_ranks(e2e["ms_per_step"] * 1e-3, world) * 1e3
-            e2e.update(value=world * ATTN_OPS / (ms * 1e-3) / 1e12, ms_per_step=ms, ranks=world,
-                       h2d_bytes_per_step=world * e2e["h2d_bytes_per_step"],
-                       d2h_bytes_per_step=world * e2e["d2h_bytes_per_step"])
-        line["e2e"] = e2e
-        if rank == 0 and world == 1:
-            line["cpu_baseline"] = _guarded(_cpu_baseline)
-    if not args.no_extras and not args.no_flux:
-        del plan, sets
-        torch.cuda.empty_cache()
-        line["flux_dit"] = _guarded(bench_flux, args, world, rank, dev, peaks,
-                                    sides=(1024, 2048) if world == 1 else (2048,), cpu_baseline=rank == 0 and world == 1)
+    sampler = ClockSampler(local, Path(args.clocks_csv_dir) / f"clocks_rank{rank}.csv" if args.clocks_csv_dir else None)
+    head = bench_flux_headline(args, world, rank, dev, peaks, sampler)
+    details = {"headline": head.pop("details")}
+    line = {
+        "metric": METRIC, "value": head["value"], "unit": "s/step", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8 W8A8 GEMMs + int8 QK^T / bf16 P.V attention, bf16 activations",
+        "data": "synthetic: seeded random-init bf16 weights (no checkpoint), N(0,1) latent, text and pooled vector",
+        "config": flux_config(world),
+        "parity_vs_1gpu": head["parity_vs_1gpu"],
+        "roofline": head["roofline"], "clocks": head["clocks"], "e2e": head["e2e"],
+        "gpu_launches": head["gpu_launches"], "finite": head["finite"],
+    }
+    if rank == 0 and world == 1:
+        if _host_gib_available() < HOST_GIB_FOR_CPU_BASELINES:
+            line["cpu_baseline"] = {"error": f"skipped: under {HOST_GIB_FOR_CPU_BASELINES:.0f} GiB of host memory free"}
+        else:
+            line["cpu_baseline"] = _guarded(_cpu_flux_baseline)
+    if not args.no_extras:
+        kern = line["roofline"]["kernels"]
+        extras = {}
+        if world == 1:
+            att = _guarded(bench_attention_config2, args, world, dev, peaks)
+            details["attention_config2"] = att
+            kern["attention_config2"] = _compact(att, ["tops", "kernel_ms", "prep_ms", "roofline.achieved",
+                                                       "roofline.frac", "roofline.mixed.frac", "ref_mode.tops",
+                                                       "e2e.value"])
+            gem = _guarded(bench_gemm, args, dev, peaks, cpu_baseline=False)
+            details["w8a8_linear_config1"] = gem
+            kern["gemm_config1"] = _compact(gem, ["gemm.ms", "gemm.roofline.achieved", "gemm.roofline.frac",
+                                                  "cublaslt_int_mm.ms", "cublaslt_int_mm.tops"])
+            kern["quantizer_config1"] = _compact(gem, ["quantizer.ms", "quantizer.roofline.achieved",
+                                                       "quantizer.roofline.frac"])
+            ref_gpu = _guarded(bench_reference_gpu, args, dev)
+            details["reference_gpu"] = ref_gpu
+            extras["reference_gpu"] = {k: _compact(v, ["reference_ms", "ours_ms", "speedup", "outputs_bit_identical",
+                                                       "cos_vs_reference"])
+                                       for k, v in ref_gpu.items()} if "error" not in ref_gpu else ref_gpu
+        fl = _guarded(bench_flux, args, world, rank, dev, peaks, sides=(2048,))
+        details["flux_2048"] = fl
+        extras["flux_2048"] = _compact(fl, ["2048px.s_per_step", "2048px.frac_of_roofline", "2048px.finite"])
         if world == 1:
             torch.cuda.empty_cache()
-            line["sdxl_unet"] = _guarded(bench_sdxl, args, dev, peaks, cpu_baseline=rank == 0)
+            sd = _guarded(bench_sdxl, args, dev, peaks, cpu_baseline=rank == 0)
+            details["sdxl_unet"] = sd
+            extras["sdxl_unet"] = _compact(sd, ["s_per_step", "cpu_baseline.value", "finite"])
+        line["extras"] = extras
     if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
-    return 0
+        print("bench details: " + json.dumps(details), file=sys.stderr, flush=True)
+    return finish(line)
 
 
 if __name__ == "__main__":

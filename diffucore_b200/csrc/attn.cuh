@@ -304,12 +304,9 @@ __device__ __forceinline__ float scaled_max(int mx, float c) {
   return mx == INT_MIN ? -INFINITY : __fmul_rn(static_cast<float>(mx), c);
 }
 
-// DYN: the MMA thread issues each Q tile's next group (P.V half, then the next Q.K^T) as soon as
-// its inputs are ready, polling the barriers of both tiles, instead of the fixed order tile 0 then
-// tile 1; the order within a tile, and so every result, is the same.
 // SPLIT: this CTA covers one range of key tiles (see AttnParams) and leaves (O, m, l) of it for
 // attn_split_combine_kernel; everything inside the range runs as without the split.
-template <int D, bool BF16, bool DYN = false, bool SPLIT = false>
+template <int D, bool BF16, bool SPLIT = false>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
                  const __grid_constant__ CUtensorMap tma_v, const AttnParams p) {
@@ -426,65 +423,7 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
         issue_s(0, 0); mma_commit(&s_ready[0]);
         issue_s(1, 0); mma_commit(&s_ready[1]);
       }
-      if constexpr (DYN) {
-        // Per tile: the step and key half of its next P.V, and whether its next Q.K^T is due.
-        // A stage is released once both tiles issued the second-half P.V of its step; until then
-        // neither tile can reach that stage's next use, so every parity tested below is the one
-        // of the phase in question.
-        int js[2] = {0, 0}, hs[2] = {0, 0};
-        bool s_due[2] = {false, false};
-        uint32_t released = 0;          // 2 bits per stage: tiles done with its current step
-        long long idle_since = clock64();
-        while (ok && (js[0] < n || js[1] < n)) {
-          bool progressed = false;
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const int j = js[i];
-            const int st = j % kAttnStages;
-            const uint32_t ph = (j / kAttnStages) & 1;
-            if (s_due[i]) {
-              if (mbar_test(&k_full[st], ph)) {
-                tc_fence_after();
-                issue_s(i, st);
-                mma_commit(&s_ready[i]);
-                s_due[i] = false;
-                progressed = true;
-              }
-            } else if (j < n) {
-              const int hh = hs[i];
-              if (mbar_test(&p_ready[i][hh], j & 1) && mbar_test(&v_full[st], ph)) {
-                tc_fence_after();
-                issue_pv(i, hh, st, j > 0 || hh > 0);
-                mma_commit(&pv_done[i][hh]);
-                if (hh == 0) {
-                  hs[i] = 1;
-                } else {
-                  if (((released >> (2 * st)) & 3u) == 1u) {
-                    mma_commit(&kv_empty[st]);
-                    released &= ~(3u << (2 * st));
-                  } else {
-                    released += 1u << (2 * st);
-                  }
-                  hs[i] = 0;
-                  js[i] = j + 1;
-                  s_due[i] = j + 1 < n;
-                }
-                progressed = true;
-              }
-            }
-          }
-          if (progressed) {
-            idle_since = clock64();
-          } else if (*abort) {
-            ok = false;
-          } else if (clock64() - idle_since > kWaitCycleLimit) {
-            record_error(kErrWaitTimeout);
-            *abort = 1;
-            ok = false;
-          }
-        }
-      }
-      for (int j = 0; j < n && ok && !DYN; ++j) {
+      for (int j = 0; j < n && ok; ++j) {
         const int st = j % kAttnStages;
         const uint32_t ph = (j / kAttnStages) & 1;
         const int st1 = (j + 1) % kAttnStages;
@@ -711,299 +650,6 @@ attn_split_combine_kernel(const float* __restrict__ part_o, const float2* __rest
                                                 pack_p<BF16>(__fmul_rn(acc[2], inv), __fmul_rn(acc[3], inv)));
   } else {
     *reinterpret_cast<uint32_t*>(dst) = pack_p<BF16>(__fmul_rn(acc[0], inv), __fmul_rn(acc[1], inv));
-  }
-}
-
-// ----------------------------------------------------------------------------- main kernel, CTA pair
-// attn_pair_kernel: the two-Q-tile kernel over a cluster of two CTAs on one TPC with `cta_group::2`
-// MMAs (M = 256 rows, 128 per CTA), D = 128. Q tile i of the pair is 256 query rows; CTA r owns rows
-// [128 r, 128 r + 128) of it (its S and O in its own TMEM, its own softmax warps, the same code as
-// attn_int8_kernel). Per 128-key step CTA r stages only keys [64 r, 64 r + 64) of K (its half of
-// Q.K^T's B, N split) and columns [64 r, 64 r + 64) of V (its half of P.V's B). Per SM that halves
-// the K/V bytes TMA writes and the tensor core reads from shared memory per step (24 KB each
-// instead of 48), and one MMA instruction from the even CTA's issuing thread does the work of two.
-// Barriers: both CTAs' Q/K/V loads count on the even CTA's q_full / k_full / v_full; its commits
-// arrive on both CTAs' kv_empty / s_ready / pv_done (CTA mask 0b11); the softmax warps of both CTAs
-// arrive on the even CTA's p_ready (8 warps per tile and key half).
-constexpr int kPairRows = 512;      // query rows per CTA pair (2 tiles x 256)
-constexpr int kPairStages = 4;
-
-struct AttnPairSmem {
-  static constexpr int kQTile = kAttnBM * 128;           // this CTA's 128 rows of one Q tile, int8
-  static constexpr int kKHalf = 64 * 128;                // 64 keys x 128 B
-  static constexpr int kVHalf = kAttnBN * 64 * 2;        // 128 keys x 64 columns, 16-bit
-  static constexpr int kStage = kKHalf + kVHalf;
-  static constexpr int kBytes = 2 * kQTile + kPairStages * kStage;
-  static constexpr int kDynamic = kBytes + 1024;
-};
-
-template <bool BF16>
-__global__ void __launch_bounds__(kAttnThreads, 1)
-attn_pair_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
-                 const __grid_constant__ CUtensorMap tma_v, const AttnParams p) {
-  constexpr int D = 128;
-  using SM = AttnPairSmem;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sq = smem;                                  // this CTA's halves of the 2 Q tiles
-  uint8_t* sstage = smem + 2 * SM::kQTile;             // stages: K half, then V half
-
-  __shared__ __align__(8) uint64_t q_full;
-  __shared__ __align__(8) uint64_t k_full[kPairStages];
-  __shared__ __align__(8) uint64_t v_full[kPairStages];
-  __shared__ __align__(8) uint64_t kv_empty[kPairStages];
-  __shared__ __align__(8) uint64_t s_ready[2];
-  __shared__ __align__(8) uint64_t p_ready[2][2];   // [Q tile][key half]; used in the even CTA
-  __shared__ __align__(8) uint64_t pv_done[2][2];
-  __shared__ __align__(8) uint64_t drain_bar;
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
-
-  const int warp = warp_id(), lane = lane_id();
-  const uint32_t rank = cluster_ctarank();
-  const int qpair = static_cast<int>(blockIdx.x >> 1), h = blockIdx.y, b = blockIdx.z;
-  const int bh = b * p.H + h;
-  const int n = p.n_ktiles;
-
-  if (threadIdx.x == 0) {
-    mbar_init(&q_full, 1);
-    for (int s = 0; s < kPairStages; ++s) {
-      mbar_init(&k_full[s], 1); mbar_init(&v_full[s], 1); mbar_init(&kv_empty[s], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_ready[i], 1);
-      for (int hh = 0; hh < 2; ++hh) { mbar_init(&p_ready[i][hh], 8); mbar_init(&pv_done[i][hh], 1); }
-    }
-    mbar_init(&drain_bar, 1);
-    abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 8 && lane == 0) { tma_prefetch_desc(&tma_q); tma_prefetch_desc(&tma_k); tma_prefetch_desc(&tma_v); }
-  if (warp == 9) { tmem_alloc_pair(&tmem_slot, 512); tmem_relinquish_pair(); }
-  tc_fence_before();
-  cluster_sync();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  volatile int* abort = &abort_flag;
-  constexpr uint32_t kOCol = 256;      // S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512)
-
-  if (warp == 8) {
-    // ------------------------------------------------------------------ TMA producer (both CTAs)
-    if (lane == 0) {
-      bool ok = true;
-      const int r = static_cast<int>(rank);
-      const int qrow0 = bh * p.Lq_pad + qpair * kPairRows + r * kAttnBM;
-      const uint32_t qbar = cluster_addr(&q_full, 0);
-      if (rank == 0) mbar_arrive_expect_tx(&q_full, 2 * 2 * SM::kQTile);
-      tma_load_2d_pair(sq, &tma_q, qbar, 0, qrow0);
-      tma_load_2d_pair(sq + SM::kQTile, &tma_q, qbar, 0, qrow0 + 2 * kAttnBM);
-      for (int j = 0; j < n && ok; ++j) {
-        const int st = j % kPairStages;
-        const uint32_t ph = (j / kPairStages) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort)) { ok = false; break; }
-        uint8_t* sk = sstage + st * SM::kStage;
-        uint8_t* sv = sk + SM::kKHalf;
-        if (rank == 0) {
-          mbar_arrive_expect_tx(&k_full[st], 2 * SM::kKHalf);
-          mbar_arrive_expect_tx(&v_full[st], 2 * SM::kVHalf);
-        }
-        tma_load_2d_pair(sk, &tma_k, cluster_addr(&k_full[st], 0), 0, bh * p.Lk_pad + j * kAttnBN + r * 64);
-        tma_load_4d_pair(sv, &tma_v, cluster_addr(&v_full[st], 0), r * 64, j * kAttnBN, h, b);
-      }
-      if (!ok) for (int i = 0; i < 1000; ++i) __nanosleep(1000);
-    }
-    __syncwarp();                  // whole warp again before the aligned cluster barrier
-  } else if (warp == 9) {
-    // ------------------------------------------------------------------ MMA issuer (even CTA, lane 0)
-    if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc_s = idesc_i8(2 * kAttnBM, kAttnBN);
-      constexpr uint32_t idesc_o = idesc_f16(2 * kAttnBM, D, BF16, true);
-      const uint32_t sq_addr = smem_u32(sq);
-      auto issue_s = [&](int i, int st) {
-        uint64_t ad = smem_desc_sw(sq_addr + i * SM::kQTile, 16, 1024, 2);
-        uint64_t bd = smem_desc_sw(smem_u32(sstage + st * SM::kStage), 16, 1024, 2);
-        const uint32_t d = tmem + i * 128;
-#pragma unroll
-        for (int kk = 0; kk < D / 32; ++kk) {
-          mma_i8_ss_pair(d, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
-          ad += 32 >> 4;
-          bd += 32 >> 4;
-        }
-      };
-      // O_i += P_i[:, 64 keys of half hh] . V half: 64-column box, 8-key groups 1024 B apart,
-      // 16 keys (2048 B) per MMA.
-      auto issue_pv = [&](int i, int hh, int st, bool acc) {
-        uint64_t bd = smem_desc_sw(smem_u32(sstage + st * SM::kStage + SM::kKHalf) + hh * 64 * 128, SM::kVHalf,
-                                   1024, 2);
-        const uint32_t d = tmem + kOCol + i * D;
-        uint32_t a = tmem + i * 128 + hh * 64;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          mma_f16_ts_pair(d, a, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
-          bd += 2048 >> 4;
-          a += 8;
-        }
-      };
-      bool ok = mbar_wait(&q_full, 0, abort) && mbar_wait(&k_full[0], 0, abort);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0); mma_commit_pair_both(&s_ready[0]);
-        issue_s(1, 0); mma_commit_pair_both(&s_ready[1]);
-      }
-      for (int j = 0; j < n && ok; ++j) {
-        const int st = j % kPairStages;
-        const uint32_t ph = (j / kPairStages) & 1;
-        const int st1 = (j + 1) % kPairStages;
-        const uint32_t ph1 = ((j + 1) / kPairStages) & 1;
-        const bool more = j + 1 < n;
-        if (!mbar_wait(&v_full[st], ph, abort)) { ok = false; break; }
-        for (int i = 0; i < 2 && ok; ++i) {
-          for (int hh = 0; hh < 2; ++hh) {
-            if (!mbar_wait_cluster(&p_ready[i][hh], j & 1, abort)) { ok = false; break; }
-            tc_fence_after();
-            issue_pv(i, hh, st, j > 0 || hh > 0);
-            mma_commit_pair_both(&pv_done[i][hh]);
-          }
-          if (!ok) break;
-          if (i == 1) mma_commit_pair_both(&kv_empty[st]);
-          if (more) {
-            if (i == 0 && !mbar_wait(&k_full[st1], ph1, abort)) { ok = false; break; }
-            tc_fence_after();
-            issue_s(i, st1);
-            mma_commit_pair_both(&s_ready[i]);
-          }
-        }
-      }
-      mma_commit_pair(&drain_bar);
-      mbar_wait(&drain_bar, 0, nullptr, 1000000);
-    }
-    __syncwarp();                  // whole warp again before the aligned cluster barrier
-  } else {
-    // ------------------------------------------------------------------ softmax warpgroups (both CTAs)
-    const int wg = warp >> 2;                 // Q tile 0 or 1
-    const int quarter = warp & 3;             // TMEM lane quarter
-    const int r_local = quarter * 32 + lane;
-    const int qrow = qpair * kPairRows + wg * 2 * kAttnBM + static_cast<int>(rank) * kAttnBM + r_local;
-    // rows past Lq_pad (the last pair of a head) get no scale and are not stored
-    const float cq = qrow < p.Lq_pad ? __fmul_rn(p.q_scale[static_cast<int64_t>(bh) * p.Lq_pad + qrow], p.scale_log2)
-                                     : 0.0f;
-    const float* ksc = p.k_scale + static_cast<int64_t>(bh) * (p.Lk_pad / kAttnKBlk);
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_addr = tmem + lane_off + wg * 128;
-    const uint32_t o_addr = tmem + lane_off + kOCol + wg * D;
-    const uint32_t p_ready_even[2] = {cluster_addr(&p_ready[wg][0], 0), cluster_addr(&p_ready[wg][1], 0)};
-    const int tail_valid = p.Lk - (n - 1) * kAttnBN;      // keys in the last tile (1..128)
-    float m = -INFINITY;
-    float2 l2 = make_float2(0.f, 0.f);
-    float ks_cur[2] = {ksc[0], ksc[1]};
-    bool ok = true;
-    auto rescale_o = [&](uint64_t* bar, uint32_t parity, float alpha) -> bool {
-      bool w = mbar_wait(bar, parity, abort);
-      if (!__all_sync(0xffffffffu, w)) return false;
-      tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
-        uint32_t o[32];
-        tmem_ld32(o_addr + c, o);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float2 v = __fmul2_rn(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])),
-                                      make_float2(alpha, alpha));
-          o[e] = __float_as_uint(v.x);
-          o[e + 1] = __float_as_uint(v.y);
-        }
-        tmem_st32(o_addr + c, o);
-      }
-      return true;
-    };
-    uint32_t r[64];
-    for (int j = 0; j < n && ok; ++j) {
-      float ks_next[2] = {0.f, 0.f};
-      if (j + 1 < n) { ks_next[0] = ksc[2 * j + 2]; ks_next[1] = ksc[2 * j + 3]; }
-      ok = mbar_wait(&s_ready[wg], j & 1, abort);
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      tc_fence_after();
-      const bool tail = j == n - 1 && tail_valid < kAttnBN;
-      tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-      tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      tmem_wait_ld();
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int valid = tail ? tail_valid - 64 * hh : 64;
-        if (valid < 64) mask_tail64(r, valid);
-        const float c = __fmul_rn(cq, ks_cur[hh]);
-        const int mx = row_max64(r);
-        if (j == 0 && hh == 0) m = scaled_max(mx, c);
-        float2 lt = make_float2(0.f, 0.f);
-        uint32_t pk[32];
-        if (valid < 64) p_half<BF16, true>(r, c, -__fmaf_rn(kMagicF, c, m), valid, lt, pk);
-        else p_half<BF16, false>(r, c, -__fmaf_rn(kMagicF, c, m), valid, lt, pk);
-        const float mt = scaled_max(mx, c);
-        if (__any_sync(0xffffffffu, mt > m + kLazyRescale)) {
-          const float mnew = fmaxf(m, mt);
-          const float alpha = ex2_approx(m - mnew);
-          l2 = __fmul2_rn(l2, make_float2(alpha, alpha));
-          m = mnew;
-          lt = make_float2(0.f, 0.f);
-          if (valid < 64) p_half<BF16, true>(r, c, -__fmaf_rn(kMagicF, c, m), valid, lt, pk);
-          else p_half<BF16, false>(r, c, -__fmaf_rn(kMagicF, c, m), valid, lt, pk);
-          const bool have_o = j > 0 || hh > 0;
-          if (have_o) {
-            const bool w = hh == 0 ? rescale_o(&pv_done[wg][1], (j - 1) & 1, alpha)
-                                   : rescale_o(&pv_done[wg][0], j & 1, alpha);
-            if (!w) { ok = false; break; }
-          }
-        }
-        l2 = __fadd2_rn(l2, lt);
-        if (hh == 0) {
-          tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-          tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-        }
-        tmem_st32(s_addr + 64 * hh, pk);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(p_ready_even[hh]);
-        if (hh == 0) tmem_wait_ld();
-      }
-      ks_cur[0] = ks_next[0];
-      ks_cur[1] = ks_next[1];
-    }
-    if (ok) {
-      ok = mbar_wait(&pv_done[wg][1], (n - 1) & 1, abort);
-      ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok) {
-      tc_fence_after();
-      const float inv = __fdiv_rn(1.0f, __fadd_rn(l2.x, l2.y));
-      const bool row_ok = qrow < p.Lq;
-      uint16_t* dst = reinterpret_cast<uint16_t*>(p.o) + b * p.o_sb + static_cast<int64_t>(qrow) * p.o_sl + h * p.o_sh;
-#pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
-        uint32_t o[32];
-        tmem_ld32(o_addr + c, o);
-        tmem_wait_ld();
-        if (row_ok) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 w;
-            w.x = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e]), inv), __fmul_rn(__uint_as_float(o[e + 1]), inv));
-            w.y = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e + 2]), inv), __fmul_rn(__uint_as_float(o[e + 3]), inv));
-            w.z = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e + 4]), inv), __fmul_rn(__uint_as_float(o[e + 5]), inv));
-            w.w = pack_p<BF16>(__fmul_rn(__uint_as_float(o[e + 6]), inv), __fmul_rn(__uint_as_float(o[e + 7]), inv));
-            *reinterpret_cast<uint4*>(dst + c + e) = w;
-          }
-        }
-      }
-    }
-  }
-
-  tc_fence_before();
-  cluster_sync();
-  if (warp == 9) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem, 512);
   }
 }
 

@@ -324,11 +324,16 @@ struct GemmEpi {
   int64_t block_stride = 0;
 };
 
-// Pair tiles (256 x 256 over a cluster of two CTAs, see gemm.cuh) are opt-in through
-// DC_GEMM_PAIR=1 and need more than one 128-row block of activations.
-bool use_pair_gemm(int64_t M) {
+// Pair tiles (256 x 256 over a cluster of two CTAs, see gemm.cuh): the default for wide GEMMs of at
+// least 512 rows without a GELU epilogue, where they measured 1-4 % faster on a B200 than the
+// one-CTA tile (config 1: 41.5 vs 42.0 us; FLUX qkv 104.3 vs 108.2; linear2 155.4 vs 161.4) with
+// bit-identical results; with the GELU epilogue they were not faster (168.1 vs 166.9). Environment
+// DC_GEMM_PAIR = "0" turns them off, "1" uses them wherever M > 128.
+bool use_pair_gemm(int64_t M, int gelu) {
   const char* env = getenv("DC_GEMM_PAIR");
-  return env != nullptr && strcmp(env, "1") == 0 && M > dc::kGemmBM;
+  if (env != nullptr && strcmp(env, "0") == 0) return false;
+  if (env != nullptr && strcmp(env, "1") == 0) return M > dc::kGemmBM;
+  return gelu == 0 && M >= 512;
 }
 
 // Largest number of two-CTA clusters of `kernel` resident at once on the current device.
@@ -453,7 +458,7 @@ template <int OUT>
 int dispatch_gemm_wide(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx,
                        const float* sw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
                        int64_t K, int gelu, const GemmEpi& epi, cudaStream_t st) {
-  if (use_pair_gemm(M))
+  if (use_pair_gemm(M, gelu))
     return dispatch_gemm_epilogue<256, OUT, true>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st);
   return dispatch_gemm_epilogue<256, OUT, false>(q, ldq, w, ldw, sx, sw, bias, out, ldo, M, N, K, gelu, epi, st);
 }
@@ -484,8 +489,17 @@ int gemm_checked(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, con
     if (gelu) return fail("gemm: a gated residual takes no gelu");
     if (epi.ldr < N) return fail("gemm: residual leading dimension smaller than the row");
   }
-  // Wide tiles unless the column blocks are not a multiple of them.
+  // Wide (128 x 256) tiles unless the column blocks are not a multiple of them, or unless 128 x 128
+  // tiles fill the SMs in fewer tile-times: with few 128-row blocks (a sequence-parallel rank's rows,
+  // FLUX's 512 text rows) the wide grid can leave most SMs idle. Cost = waves x tile width; the wide
+  // tile wins ties (it re-reads each activation block half as often).
   bool wide = N > 128;
+  if (wide) {
+    const int64_t tm = (M + dc::kGemmBM - 1) / dc::kGemmBM, sms = sm_count();
+    const int64_t cost_wide = (tm * ((N + 255) / 256) + sms - 1) / sms * 256;
+    const int64_t cost_narrow = (tm * ((N + 127) / 128) + sms - 1) / sms * 128;
+    if (cost_narrow * 100 <= cost_wide * 85) wide = false;
+  }
   if (epi.col_block > 0) {
     if (epi.col_block % 128 || epi.block_stride % 8) return fail("gemm: col_block must be a multiple of 128 and block_stride of 8");
     if (ldo < epi.col_block) return fail("gemm: ldo smaller than col_block");
@@ -596,7 +610,6 @@ int attn_prep(const void* q, const void* k, int64_t B, int64_t H, int64_t Lq, in
 // 49 vs 81 us per wave) and so wins when the two-tile grid ends in a poorly filled wave (few
 // heads per GPU, as with a sequence-parallel split). Environment DC_ATTN_KERNEL = "two_tile" or
 // "single_tile" pins one (tests use it to cover both).
-// DC_ATTN_KERNEL = "pair" selects the CTA-pair kernel for D = 128 (attn_pair_kernel; opt-in).
 bool use_single_tile_kernel(int64_t ctas_two_tile, int64_t ctas_single_tile) {
   const char* env = getenv("DC_ATTN_KERNEL");
   if (env != nullptr && strcmp(env, "two_tile") == 0) return false;
@@ -646,33 +659,6 @@ int attn_main(const void* v, int64_t B, int64_t H, int64_t Lq, int64_t Lk, const
   p.q_scale = reinterpret_cast<const float*>(ws + a.q_scale);
   p.k_scale = reinterpret_cast<const float*>(ws + a.k_scale);
   p.o = o; p.o_sb = os[0]; p.o_sl = os[1]; p.o_sh = os[2];
-  const char* which = getenv("DC_ATTN_KERNEL");
-  if (D == 128 && which != nullptr && strcmp(which, "pair") == 0) {
-    // CTA-pair kernel (opt-in): K staged in 64-key halves, one per CTA of a pair
-    CUtensorMap tk_half;
-    const uint64_t dims[2] = {static_cast<uint64_t>(D), static_cast<uint64_t>(B * H * a.Lk_pad)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(D)};
-    const uint32_t box[2] = {static_cast<uint32_t>(D), 64};
-    int r = make_map(&tk_half, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, ws + a.k_codes, dims, strides, box, qk_swz);
-    if (r) return r;
-    auto kernel = dc::attn_pair_kernel<BF16>;
-    if ((r = set_smem(kernel, dc::AttnPairSmem::kDynamic))) return r;
-    const int64_t pairs = (a.Lq_pad + dc::kPairRows - 1) / dc::kPairRows;
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), static_cast<unsigned>(H), static_cast<unsigned>(B));
-    cfg.blockDim = dim3(dc::kAttnThreads);
-    cfg.dynamicSmemBytes = static_cast<size_t>(dc::AttnPairSmem::kDynamic);
-    cfg.stream = st;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tq, tk_half, tv, p);
-    if (e != cudaSuccess) return cuda_fail(e, "attention pair launch");
-    DC_CHECK_LAUNCH("attention launch");
-    return DC_OK;
-  }
   if (use_single_tile_kernel(B * H * (a.Lq_pad / dc::kAttnRows), B * H * (a.Lq_pad / dc::kDbRows))) {
     using SD = dc::AttnDbSmem<D>;
     auto kernel = dc::attn_db_kernel<D, BF16>;
@@ -681,9 +667,7 @@ int attn_main(const void* v, int64_t B, int64_t H, int64_t Lq, int64_t Lk, const
     dim3 grid(static_cast<unsigned>(a.Lq_pad / dc::kDbRows), static_cast<unsigned>(H), static_cast<unsigned>(B));
     kernel<<<grid, dc::kAttnThreads, SD::kDynamic, st>>>(tq, tk, tv, p);
   } else {
-    const char* issue = getenv("DC_ATTN_ISSUE");
-    auto kernel = issue != nullptr && strcmp(issue, "dynamic") == 0 ? dc::attn_int8_kernel<D, BF16, true>
-                                                                     : dc::attn_int8_kernel<D, BF16, false>;
+    auto kernel = dc::attn_int8_kernel<D, BF16, false>;
     int r = set_smem(kernel, SM::kDynamic);
     if (r) return r;
     dim3 grid(static_cast<unsigned>(a.Lq_pad / dc::kAttnRows), static_cast<unsigned>(H), static_cast<unsigned>(B));
@@ -755,7 +739,7 @@ int attn_main_split(const void* v, int64_t B, int64_t H, int64_t Lq, int64_t Lk,
   p.part_o = static_cast<float*>(partials);
   p.part_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(partials) +
                                         static_cast<size_t>(ranges) * static_cast<size_t>(B * H * a.Lq_pad) * D * 4);
-  auto kernel = dc::attn_int8_kernel<D, BF16, false, true>;
+  auto kernel = dc::attn_int8_kernel<D, BF16, true>;
   int r = set_smem(kernel, SM::kDynamic);
   if (r) return r;
   dim3 grid(static_cast<unsigned>(a.Lq_pad / dc::kAttnRows * ranges), static_cast<unsigned>(H), static_cast<unsigned>(B));
@@ -1119,21 +1103,43 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratch];
 namespace {
 std::mutex g_noalloc_mutex;
 void* g_noalloc_addr[256] = {};   // device address of g_noalloc_scratch, per device ordinal
+void* g_noalloc_ctx[256] = {};    // the CUDA context that address belongs to
+
+// The current CUDA context (cuCtxGetCurrent through the runtime's driver entry point), or null.
+void* current_context() {
+  typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  CUcontext ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
 
 // The scratch array's device address for the current device. In host code the array's name is
-// only a host-side stand-in, so the address comes from cudaGetSymbolAddress, once per device,
-// with that device current (the first call on each device does this).
+// only a host-side stand-in, so the address comes from cudaGetSymbolAddress with that device
+// current: on the first call on each device, and again whenever the device's context is not the
+// one the address was looked up in (after cudaDeviceReset the module is loaded anew and the array
+// may sit elsewhere).
 int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 256) return fail("device ordinal %d out of range", dev);
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_addr[dev] == nullptr) {
+  void* ctx = current_context();
+  if (g_noalloc_addr[dev] == nullptr || ctx == nullptr || ctx != g_noalloc_ctx[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(scratch)");
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx[dev] = current_context();   // the lookup made the primary context current if none was
   }
   *out = g_noalloc_addr[dev];
   return DC_OK;

@@ -235,12 +235,13 @@ def attn_int8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float
               mode: int = _lib.MODE_REF, workspace: torch.Tensor | None = None,
               out: torch.Tensor | None = None) -> torch.Tensor:
     """INT8 attention over ``(B, L, H, D)`` q/k/v (any strides with stride(-1) == 1 and the
-    others multiples of 8) -> contiguous ``(B, Lq, H, D)`` in the input dtype. With the environment
-    variable ``DC_ATTN_SPLIT=auto`` (opt-in) shapes whose grid fills the GPU poorly run
-    :func:`attn_int8_split` with the key-range count :func:`choose_attn_split` picks."""
+    others multiples of 8) -> contiguous ``(B, Lq, H, D)`` in the input dtype. Shapes whose grid
+    fills the GPU poorly (few heads over long sequences, a sequence-parallel rank's share) run
+    :func:`attn_int8_split` with the key-range count :func:`choose_attn_split` picks; the
+    environment variable ``DC_ATTN_SPLIT=0`` turns that routing off."""
     B, Lq, Lk, H, D = _check_attn_inputs(q, k, v)
-    if os.environ.get("DC_ATTN_SPLIT") == "auto":
-        nsplit = choose_attn_split(B, H, Lq, Lk, torch.cuda.get_device_properties(q.device).multi_processor_count)
+    if os.environ.get("DC_ATTN_SPLIT", "auto") != "0":
+        nsplit = choose_attn_split(B, H, Lq, Lk, _sm_count(q.device), D=D)
         if nsplit > 1:
             return attn_int8_split(q, k, v, sm_scale, nsplit, mode, workspace=workspace, out=out)
     lib = _lib.load()
@@ -258,12 +259,26 @@ def attn_int8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float
     return out
 
 
-def choose_attn_split(B: int, H: int, Lq: int, Lk: int, sms: int = 148, max_split: int = 4) -> int:
-    """Key ranges for :func:`attn_int8_split` (1 = do not split), from a wave-count model: the
-    two-tile kernel runs ceil(Lq / 256) CTAs per head, each for its key tiles of 128 plus about one
-    tile's worth of prologue and epilogue; the single-tile kernel the unsplit call would otherwise
-    choose takes 0.61 of a two-tile CTA's time for 128 rows. A split is chosen only when it saves
-    at least 10 % against the better unsplit kernel (it adds the combine pass)."""
+_SMS: dict = {}
+
+
+def _sm_count(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SMS[idx]
+
+
+def choose_attn_split(B: int, H: int, Lq: int, Lk: int, sms: int = 148, max_split: int = 4, D: int = 128) -> int:
+    """Key ranges for :func:`attn_int8_split` (1 = do not split), from a wave-count model in units
+    of one two-tile CTA's 128-key step (~2.4 us on a B200): the two-tile kernel runs
+    ceil(Lq / 256) CTAs per head, each for its key tiles plus about one tile's worth of prologue
+    and epilogue; the single-tile kernel the unsplit call would otherwise choose takes 0.61 of a
+    two-tile CTA's time for 128 rows. A split also pays for its combine pass: about 1.3 units of
+    launch and tail plus the fp32 partials written and read back (ranges x 2 x B H Lq D x 4 bytes,
+    ~14 MB per unit at HBM speed). A split is chosen only when it saves at least 10 % against the
+    better unsplit kernel. Measured on a B200 (3 heads, mode ref): 16896 tokens split in two
+    0.486 ms against 0.529 unsplit; 4608 tokens 0.076 against 0.071, so not split."""
     qctas = B * H * -(-Lq // 256)
     n = -(-Lk // 128)
 
@@ -273,7 +288,10 @@ def choose_attn_split(B: int, H: int, Lq: int, Lk: int, sms: int = 148, max_spli
     def cost_split(r: int) -> float:
         tps = -(-n // r)
         ranges = -(-n // tps)
-        return waves(qctas * ranges) * (tps + 1)
+        cost = waves(qctas * ranges) * (tps + 1)
+        if ranges > 1:
+            cost += 1.3 + ranges * 2 * B * H * Lq * D * 4 / 14e6
+        return cost
 
     unsplit = min(cost_split(1), 0.61 * waves(2 * qctas) * (n + 1))
     best = min(range(1, min(max_split, n) + 1), key=lambda r: (cost_split(r), r))

@@ -148,10 +148,6 @@ int dc_attn_workspace_layout(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64
  * The main kernel is picked by grid size (two 128-row Q tiles per CTA, or one with S double-
  * buffered when that fills the last wave better); environment DC_ATTN_KERNEL = "two_tile" or
  * "single_tile" pins one. Both give the same result within the stated tolerance.
- * DC_ATTN_ISSUE = "dynamic" makes the two-tile kernel's MMA thread issue each tile's next group
- * as soon as its inputs are ready (same arithmetic, bit-identical output; experimental).
- * DC_ATTN_KERNEL = "pair" (D = 128) runs the two-tile kernel over CTA pairs with cta_group::2 MMAs,
- * each SM staging half of every K and V tile (experimental).
  * Replaces the pybind `fwd(q, k, v, sm_scale)` of src/diffucore/kernels/int8_attn_sm80.cu:460-497
  * (and int8_attn_sm75.cu:477-514) called from `attention_blhd` / `attention_bhld`
  * (src/diffucore/models/_attention.py:216-217, :268-271). */
@@ -197,8 +193,9 @@ int dc_attn_int8_main_split(const void* v, int dtype, int64_t B, int64_t H, int6
  * DC_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads the library holds until
  * the process exits. Shapes whose workspace (dc_attn_workspace_size) exceeds that size are
  * rejected with DC_ERR_INVALID. Allocates nothing (no cudaMalloc / cudaFree). The first call on each
- * device looks up the array's device address (cudaGetSymbolAddress) with that device current;
- * make that first call before any stream capture. All calls on a device share the one array and it
+ * device looks up the array's device address (cudaGetSymbolAddress) with that device current, and
+ * so does the first call after the device's context changed (cudaDeviceReset); make those calls
+ * before any stream capture. All calls on a device share the one array and it
  * keeps the last call's contents (nothing in it needs to start at zero); calls that overlap on the
  * GPU (different streams) race on it, so order them on one stream or with events.
  * No counterpart in the reference (its pybind `fwd` always allocates its workspace). */

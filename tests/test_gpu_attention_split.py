@@ -2,13 +2,10 @@
 attn_int8_kernel<..., SPLIT> over key ranges + attn_split_combine_kernel) on a B200: within the
 attention tolerance of the CPU oracle (max-abs 2e-2, cosine >= 0.999) and within rounding of the
 unsplit two-tile kernel it divides (cosine >= 0.99999), over ranges that end in a key tail, one
-key tile per range, query tails, D = 64, fp16 and both quant modes; the opt-in routing
-(DC_ATTN_SPLIT=auto) of kernels.attn_int8. Opt-in until it has run on a B200: set
-DC_TEST_ATTN_SPLIT=1."""
+key tile per range, query tails, D = 64, fp16 and both quant modes; the default routing of
+kernels.attn_int8 (DC_ATTN_SPLIT=0 turns it off)."""
 
 from __future__ import annotations
-
-import os
 
 import pytest
 import torch
@@ -17,11 +14,7 @@ import oracle
 from diffucore_b200 import _lib, kernels
 from tests.conftest import DTAG, torch_to_bits
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("DC_TEST_ATTN_SPLIT") != "1",
-                       reason="split attention is opt-in until run on a B200 (DC_TEST_ATTN_SPLIT=1)"),
-]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 MODES = {"ref": _lib.MODE_REF, "block64": _lib.MODE_BLOCK64}
 
@@ -45,7 +38,7 @@ def _cos(a, b):
                                               (1, 256, 1000, 1, 8), (1, 70, 129, 2, 2)])
 def test_split_matches_oracle_and_unsplit(monkeypatch, mode, dtype, D, B, Lq, Lk, H, nsplit):
     monkeypatch.setenv("DC_ATTN_KERNEL", "two_tile")
-    monkeypatch.delenv("DC_ATTN_SPLIT", raising=False)
+    monkeypatch.setenv("DC_ATTN_SPLIT", "0")
     q, k, v = _inputs(B, Lq, Lk, H, D, dtype)
     qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
     sm = D ** -0.5
@@ -70,17 +63,21 @@ def test_split_is_deterministic():
 
 
 def test_auto_routing_splits_few_heads(monkeypatch):
-    """DC_ATTN_SPLIT=auto sends a 3-head 4608-token call (FLUX 1024^2 on 8 GPUs) through the split
-    path, whose result equals an explicit split call bit for bit."""
-    q, k, v = (t.to(DEV) for t in _inputs(1, 4608, 4608, 3, 128, torch.bfloat16, seed=6))
+    """The default dispatch sends a 3-head 16896-token call (FLUX 2048^2 on 8 GPUs) through the
+    split path, whose result equals an explicit split call bit for bit; DC_ATTN_SPLIT=0 turns the
+    routing off (the unsplit kernel's result)."""
+    q, k, v = (t.to(DEV) for t in _inputs(1, 16896, 16896, 3, 128, torch.bfloat16, seed=6))
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    nsplit = kernels.choose_attn_split(1, 3, 4608, 4608, sms)
+    nsplit = kernels.choose_attn_split(1, 3, 16896, 16896, sms)
     assert nsplit > 1
-    monkeypatch.setenv("DC_ATTN_SPLIT", "auto")
+    monkeypatch.delenv("DC_ATTN_SPLIT", raising=False)
     routed = kernels.attn_int8(q, k, v, 128 ** -0.5, _lib.MODE_REF)
-    monkeypatch.delenv("DC_ATTN_SPLIT")
     explicit = kernels.attn_int8_split(q, k, v, 128 ** -0.5, nsplit, _lib.MODE_REF)
     assert torch.equal(routed, explicit)
+    monkeypatch.setenv("DC_ATTN_SPLIT", "0")
+    plain = kernels.attn_int8(q, k, v, 128 ** -0.5, _lib.MODE_REF)
+    assert not torch.equal(plain, routed)
+    assert _cos(plain.float().cpu(), routed.float().cpu()) >= 0.99999
 
 
 def test_running_max_moves_inside_a_range():

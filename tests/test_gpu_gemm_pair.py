@@ -6,24 +6,18 @@ column-block layout) must be bit-identical; the int32 result is also checked aga
 ``torch._int_mm``. Shapes cover BASELINE config 1, FLUX's widest reduction (K = 15360), and row /
 column tails where the odd CTA of a pair holds no valid rows.
 
-The pair kernel is selected with ``DC_GEMM_PAIR=1``. Until it has run on a B200 these tests are
-opt-in: set ``DC_TEST_GEMM_PAIR=1``.
+The pair kernel is the default for wide GEMMs of at least 512 rows without GELU; the tests force it
+with ``DC_GEMM_PAIR=1`` and the one-CTA kernel with ``DC_GEMM_PAIR=0``.
 """
 
 from __future__ import annotations
-
-import os
 
 import pytest
 import torch
 
 from diffucore_b200 import _lib, kernels
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("DC_TEST_GEMM_PAIR") != "1",
-                       reason="pair-tile GEMM is opt-in until run on a B200 (DC_TEST_GEMM_PAIR=1)"),
-]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 SHAPES = [(4096, 3072, 3072), (4608, 3072, 15360), (300, 640, 512), (129, 257, 4096), (200, 1000, 256),
@@ -41,7 +35,7 @@ def _operands(M, N, K, seed):
 
 
 def _both(monkeypatch, fn):
-    monkeypatch.delenv("DC_GEMM_PAIR", raising=False)
+    monkeypatch.setenv("DC_GEMM_PAIR", "0")
     one = fn()
     monkeypatch.setenv("DC_GEMM_PAIR", "1")
     pair = fn()
