@@ -1100,9 +1100,17 @@ def bench_reference_gpu(args, dev) -> dict:
             same = bool(torch.equal(ref_layer(xs[0]), our_layer(xs[0])))
             ref_ms = timeit(lambda i: ref_layer(xs[i % 6]))
             our_ms = timeit(lambda i: our_layer(xs[i % 6]))
+            # the reference's three steps alone
+            rq = [ref.quantize_activation(x, 0) for x in xs]
+            accs = [ref.int_mm(q, ref_layer.weight) for q, _ in rq[:2]]
+            parts = {"quantize_ms": timeit(lambda i: ref.quantize_activation(xs[i % 6], 0)),
+                     "int_mm_ms": timeit(lambda i: ref.int_mm(rq[i % 6][0], ref_layer.weight)),
+                     "rescale_ms": timeit(lambda i: ref.rescale(accs[i % 2], rq[i % 2][1], ref_layer.scale,
+                                                                ref_layer.bias, torch.bfloat16))}
         out["w8a8_linear_config1"] = {"reference_ms": ref_ms, "ours_ms": our_ms, "speedup": ref_ms / our_ms,
-                                      "outputs_bit_identical": same,
+                                      "outputs_bit_identical": same, "reference_parts": parts,
                                       "reference_path": "Triton _rot_quant_kernel + torch._int_mm + Triton _rescale_kernel"}
+        del rq, accs
         del xs
     else:
         out["w8a8_linear_config1"] = {"error": "reference _int8.py not staged in oracle/_ref"}
@@ -1249,6 +1257,23 @@ def bench_variants(args, dev, peaks) -> dict:
         for tag, env in (("one_cta", {"DC_GEMM_PAIR": "0"}), ("pair", {"DC_GEMM_PAIR": "1"})):
             ms = _time_env(fn, env, warm, steps)
             row[tag] = {"ms": round(ms, 4), "tops": round(ops / ms / 1e9, 1), "frac": round(ops / ms / 1e9 / peak, 3)}
+        if not gated and gelu == _lib.GELU_NONE:
+            # the same GEMM with the raw int32 accumulator as output (no rescale epilogue), and cuBLASLt's
+            acc = torch.empty(M, N, device=dev, dtype=torch.int32)
+            lib = _lib.load()
+
+            def fn_i32(i, qs=qs, w=w, acc=acc):
+                qq = qs[i % len(qs)]
+                _lib.check(lib.dc_gemm_w8a8(kernels._ptr(qq), K, kernels._ptr(w), K, None, None, None,
+                                            kernels._ptr(acc), N, _lib.DTYPE_I32, M, N, K, 0, kernels._stream(qq)))
+
+            for tag, env in (("one_cta_int32_out", {"DC_GEMM_PAIR": "0"}), ("pair_int32_out", {"DC_GEMM_PAIR": "1"})):
+                ms = _time_env(fn_i32, env, warm, steps)
+                row[tag] = {"ms": round(ms, 4), "tops": round(ops / ms / 1e9, 1)}
+            wt = w.t()
+            ms = _time_env(lambda i, qs=qs, wt=wt: torch._int_mm(qs[i % len(qs)], wt), {}, warm, steps)
+            row["cublaslt_int32_out"] = {"ms": round(ms, 4), "tops": round(ops / ms / 1e9, 1)}
+            del acc
         out[name] = row
         del qs, w, ys
         torch.cuda.empty_cache()

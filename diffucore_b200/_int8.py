@@ -109,6 +109,25 @@ def dequantize_weight(q: torch.Tensor, scale: torch.Tensor, group: int) -> torch
 
 # ─── hot path ───────────────────────────────────────────────────────────────────────────
 
+_QDIV = {"ieee": _lib.QDIV_IEEE, "triton": _lib.QDIV_FULL}
+
+
+def set_quant_division(mode: str) -> None:
+    """Which of the reference's quantizer arithmetics the activation codes reproduce, process-wide:
+    ``"ieee"`` (default) rounds ``amax / 127`` and ``x / scale`` correctly, the reference's torch-op
+    path as it runs on the CPU (_int8.py:87-97); ``"triton"`` divides as the reference's Triton
+    kernels do on a GPU (``_store_quantized``, _int8.py:393-397). The two give the same codes except
+    for one step at ~1.5e-4 of elements."""
+    if mode not in _QDIV:
+        raise ValueError(f"quant division must be one of {sorted(_QDIV)}, got {mode!r}")
+    _lib.check(_lib.load().dc_set_quant_division(_QDIV[mode]))
+
+
+def quant_division() -> str:
+    code = _lib.load().dc_quant_division()
+    return next(k for k, v in _QDIV.items() if v == code)
+
+
 def quantize_activation(x2: torch.Tensor, group: int):
     """``(int8 [M, K], fp32 scale [M])``: rotate, then per-row int8 (_int8.py:299-310), as one
     HBM pass of the native quantizer."""

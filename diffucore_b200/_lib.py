@@ -18,6 +18,7 @@ DC_OK = 0
 DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_I8, DTYPE_I32 = 0, 1, 2, 3, 4
 GELU_NONE, GELU_ERF, GELU_TANH = 0, 1, 2
 MODE_REF, MODE_BLOCK64 = 0, 1
+QDIV_IEEE, QDIV_FULL = 0, 1
 ABI_VERSION = 1
 NOALLOC_SCRATCH_BYTES = 32 << 20
 
@@ -29,6 +30,8 @@ _c_i64p = ctypes.POINTER(ctypes.c_int64)
 _SIGNATURES = {
     "dc_version": (ctypes.c_int, []),
     "dc_last_error": (ctypes.c_char_p, []),
+    "dc_set_quant_division": (ctypes.c_int, [ctypes.c_int]),
+    "dc_quant_division": (ctypes.c_int, []),
     "dc_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]),
     "dc_quant_rows": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, ctypes.c_int, ctypes.c_int,
                                      _c_p, _c_p, _c_p]),

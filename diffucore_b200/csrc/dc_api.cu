@@ -28,6 +28,12 @@ namespace {
 
 thread_local char g_err[512] = "";
 
+// Division arithmetic of every per-row quantizer launch (DC_QDIV_IEEE / DC_QDIV_FULL), set by
+// dc_set_quant_division; read when a launch is enqueued.
+std::atomic<int> g_quant_div{DC_QDIV_IEEE};
+
+int quant_full_div() { return g_quant_div.load(std::memory_order_relaxed) == DC_QDIV_FULL ? 1 : 0; }
+
 int fail(const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
@@ -238,6 +244,22 @@ int launch_quant_t(const dc::RowSrc& src, int64_t M, int64_t K, int8_t* q, float
       return DC_OK;
     }
   }
+  if constexpr (!GROUP && GELU == 0 && sizeof(T) == 2) {
+    // plain 16-bit rows up to 4096 wide: a CTA per row at full occupancy (unless DC_QUANT_CTA=0)
+    const char* env = getenv("DC_QUANT_CTA");
+    if (vec && K <= 4096 && (env == nullptr || strcmp(env, "0") != 0)) {
+      const int64_t cap = static_cast<int64_t>(sm_count()) * 64;
+      const int ctas = static_cast<int>(M < cap ? M : cap);
+      const int vpt = static_cast<int>((K / 8 + 127) / 128);
+      const int Ki = static_cast<int>(K);
+      if (vpt <= 1) dc::quant_rows_cta_kernel<T, 1, SEG><<<ctas, 128, 0, st>>>(src, M, Ki, q, s);
+      else if (vpt <= 2) dc::quant_rows_cta_kernel<T, 2, SEG><<<ctas, 128, 0, st>>>(src, M, Ki, q, s);
+      else if (vpt <= 3) dc::quant_rows_cta_kernel<T, 3, SEG><<<ctas, 128, 0, st>>>(src, M, Ki, q, s);
+      else dc::quant_rows_cta_kernel<T, 4, SEG><<<ctas, 128, 0, st>>>(src, M, Ki, q, s);
+      DC_CHECK_LAUNCH("quant_rows launch");
+      return DC_OK;
+    }
+  }
   if (vec && K <= 4096) {
     // warp per row, 4 rows per CTA
     const int64_t ctas64 = (M + 3) / 4;
@@ -259,7 +281,7 @@ int launch_quant_t(const dc::RowSrc& src, int64_t M, int64_t K, int8_t* q, float
     if constexpr (!SEG) {
       const int64_t grid64 = M < static_cast<int64_t>(sm_count()) * 16 ? M : static_cast<int64_t>(sm_count()) * 16;
       dc::quant_rows_scalar_kernel<T, GELU><<<static_cast<int>(grid64), dc::kQuantThreads, 0, st>>>(
-          static_cast<const T*>(src.x), M, static_cast<int>(K), src.ldx, q, s);
+          static_cast<const T*>(src.x), M, static_cast<int>(K), src.ldx, q, s, src.full_div);
     } else {
       return fail("segmented quant_rows needs 16-byte aligned segments");
     }
@@ -271,7 +293,8 @@ int launch_quant_t(const dc::RowSrc& src, int64_t M, int64_t K, int8_t* q, float
 template <typename T>
 int launch_quant(const void* x, int64_t M, int64_t K, int64_t ldx, int group, int gelu, int8_t* q, float* s,
                  cudaStream_t st) {
-  const dc::RowSrc src = dc::plain_rows(x, ldx);
+  dc::RowSrc src = dc::plain_rows(x, ldx);
+  src.full_div = quant_full_div();
   const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(q) % 8 == 0) && K <= 16384;
   if (group != 0 && !vec) return fail("rotated quantization needs K %% 256 == 0, ldx %% 8 == 0, 16-byte aligned rows");
@@ -305,10 +328,10 @@ int launch_ln_mod_quant(const void* x, int64_t M, int64_t K, int64_t ldx, const 
   const T* xp = static_cast<const T*>(x);
   const T* sh = static_cast<const T*>(shift);
   const T* sc = static_cast<const T*>(scale);
-  if (vpt <= 4) dc::ln_mod_quant_kernel<T, 4, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s);
-  else if (vpt <= 8) dc::ln_mod_quant_kernel<T, 8, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s);
-  else if (vpt <= 12) dc::ln_mod_quant_kernel<T, 12, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s);
-  else dc::ln_mod_quant_kernel<T, 16, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s);
+  if (vpt <= 4) dc::ln_mod_quant_kernel<T, 4, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s, quant_full_div());
+  else if (vpt <= 8) dc::ln_mod_quant_kernel<T, 8, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s, quant_full_div());
+  else if (vpt <= 12) dc::ln_mod_quant_kernel<T, 12, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s, quant_full_div());
+  else dc::ln_mod_quant_kernel<T, 16, GROUP><<<ctas, 128, 0, st>>>(xp, M, Ki, ldx, sh, sc, rows_per_mod, mod_ld, q, s, quant_full_div());
   DC_CHECK_LAUNCH("ln_mod_quant launch");
   return DC_OK;
 }
@@ -789,6 +812,14 @@ extern "C" {
 
 int dc_version(void) { return DC_ABI_VERSION; }
 
+int dc_set_quant_division(int mode) {
+  if (mode != DC_QDIV_IEEE && mode != DC_QDIV_FULL) return fail("unknown quantizer division mode %d", mode);
+  g_quant_div.store(mode, std::memory_order_relaxed);
+  return DC_OK;
+}
+
+int dc_quant_division(void) { return g_quant_div.load(std::memory_order_relaxed); }
+
 const char* dc_last_error(void) { return g_err; }
 
 int dc_device_error(unsigned int* code, int clear) {
@@ -867,7 +898,7 @@ int dc_quant_rows_seg(const void* x, int x_dtype, int64_t M, int64_t K, int64_t 
   if (int r = check_sm100()) return r;
   dc::RowSrc src;
   src.x = x; src.ldx = ldx; src.seg_len = static_cast<int>(seg_len); src.seg_stride = seg_stride;
-  src.k1 = static_cast<int>(k1); src.x2 = x2; src.ldx2 = ldx2;
+  src.k1 = static_cast<int>(k1); src.x2 = x2; src.ldx2 = ldx2; src.full_div = quant_full_div();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (x_dtype == DC_DTYPE_BF16)
     return group ? launch_quant_t<__nv_bfloat16, true, 0, true>(src, M, K, q, s, true, st)
@@ -895,7 +926,8 @@ int dc_ln_mod_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (K % 256 == 0 && rows_per_mod >= M && reinterpret_cast<uintptr_t>(q) % 16 == 0 &&
       (x_dtype == DC_DTYPE_BF16 || x_dtype == DC_DTYPE_F16)) {
-    const dc::RowSrc src = dc::plain_rows(x, ldx);
+    dc::RowSrc src = dc::plain_rows(x, ldx);
+    src.full_div = quant_full_div();
     if (x_dtype == DC_DTYPE_BF16)
       return group ? launch_rowq_warp<__nv_bfloat16, true, true, false>(src, M, K, shift, scale, q, s, st)
                    : launch_rowq_warp<__nv_bfloat16, false, true, false>(src, M, K, shift, scale, q, s, st);

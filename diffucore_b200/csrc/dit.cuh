@@ -39,7 +39,7 @@ template <typename T, int VPT, bool GROUP>
 __global__ void __launch_bounds__(128)
 ln_mod_quant_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, const T* __restrict__ shift,
                     const T* __restrict__ scale, int64_t rows_per_mod, int64_t mod_ld, int8_t* __restrict__ q,
-                    float* __restrict__ s) {
+                    float* __restrict__ s, int full_div) {
   const int lane = threadIdx.x & 31;
   const int nvec = K >> 3;
   const float inv_k = 1.0f / static_cast<float>(K);
@@ -103,13 +103,13 @@ ln_mod_quant_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, cons
     float am = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    const float sc = fmaxf(__fdiv_rn(am, 127.0f), 1e-30f);
+    const float sc = row_scale(am, full_div);
     const float inv = __fdiv_rn(1.0f, sc);
     int8_t* qr = q + row * static_cast<int64_t>(K);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = lane + 32 * i;
-      if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant8(v[i], sc, inv);
+      if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant8(v[i], sc, inv, full_div);
     }
     if (lane == 0) s[row] = sc;
   }

@@ -90,15 +90,30 @@ __device__ __forceinline__ float gelu_dtype(float h, int mode) {
   return h;
 }
 
+// The four-term sums of the 256-wide ConvRot butterfly, in the order the reference's Triton
+// `_hadamard_rows` (src/diffucore/models/_int8.py:364-372) computes them for rows of 1024 and more
+// elements (measured on a B200 from that function's own output, bit for bit): the stages over the
+// base-4 digits d3 (stride 64) and d1 (stride 4) add pairs (x0 + x1) + (x2 + x3), the stage over d2
+// (stride 16) adds (x0 + x2) + (x1 + x3), the stage over d0 (stride 1) adds in sequence
+// ((x0 + x1) + x2) + x3.
 __device__ __forceinline__ float quad_sum(float a0, float a1, float a2, float a3) {
   return __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
 }
+__device__ __forceinline__ float quad_sum_02_13(float a0, float a1, float a2, float a3) {
+  return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
+}
+__device__ __forceinline__ float quad_sum_seq(float a0, float a1, float a2, float a3) {
+  return __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+}
 
-// One radix-4 stage across lanes: the digit lives in lane bits (xor masks m_lo, m_hi);
-// `flip_mask` = m_lo | m_hi selects the lane holding digit 3 - d.
-__device__ __forceinline__ float hstage_lanes(float x, int m_lo, int m_hi) {
-  const float a = __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, m_lo));   // x[d] + x[d^1]
-  const float s = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, m_hi));   // (x0+x1)+(x2+x3) in every lane
+// One radix-4 stage across lanes: the digit lives in lane bits (xor masks m_lo, m_hi for its low
+// and high bit). The first shuffle pairs the lanes whose digits differ in the bit `first` selects,
+// the second adds the pair sums: first = m_lo gives (x0 + x1) + (x2 + x3), first = m_hi gives
+// (x0 + x2) + (x1 + x3). m_lo | m_hi selects the lane holding digit 3 - d.
+__device__ __forceinline__ float hstage_lanes(float x, int m_lo, int m_hi, int first) {
+  const int second = first == m_lo ? m_hi : m_lo;
+  const float a = __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, first));
+  const float s = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, second));
   const float f = __shfl_xor_sync(0xffffffffu, x, m_lo | m_hi);          // x[3 - d]
   return __fsub_rn(s, __fmul_rn(2.0f, f));
 }
@@ -109,10 +124,10 @@ __device__ __forceinline__ float hstage_lanes(float x, int m_lo, int m_hi) {
 __device__ __forceinline__ void hadamard256_warp(float (&x)[8]) {
   // d3: lane bits 3 and 4.
 #pragma unroll
-  for (int j = 0; j < 8; ++j) x[j] = hstage_lanes(x[j], 8, 16);
-  // d2: lane bits 1 and 2.
+  for (int j = 0; j < 8; ++j) x[j] = hstage_lanes(x[j], 8, 16, 8);
+  // d2: lane bits 1 and 2, pairs (d, d + 2) first.
 #pragma unroll
-  for (int j = 0; j < 8; ++j) x[j] = hstage_lanes(x[j], 2, 4);
+  for (int j = 0; j < 8; ++j) x[j] = hstage_lanes(x[j], 2, 4, 4);
   // d1: low bit is j bit 2 (in-thread), high bit is lane bit 0.
   {
     float y[8];
@@ -133,7 +148,7 @@ __device__ __forceinline__ void hadamard256_warp(float (&x)[8]) {
     float y[8];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const float s = quad_sum(x[4 * h], x[4 * h + 1], x[4 * h + 2], x[4 * h + 3]);
+      const float s = quad_sum_seq(x[4 * h], x[4 * h + 1], x[4 * h + 2], x[4 * h + 3]);
 #pragma unroll
       for (int d = 0; d < 4; ++d) y[4 * h + d] = __fsub_rn(s, __fmul_rn(2.0f, x[4 * h + (3 - d)]));
     }
@@ -155,11 +170,12 @@ struct RowSrc {
   int k1;
   const void* x2;
   int64_t ldx2;
+  int full_div;       // 1: the quantizer divides with div.full.f32 (see row_scale)
 };
 
 __host__ __device__ inline RowSrc plain_rows(const void* x, int64_t ldx) {
   RowSrc r;
-  r.x = x; r.ldx = ldx; r.seg_len = 0; r.seg_stride = 0; r.k1 = 0; r.x2 = nullptr; r.ldx2 = 0;
+  r.x = x; r.ldx = ldx; r.seg_len = 0; r.seg_stride = 0; r.k1 = 0; r.x2 = nullptr; r.ldx2 = 0; r.full_div = 0;
   return r;
 }
 
@@ -173,8 +189,27 @@ __device__ __forceinline__ const T* src_ptr(const RowSrc& s, int64_t row, int c)
   return static_cast<const T*>(s.x2) + row * s.ldx2 + (c - s.k1);
 }
 
-__device__ __forceinline__ int8_t quant_code(float x, float scale) {
-  float t = rintf(__fdiv_rn(x, scale));
+// The two divisions of the per-row quantizer, scale = max(amax / 127, 1e-30) and
+// code = clamp(rint(x / scale), -128, 127), in one of two arithmetics:
+//   IEEE (full = 0): correctly rounded quotients, the reference's torch-op path as it runs on the
+//     CPU (src/diffucore/models/_int8.py:87-97), which the CPU oracle restates and the golden
+//     vectors pin;
+//   FULL (full = 1): the PTX full-range approximate division (div.full.f32) for both quotients, the
+//     arithmetic of the reference's Triton quantizers (`_store_quantized`, _int8.py:393-397), which
+//     is what the reference runs on a GPU; measured on a B200 to give their codes and scales bit
+//     for bit (the reference's GPU torch-op path, amax * (1/127) and IEEE codes, differs from both).
+__device__ __forceinline__ float div_full(float a, float b) {
+  float r;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+__device__ __forceinline__ float row_scale(float amax, int full) {
+  return fmaxf(full ? div_full(amax, 127.0f) : __fdiv_rn(amax, 127.0f), 1e-30f);
+}
+
+__device__ __forceinline__ int8_t quant_code(float x, float scale, int full = 0) {
+  float t = rintf(full ? div_full(x, scale) : __fdiv_rn(x, scale));
   t = fminf(fmaxf(t, -128.0f), 127.0f);
   return static_cast<int8_t>(static_cast<int>(t));
 }
@@ -188,8 +223,14 @@ __device__ __forceinline__ int8_t quant_code(float x, float scale) {
 // is bit-identical to quant_code on every element.
 constexpr float kRoundMagic = 12582912.0f;      // 1.5 * 2^23
 
-__device__ __forceinline__ uint2 quant8(const float (&v)[8], float scale, float inv_scale) {
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], float scale, float inv_scale, int full = 0) {
   uint32_t b[8];
+  if (full) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) b[j] = static_cast<uint32_t>(static_cast<uint8_t>(quant_code(v[j], scale, 1)));
+    return make_uint2(__byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410),
+                      __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410));
+  }
   uint32_t d[8];     // |y - rint(y)| as sign-cleared float bits: unsigned order == magnitude order
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -243,7 +284,7 @@ quant_rows_stream_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict_
     float amax = Vec8<T>::half_bits_to_float(max(am2 & 0xFFFFu, am2 >> 16));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    const float scale = row_scale(amax, src.full_div);
     const float inv = __fdiv_rn(1.0f, scale);
     uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(K));
     for (int v0 = lane; v0 < nvec; v0 += 32 * kBatch) {
@@ -260,11 +301,57 @@ quant_rows_stream_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict_
         if (vi < nvec) {
           float f[8];
           Vec8<T>::from_raw(raw[b], f);
-          qr[vi] = quant8(f, scale, inv);
+          qr[vi] = quant8(f, scale, inv, src.full_div);
         }
       }
     }
     if (lane == 0) s[row] = scale;
+  }
+}
+
+// Plain 16-bit rows (no rotation, no GELU), K <= 128 * 8 * VPT, K % 8 == 0, 16-byte aligned rows:
+// one 128-thread CTA per row, each thread VPT 16-byte vectors held raw in registers (few registers,
+// so 16 CTAs, the whole SM's 2048 threads, are resident and many rows' loads are in flight while
+// other rows compute). The row's abs-max is a packed 16-bit max per thread, a warp reduction and a
+// four-warp reduction through shared memory; then codes exactly as quant_rows_warp_kernel makes them.
+template <typename T, int VPT, bool SEG = false>
+__global__ void __launch_bounds__(128, 16)
+quant_rows_cta_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, float* __restrict__ s) {
+  __shared__ uint32_t red[2][4];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nvec = K >> 3;
+  int buf = 0;
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x, buf ^= 1) {
+    uint4 raw[VPT];
+    uint32_t am2 = 0u;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = tid + 128 * i;
+      raw[i] = vi < nvec ? *reinterpret_cast<const uint4*>(src_ptr<T, SEG>(src, row, vi * 8)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+      am2 = __vmaxu2(am2, __vmaxu2(__vmaxu2(raw[i].x & 0x7FFF7FFFu, raw[i].y & 0x7FFF7FFFu),
+                                   __vmaxu2(raw[i].z & 0x7FFF7FFFu, raw[i].w & 0x7FFF7FFFu)));
+    uint32_t hm = max(am2 & 0xFFFFu, am2 >> 16);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) hm = max(hm, __shfl_xor_sync(0xffffffffu, hm, o));
+    if (lane == 0) red[buf][warp] = hm;
+    __syncthreads();   // red[buf] is rewritten two rows later, after the next row's barrier
+    hm = max(max(red[buf][0], red[buf][1]), max(red[buf][2], red[buf][3]));
+    const float scale = row_scale(Vec8<T>::half_bits_to_float(hm), src.full_div);
+    const float inv = __fdiv_rn(1.0f, scale);
+    uint2* qr = reinterpret_cast<uint2*>(q + row * static_cast<int64_t>(K));
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = tid + 128 * i;
+      if (vi < nvec) {
+        float f[8];
+        Vec8<T>::from_raw(raw[i], f);
+        qr[vi] = quant8(f, scale, inv, src.full_div);
+      }
+    }
+    if (tid == 0) s[row] = scale;
   }
 }
 
@@ -329,7 +416,7 @@ quant_rows_warp_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ 
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    const float scale = row_scale(amax, src.full_div);
     const float inv = __fdiv_rn(1.0f, scale);
     int8_t* qr = q + row * static_cast<int64_t>(K);
 #pragma unroll
@@ -340,9 +427,9 @@ quant_rows_warp_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ 
         if (kRaw) {
           float f[8];
           Vec8<T>::from_raw(raw[kRaw ? i : 0], f);
-          w = quant8(f, scale, inv);
+          w = quant8(f, scale, inv, src.full_div);
         } else {
-          w = quant8(v[kRaw ? 0 : i], scale, inv);
+          w = quant8(v[kRaw ? 0 : i], scale, inv, src.full_div);
         }
         *reinterpret_cast<uint2*>(qr + vi * 8) = w;
       }
@@ -392,13 +479,13 @@ quant_rows_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, fl
 #pragma unroll
     for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
     __syncthreads();
-    const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    const float scale = row_scale(amax, src.full_div);
     const float inv = __fdiv_rn(1.0f, scale);
     int8_t* qr = q + row * static_cast<int64_t>(K);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = tid + i * kQuantThreads;
-      if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant8(v[i], scale, inv);
+      if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant8(v[i], scale, inv, src.full_div);
     }
     if (tid == 0) s[row] = scale;
   }
@@ -408,7 +495,7 @@ quant_rows_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, fl
 template <typename T, int GELU>
 __global__ void __launch_bounds__(kQuantThreads)
 quant_rows_scalar_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, int8_t* __restrict__ q,
-                         float* __restrict__ s) {
+                         float* __restrict__ s, int full_div) {
   __shared__ float red[kQuantThreads / 32];
   const int tid = threadIdx.x;
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
@@ -427,12 +514,12 @@ quant_rows_scalar_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx,
 #pragma unroll
     for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
     __syncthreads();
-    const float scale = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    const float scale = row_scale(amax, full_div);
     int8_t* qr = q + row * static_cast<int64_t>(K);
     for (int c = tid; c < K; c += kQuantThreads) {
       float t = Vec8<T>::one(xr + c);
       if (GELU != kGeluNone) t = gelu_dtype<T>(t, GELU);
-      qr[c] = quant_code(t, scale);
+      qr[c] = quant_code(t, scale, full_div);
     }
     if (tid == 0) s[row] = scale;
   }

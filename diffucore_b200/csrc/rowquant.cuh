@@ -10,8 +10,9 @@
 //   transpose through a swizzled scratch (word 16 (e >> 4) + ((e & 15) ^ (e >> 4 & 15)), so both
 //   the stores of X and the loads of Y hit 32 distinct banks);
 //   layout Y: lane L holds e = 16 L + c (c = 4 d1 + d0): stages d1, d0 in registers, then x 1/16.
-// Each stage computes S = (x[d=0] + x[d=1]) + (x[d=2] + x[d=3]) and y = S - 2 x[3 - d], in the
-// order the warp-shuffle butterfly of quant.cuh (and the CPU oracle) uses, so codes and scales are
+// Each stage computes S, the sum of the four x[d], and y = S - 2 x[3 - d], with the sums in the
+// order of the reference's Triton butterfly (quad_sum, quad_sum_02_13, quad_sum_seq in quant.cuh),
+// which the warp-shuffle butterfly of quant.cuh and the CPU oracle use too, so codes and scales are
 // bit-identical to it. Without rotation the same kernels read layout Y directly.
 //
 //   rowq_warp_kernel  one warp per row, K <= 4096 (K % 256 == 0); optionally LayerNorm + AdaLN
@@ -46,11 +47,14 @@ __device__ __forceinline__ void r4_outer(float (&x)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) x[i] = y[i];
 }
+// SEQ: the four terms added in sequence (the d0 stage), else as (x0 + x2) + (x1 + x3) (the d2 stage).
+template <bool SEQ>
 __device__ __forceinline__ void r4_inner(float (&x)[16]) {
   float y[16];
 #pragma unroll
   for (int a = 0; a < 4; ++a) {
-    const float s = quad_sum(x[4 * a], x[4 * a + 1], x[4 * a + 2], x[4 * a + 3]);
+    const float s = SEQ ? quad_sum_seq(x[4 * a], x[4 * a + 1], x[4 * a + 2], x[4 * a + 3])
+                        : quad_sum_02_13(x[4 * a], x[4 * a + 1], x[4 * a + 2], x[4 * a + 3]);
 #pragma unroll
     for (int b = 0; b < 4; ++b) y[4 * a + b] = __fsub_rn(s, __fmul_rn(2.0f, x[4 * a + 3 - b]));
   }
@@ -64,7 +68,7 @@ constexpr int kRotScratch = 272;   // floats per half-warp: 256 + 16 so the two 
 // layout Y (times 1/16). Both halves of the warp must call it together (it syncs the warp).
 __device__ __forceinline__ void rotate256_half(float (&x)[16], float* scr, int L) {
   r4_outer(x);                      // d3
-  r4_inner(x);                      // d2
+  r4_inner<false>(x);               // d2
 #pragma unroll
   for (int i = 0; i < 16; ++i) scr[16 * i + (L ^ i)] = x[i];       // e >> 4 == i, e & 15 == L
   __syncwarp();
@@ -72,7 +76,7 @@ __device__ __forceinline__ void rotate256_half(float (&x)[16], float* scr, int L
   for (int c = 0; c < 16; ++c) x[c] = scr[16 * L + (c ^ L)];
   __syncwarp();
   r4_outer(x);                      // d1
-  r4_inner(x);                      // d0
+  r4_inner<true>(x);                // d0
 #pragma unroll
   for (int c = 0; c < 16; ++c) x[c] = __fmul_rn(x[c], 0.0625f);
 }
@@ -111,11 +115,11 @@ __device__ __forceinline__ int group_col(int g, int L, int i) {
 }
 
 // Codes of a group's 16 values (layout Y: 16 consecutive columns) -> one 16-byte store.
-__device__ __forceinline__ void store_codes16(int8_t* dst, const float (&v)[16], float scale, float inv) {
+__device__ __forceinline__ void store_codes16(int8_t* dst, const float (&v)[16], float scale, float inv, int full) {
   float a[8], b[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) { a[j] = v[j]; b[j] = v[8 + j]; }
-  const uint2 lo = quant8(a, scale, inv), hi = quant8(b, scale, inv);
+  const uint2 lo = quant8(a, scale, inv, full), hi = quant8(b, scale, inv, full);
   *reinterpret_cast<uint4*>(dst) = make_uint4(lo.x, lo.y, hi.x, hi.y);
 }
 
@@ -210,13 +214,13 @@ rowq_warp_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift
     float am = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    const float scale = fmaxf(__fdiv_rn(am, 127.0f), 1e-30f);
+    const float scale = row_scale(am, src.full_div);
     const float inv = __fdiv_rn(1.0f, scale);
     int8_t* qr = q + row * static_cast<int64_t>(K);
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int g = 2 * it + half;
-      if (g < ng) store_codes16(qr + 256 * g + 16 * L, vals[it], scale, inv);
+      if (g < ng) store_codes16(qr + 256 * g + 16 * L, vals[it], scale, inv, src.full_div);
     }
     if (lane == 0) s[row] = scale;
     __syncwarp();
@@ -276,13 +280,13 @@ rowq_cta_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, floa
     am = red[0];
 #pragma unroll
     for (int w = 1; w < 8; ++w) am = fmaxf(am, red[w]);
-    const float scale = fmaxf(__fdiv_rn(am, 127.0f), 1e-30f);
+    const float scale = row_scale(am, src.full_div);
     const float inv = __fdiv_rn(1.0f, scale);
     int8_t* qr = q + row * static_cast<int64_t>(K);
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int g = 16 * it + hw;
-      if (g < ng) store_codes16(qr + 256 * g + 16 * L, vals[it], scale, inv);
+      if (g < ng) store_codes16(qr + 256 * g + 16 * L, vals[it], scale, inv, src.full_div);
     }
     if (threadIdx.x == 0) s[row] = scale;
     __syncthreads();                     // row buffer and red[] free again
@@ -326,11 +330,13 @@ __device__ __forceinline__ void r4_outer2(float2 (&x)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) x[i] = y[i];
 }
+template <bool SEQ>
 __device__ __forceinline__ void r4_inner2(float2 (&x)[16]) {
   float2 y[16];
 #pragma unroll
   for (int a = 0; a < 4; ++a) {
-    const float2 s = add2(add2(x[4 * a], x[4 * a + 1]), add2(x[4 * a + 2], x[4 * a + 3]));
+    const float2 s = SEQ ? add2(add2(add2(x[4 * a], x[4 * a + 1]), x[4 * a + 2]), x[4 * a + 3])
+                         : add2(add2(x[4 * a], x[4 * a + 2]), add2(x[4 * a + 1], x[4 * a + 3]));
 #pragma unroll
     for (int b = 0; b < 4; ++b) y[4 * a + b] = sub_twice2(s, x[4 * a + 3 - b]);
   }
@@ -343,7 +349,7 @@ constexpr int kRotScratch2 = 256;   // float2 per half-warp (64-bit accesses: on
 // rotate256_half on pairs: layout X in, layout Y (times 1/16) out; both halves call it together.
 __device__ __forceinline__ void rotate256_pair(float2 (&x)[16], float2* scr, int L) {
   r4_outer2(x);                     // d3
-  r4_inner2(x);                     // d2
+  r4_inner2<false>(x);              // d2
 #pragma unroll
   for (int i = 0; i < 16; ++i) scr[16 * i + (L ^ i)] = x[i];
   __syncwarp();
@@ -351,7 +357,7 @@ __device__ __forceinline__ void rotate256_pair(float2 (&x)[16], float2* scr, int
   for (int c = 0; c < 16; ++c) x[c] = scr[16 * L + (c ^ L)];
   __syncwarp();
   r4_outer2(x);                     // d1
-  r4_inner2(x);                     // d0
+  r4_inner2<true>(x);               // d0
 #pragma unroll
   for (int c = 0; c < 16; ++c) x[c] = mul2(x[c], make_float2(0.0625f, 0.0625f));
 }
@@ -448,7 +454,7 @@ rowq_pair_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift
     float am = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    const float scale = fmaxf(__fdiv_rn(am, 127.0f), 1e-30f);
+    const float scale = row_scale(am, src.full_div);
     const float inv = __fdiv_rn(1.0f, scale);
     int8_t* qr = q + row * static_cast<int64_t>(K);
 #pragma unroll
@@ -457,8 +463,8 @@ rowq_pair_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift
       float va[16], vb[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) { va[c] = vals[j][c].x; vb[c] = vals[j][c].y; }
-      if (ga < ng) store_codes16(qr + 256 * ga + 16 * L, va, scale, inv);
-      if (gb < ng) store_codes16(qr + 256 * gb + 16 * L, vb, scale, inv);
+      if (ga < ng) store_codes16(qr + 256 * ga + 16 * L, va, scale, inv, src.full_div);
+      if (gb < ng) store_codes16(qr + 256 * gb + 16 * L, vb, scale, inv, src.full_div);
     }
     if (lane == 0) s[row] = scale;
     __syncwarp();
@@ -518,7 +524,7 @@ rowq_cta_pair_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q,
     am = red[0];
 #pragma unroll
     for (int w = 1; w < 8; ++w) am = fmaxf(am, red[w]);
-    const float scale = fmaxf(__fdiv_rn(am, 127.0f), 1e-30f);
+    const float scale = row_scale(am, src.full_div);
     const float inv = __fdiv_rn(1.0f, scale);
     int8_t* qr = q + row * static_cast<int64_t>(K);
 #pragma unroll
@@ -527,8 +533,8 @@ rowq_cta_pair_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q,
       float va[16], vb[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) { va[c] = vals[j][c].x; vb[c] = vals[j][c].y; }
-      if (ga < ng) store_codes16(qr + 256 * ga + 16 * L, va, scale, inv);
-      if (gb < ng) store_codes16(qr + 256 * gb + 16 * L, vb, scale, inv);
+      if (ga < ng) store_codes16(qr + 256 * ga + 16 * L, va, scale, inv, src.full_div);
+      if (gb < ng) store_codes16(qr + 256 * gb + 16 * L, vb, scale, inv, src.full_div);
     }
     if (threadIdx.x == 0) s[row] = scale;
     __syncthreads();                     // row buffer and red[] free again

@@ -41,8 +41,24 @@ extern "C" {
 #define DC_ATTN_MODE_REF 0      /* Q per token, K per 64 keys after subtracting K's mean */
 #define DC_ATTN_MODE_BLOCK64 1  /* Q and K per 64-token block, symmetric abs-max */
 
+#define DC_QDIV_IEEE 0          /* correctly rounded divisions: the reference's torch-op (CPU) path */
+#define DC_QDIV_FULL 1          /* div.full.f32 divisions: the reference's Triton (GPU) quantizers */
+
 int dc_version(void);
 const char* dc_last_error(void);
+
+/* Division arithmetic of the per-row activation quantizers (dc_quant_rows, dc_quant_rows_seg,
+ * dc_ln_mod_quant and the GEMM callers' codes), process-wide, taking effect for launches enqueued
+ * after the call. The reference computes the two quotients of its quantizer,
+ * scale = max(amax / 127, 1e-30) and code = rint(x / scale), differently depending on where it runs:
+ * its torch-op path on the CPU (src/diffucore/models/_int8.py:87-97) rounds both correctly
+ * (DC_QDIV_IEEE, the default: bit-exact with that path), its Triton kernels on a GPU
+ * (`_store_quantized`, _int8.py:393-397, behind `quantize_activation` :299-310) divide with
+ * div.full.f32 (DC_QDIV_FULL: bit-exact with those kernels). The two differ by one code step at
+ * ~1.5e-4 of elements. The attention's Q/K codes follow the reference's CUDA kernels, whose
+ * divisions are correctly rounded, in both modes. dc_quant_division() returns the current mode. */
+int dc_set_quant_division(int mode);
+int dc_quant_division(void);
 
 /* Read (and optionally clear) the device-global error word that bounded in-kernel waits set
  * when they give up (1 = a wait timed out, 2 = the timeout self-test fired). Synchronous. */

@@ -242,3 +242,22 @@ def test_fused_mlp_matches_reference_unfused():
     h = torch_ref.int8_linear(x, l1.weight.cpu(), l1.scale.cpu(), None, l1.group)
     y_ref = torch_ref.int8_linear(torch.nn.functional.gelu(h), l2.weight.cpu(), l2.scale.cpu(), None, l2.group)
     assert _rel(y, y_ref) < 2e-3
+
+
+@pytest.mark.parametrize("M,K,dtype", [(4096, 3072, torch.bfloat16), (300, 640, torch.float16), (5, 4096, torch.bfloat16),
+                                       (129, 8, torch.float16), (64, 1000, torch.bfloat16)])
+@pytest.mark.parametrize("division", ["ieee", "triton"])
+def test_cta_per_row_quantizer_equals_warp_kernel(monkeypatch, M, K, dtype, division):
+    """The CTA-per-row quantizer that plain 16-bit rows up to 4096 wide now take gives the warp-per-row
+    kernel's codes and scales bit for bit (DC_QUANT_CTA=0 selects the latter), in both divisions."""
+    g = torch.Generator().manual_seed(M + K)
+    x = (torch.randn(M, K, generator=g) * 3).to(dtype).to(DEV)
+    _int8.set_quant_division(division)
+    try:
+        monkeypatch.setenv("DC_QUANT_CTA", "0")
+        qw, sw = kernels.quant_rows(x, 0)
+        monkeypatch.delenv("DC_QUANT_CTA")
+        qc, sc = kernels.quant_rows(x, 0)
+    finally:
+        _int8.set_quant_division("ieee")
+    assert torch.equal(qw, qc) and torch.equal(sw, sc)

@@ -92,3 +92,20 @@ def test_pointer_validation_without_gpu():
     assert lib.dc_qk_norm_rope(a16, _lib.DTYPE_BF16, 4, 2, 128, 768, 0, 256, a16, a16, None, None, 4,
                                a16 + 8, 0, None) != 0
     assert b"16-byte" in lib.dc_last_error()
+
+
+def test_quant_division_setting_round_trips():
+    """The quantizer's division mode is host state: settable and readable without a GPU, unknown
+    modes refused, IEEE (the reference's CPU arithmetic) by default."""
+    from diffucore_b200 import _int8
+    lib = _lib.load()
+    assert lib.dc_quant_division() == _lib.QDIV_IEEE
+    assert lib.dc_set_quant_division(7) != 0 and b"division" in lib.dc_last_error()
+    try:
+        _int8.set_quant_division("triton")
+        assert lib.dc_quant_division() == _lib.QDIV_FULL and _int8.quant_division() == "triton"
+        with pytest.raises(ValueError):
+            _int8.set_quant_division("fast")
+    finally:
+        _int8.set_quant_division("ieee")
+    assert _int8.quant_division() == "ieee"

@@ -39,10 +39,14 @@ def _r4_outer(x):                     # x: [16, lanes]
     return y
 
 
-def _r4_inner(x):
+def _r4_inner(x, seq):
+    """Sum over the inner digit in sequence (the d0 stage) or as (x0 + x2) + (x1 + x3) (the d2 stage)."""
     y = np.empty_like(x)
     for a in range(4):
-        s = ((x[4 * a] + x[4 * a + 1]).astype(F) + (x[4 * a + 2] + x[4 * a + 3]).astype(F)).astype(F)
+        if seq:
+            s = (((x[4 * a] + x[4 * a + 1]).astype(F) + x[4 * a + 2]).astype(F) + x[4 * a + 3]).astype(F)
+        else:
+            s = ((x[4 * a] + x[4 * a + 2]).astype(F) + (x[4 * a + 1] + x[4 * a + 3]).astype(F)).astype(F)
         for b in range(4):
             y[4 * a + b] = _sub_twice(s, x[4 * a + 3 - b])
     return y
@@ -50,7 +54,7 @@ def _r4_inner(x):
 
 def _rotate_half_warp(x):
     """rotate256_pair for one slot (.x or .y) of the 16 lanes: x [16 values, 16 lanes]."""
-    x = _r4_inner(_r4_outer(x))
+    x = _r4_inner(_r4_outer(x), False)
     scr = np.zeros(256, dtype=F)
     for L in range(16):
         for i in range(16):
@@ -59,7 +63,7 @@ def _rotate_half_warp(x):
     for L in range(16):
         for c in range(16):
             y[c, L] = scr[16 * L + (c ^ L)]
-    y = _r4_inner(_r4_outer(y))
+    y = _r4_inner(_r4_outer(y), True)
     return (y * F(0.0625)).astype(F)
 
 
