@@ -624,10 +624,9 @@ def _cpu_flux_baseline() -> dict:
     r = step.sample()
     return {"value": r["s_step"], "unit": "s/step", "cores": step.threads, "kind": "port", "extrapolated": True,
             "s_per_double_block": r["double"], "s_per_single_block": r["single"], "s_rest_of_forward": r["rest"],
-            "sample": "one double- and one single-stream block of the full-width FLUX.1 architecture at "
-                      "1024^2 (512 + 4096 tokens), measured; step = 19 x double + 38 x single + rest",
-            "note": "the reference's CPU path: torch-op W8A8 linears (torch._int_mm), SDPA attention, bf16",
-            "finite": r["finite"], "build_s": step.build_s, "cpu": _cpu_model()}
+            "sample": "1 double + 1 single full-width block at 1024^2, measured; step = 19 x double + "
+                      "38 x single + rest (torch-op int8 linears, SDPA, bf16)",
+            "finite": r["finite"]}
 
 
 def bench_flux(args, world, rank, dev, peaks, sides=(1024, 2048), cpu_baseline: bool = False) -> dict:
@@ -847,9 +846,9 @@ def flux_config(world: int) -> dict:
             "image_tokens": (FLUX_SIDE // 16) ** 2, "text_tokens": FLUX_TXT, "batch": 1, "hidden": 3072, "heads": 24,
             "head_dim": 128, "blocks": "19 double + 38 single", "linears": "W8A8, ConvRot 256",
             "attention": "INT8, reference quant mode", "sampler": "euler, 4-step schedule repeated, shift 1",
-            "parallelism": (f"ulysses x{world}: tokens split over the ranks, NCCL all-to-all of q/k/v and of the "
-                            "attention output around every attention" if world > 1 else "one GPU"),
-            "l2": "each step streams ~12 GB of weights (> 126 MB L2)", "graph": "one CUDA graph per forward"}
+            "parallelism": (f"ulysses x{world}: tokens split over the ranks, NCCL all-to-all of q/k/v and "
+                            "attention output" if world > 1 else "one GPU"),
+            "l2": "~12 GB of weights streamed per step (> 126 MB L2)", "graph": "one CUDA graph per forward"}
 
 
 # GPU kernel launches of this library per runner op (attention in the reference's quant mode:
@@ -981,8 +980,7 @@ def bench_flux_headline(args, world, rank, dev, peaks, sampler) -> dict:
         dist.all_reduce(tot)
         bi, bo = int(tot[0].item()), int(tot[1].item())
     e2e = {"value": e2e_s, "unit": "s/step", "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
-           "steps": args.steps, "api": "FluxGraph (captured FluxRunner.forward) + Euler update, pinned host latent "
-                                     "and text rows in, updated latent out, every step"}
+           "steps": args.steps, "api": "FluxGraph + Euler update; pinned host latent/text in, latent out"}
 
     # per-op GPU time of one eager forward (events around every runner op): the dominant kernel's
     # achieved rate, the other hot kernels, and the launches per forward
@@ -1043,11 +1041,9 @@ def bench_flux_headline(args, world, rank, dev, peaks, sampler) -> dict:
         "gpu_launches": launches * args.steps,
         "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": peak, "unit": "TOPS",
                      "frac": gemm_tops / peak if gemm_tops else None, "traffic": None,
-                     "kernel": "gemm_w8a8_kernel: every W8A8 block GEMM of one forward, ops-weighted (events per launch)",
-                     "peak_source": f"2 x bf16_tflops ({peaks['source']}); nominal dense INT8 4500 TOPS",
-                     "step": {"roofline_s": roof, "frac": roof / s_step,
-                              "note": "int8 ops at the INT8 peak + P.V at the bf16 peak, / N; at N > 1 at least the "
-                                      "all-to-all bytes at 770 GB/s"}},
+                     "kernel": "gemm_w8a8_kernel, all block GEMMs of a forward, ops-weighted",
+                     "peak_source": f"2 x bf16_tflops ({peaks['source']})",
+                     "step": {"roofline_s": roof, "frac": roof / s_step}},
         "parity_vs_1gpu": parity, "finite": finite,
     }
     head["roofline"]["kernels"] = {"attention_flux": {
@@ -1097,7 +1093,14 @@ def bench_reference_gpu(args, dev) -> dict:
         our_layer = _int8.Int8Linear.from_linear(lin, group=0)
         xs = [torch.randn(GEMM_M, GEMM_K, generator=g).to(torch.bfloat16).to(dev) for _ in range(6)]
         with torch.no_grad():
-            same = bool(torch.equal(ref_layer(xs[0]), our_layer(xs[0])))
+            # bit-identity with the reference's GPU arithmetic (its Triton kernels divide with
+            # div.full.f32); the timing below uses this library's default (correctly rounded) division
+            prev = _int8.quant_division()
+            _int8.set_quant_division("triton")
+            try:
+                same = bool(torch.equal(ref_layer(xs[0]), our_layer(xs[0])))
+            finally:
+                _int8.set_quant_division(prev)
             ref_ms = timeit(lambda i: ref_layer(xs[i % 6]))
             our_ms = timeit(lambda i: our_layer(xs[i % 6]))
             # the reference's three steps alone
@@ -1108,7 +1111,7 @@ def bench_reference_gpu(args, dev) -> dict:
                      "rescale_ms": timeit(lambda i: ref.rescale(accs[i % 2], rq[i % 2][1], ref_layer.scale,
                                                                 ref_layer.bias, torch.bfloat16))}
         out["w8a8_linear_config1"] = {"reference_ms": ref_ms, "ours_ms": our_ms, "speedup": ref_ms / our_ms,
-                                      "outputs_bit_identical": same, "reference_parts": parts,
+                                      "bit_identical_triton_division": same, "reference_parts": parts,
                                       "reference_path": "Triton _rot_quant_kernel + torch._int_mm + Triton _rescale_kernel"}
         del rq, accs
         del xs
@@ -1322,9 +1325,11 @@ def bench_variants(args, dev, peaks) -> dict:
 
 
 def bench_rowq(args, dev, peaks) -> dict:
-    """The rotated row quantizers at FLUX row widths (bf16, group 256): the packed-pair kernels (the
-    default) against the one-group kernels (DC_ROWQ_PAIR=0), same inputs rotating over sets larger
-    than L2. Device us per call and GB/s of 2 B read + 1 B written per element."""
+    """The row quantizers at FLUX row widths (bf16, group 256), same inputs rotating over sets
+    larger than L2: the register-row kernel (the default), the packed-pair shared-memory kernels
+    (DC_ROWQ_REG=0) and the one-group kernels (DC_ROWQ_REG=0 DC_ROWQ_PAIR=0); plain config-1 rows
+    (no rotation) through the register-row kernel (DC_ROWQ_REG=2) against their default kernel.
+    Device us per call and GB/s of 2 B read + 1 B written per element."""
     import torch
     from diffucore_b200 import _lib, kernels
     g = torch.Generator(device=dev).manual_seed(11)
@@ -1346,12 +1351,22 @@ def bench_rowq(args, dev, peaks) -> dict:
              ("quant_rows 4608x15360 group 256",
               lambda i: kernels.quant_rows_into(wide[i % 2], 256, qbuf, sbuf), M * W))
     out = {"unit": "us per call", "peak_hbm_gbs": peaks["hbm_gbs"]}
+    variants = (("one_group", {"DC_ROWQ_REG": "0", "DC_ROWQ_PAIR": "0"}),
+                ("pair", {"DC_ROWQ_REG": "0", "DC_ROWQ_PAIR": None}),
+                ("register", {"DC_ROWQ_REG": None, "DC_ROWQ_PAIR": None}))
     for name, fn, elems in cases:
         row = {}
-        for tag, env in (("one_group", {"DC_ROWQ_PAIR": "0"}), ("pair", {"DC_ROWQ_PAIR": None})):
+        for tag, env in variants:
             ms = _time_env(fn, env, warm, steps)
             row[tag] = {"us": round(ms * 1e3, 2), "gbs": round(elems * 3 / ms / 1e6, 1)}
         out[name] = row
+    plain = [torch.randn(GEMM_M, GEMM_K, generator=g, device=dev).to(torch.bfloat16) for _ in range(6)]
+    fn = lambda i: kernels.quant_rows_into(plain[i % 6], 0, qbuf[:GEMM_M, :GEMM_K], sbuf[:GEMM_M])  # noqa: E731
+    row = {}
+    for tag, env in (("default", {"DC_ROWQ_REG": None}), ("register", {"DC_ROWQ_REG": "2"})):
+        ms = _time_env(fn, env, warm, steps)
+        row[tag] = {"us": round(ms * 1e3, 2), "gbs": round(GEMM_M * GEMM_K * 3 / ms / 1e6, 1)}
+    out[f"quant_rows {GEMM_M}x{GEMM_K} plain (config 1)"] = row
     out["device_error"] = _lib.device_error()
     return out
 
@@ -1454,8 +1469,8 @@ def main() -> int:
     line = {
         "metric": METRIC, "value": head["value"], "unit": "s/step", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": False, "scaling": "strong",
-        "vs_baseline": None, "dtype": "int8 W8A8 GEMMs + int8 QK^T / bf16 P.V attention, bf16 activations",
-        "data": "synthetic: seeded random-init bf16 weights (no checkpoint), N(0,1) latent, text and pooled vector",
+        "vs_baseline": None, "dtype": "int8 (GEMMs, QK^T) + bf16 (P.V, activations)",
+        "data": "synthetic: seeded random bf16 weights, N(0,1) latent/text/pooled",
         "config": flux_config(world),
         "parity_vs_1gpu": head["parity_vs_1gpu"],
         "roofline": head["roofline"], "clocks": head["clocks"], "e2e": head["e2e"],
@@ -1473,8 +1488,7 @@ def main() -> int:
             att = _guarded(bench_attention_config2, args, world, dev, peaks)
             details["attention_config2"] = att
             kern["attention_config2"] = _compact(att, ["tops", "kernel_ms", "prep_ms", "roofline.achieved",
-                                                       "roofline.frac", "roofline.mixed.frac", "ref_mode.tops",
-                                                       "e2e.value"])
+                                                       "roofline.frac", "roofline.mixed.frac", "ref_mode.tops"])
             gem = _guarded(bench_gemm, args, dev, peaks, cpu_baseline=False)
             details["w8a8_linear_config1"] = gem
             kern["gemm_config1"] = _compact(gem, ["gemm.ms", "gemm.roofline.achieved", "gemm.roofline.frac",
@@ -1483,8 +1497,8 @@ def main() -> int:
                                                        "quantizer.roofline.frac"])
             ref_gpu = _guarded(bench_reference_gpu, args, dev)
             details["reference_gpu"] = ref_gpu
-            extras["reference_gpu"] = {k: _compact(v, ["reference_ms", "ours_ms", "speedup", "outputs_bit_identical",
-                                                       "cos_vs_reference"])
+            extras["reference_gpu"] = {k: _compact(v, ["reference_ms", "ours_ms", "speedup",
+                                                       "bit_identical_triton_division", "cos_vs_reference"])
                                        for k, v in ref_gpu.items()} if "error" not in ref_gpu else ref_gpu
         fl = _guarded(bench_flux, args, world, rank, dev, peaks, sides=(2048,))
         details["flux_2048"] = fl

@@ -276,8 +276,11 @@ __device__ __forceinline__ void mask_tail64(uint32_t (&r)[64], int valid) {
 // add, so s * c - m = fma(x, c, -(1.5 * 2^23 * c + m)) = fma(x, c, nb), two keys per packed FMA,
 // exp2 on the MUFU. Keys at or past `valid` get p = 0 (TAIL only). The sum of p goes to `lsum`
 // (four independent accumulators, so no long dependency chain); P as 16-bit pairs to pk[0..31].
-// (exp2_poly2 above can take a share of the exponentials off the MUFU; measured on this kernel
-// it did not pay while the softmax is latency- rather than MUFU-bound.)
+// (Measured on a B200: this loop alone, two warps per SM sub-partition, takes 1048 cycles per 64
+// keys, MUFU-bound; with a quarter of the exponentials on the FMA pipe (exp2_poly2) 871. In the
+// whole kernel at B=1, H=24, L=4608, D=128 that share changed nothing, 253.8 against 252.6 us:
+// there one softmax warp alone on its sub-partition takes ~780 cycles per 64 keys, issue- rather
+// than MUFU-bound.)
 template <bool BF16, bool TAIL>
 __device__ __forceinline__ void p_half(const uint32_t (&r)[64], float c, float nb, int valid, float2& lsum,
                                        uint32_t* pk) {

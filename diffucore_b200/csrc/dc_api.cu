@@ -155,9 +155,42 @@ int launch_rowq_pair(const dc::RowSrc& src, int64_t M, int64_t K, const void* sh
   return DC_OK;
 }
 
+// Rows held in registers, one CTA per row (rowq_reg_kernel): the default for rotated 16-bit rows
+// and LayerNorm + modulation rows, K % 256 == 0 up to 16384 wide (segmented rows: segments of 256
+// columns or more). DC_ROWQ_REG=0 selects the shared-memory streaming kernels below; =2 also
+// sends plain (unrotated) rows to it.
+int rowq_reg_mode() {
+  const char* env = getenv("DC_ROWQ_REG");
+  if (env == nullptr) return 1;
+  return atoi(env);
+}
+
+template <typename T, bool LNMOD, bool ROT, bool SEG>
+int launch_rowq_reg(const dc::RowSrc& src, int64_t M, int64_t K, const void* shift, const void* scale, int8_t* q,
+                    float* s, cudaStream_t st) {
+  const int nw = static_cast<int>((K / 256 + 3) / 4);
+  const int threads = 32 * nw;
+  const size_t smem = static_cast<size_t>(nw) * 4 * dc::kRegBlk * sizeof(float) +
+                      (LNMOD ? static_cast<size_t>(2) * 16 * threads * sizeof(float2) : 0);
+  auto kernel = dc::rowq_reg_kernel<T, LNMOD, ROT, SEG>;
+  if (int r = set_smem(kernel, static_cast<int>(smem))) return r;
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  const int64_t cap = static_cast<int64_t>(sm_count()) * (per_sm > 0 ? per_sm : 1);
+  const int ctas = static_cast<int>(M < cap ? M : cap);
+  kernel<<<ctas, threads, smem, st>>>(src, M, static_cast<int>(K), static_cast<const T*>(shift),
+                                      static_cast<const T*>(scale), q, s);
+  DC_CHECK_LAUNCH("quant_rows launch");
+  return DC_OK;
+}
+
 template <typename T, bool GROUP, bool LNMOD, bool SEG>
 int launch_rowq_warp(const dc::RowSrc& src, int64_t M, int64_t K, const void* shift, const void* scale, int8_t* q,
                      float* s, cudaStream_t st) {
+  if constexpr (LNMOD && !SEG) {
+    if (rowq_reg_mode() != 0) return launch_rowq_reg<T, true, GROUP, false>(src, M, K, shift, scale, q, s, st);
+  }
   if constexpr (GROUP && !(LNMOD && SEG)) {
     if (use_rowq_pair()) return launch_rowq_pair<T, LNMOD, SEG>(src, M, K, shift, scale, q, s, st);
   }
@@ -231,6 +264,10 @@ int launch_quant_t(const dc::RowSrc& src, int64_t M, int64_t K, int8_t* q, float
     // Shared-memory streaming kernels where they pay: with the ConvRot rotation (no warp-shuffle
     // butterfly), and for wide rows (no second pass over rows L2 has evicted). Plain rows up to
     // 4096 wide keep the register warp kernel below, which has more rows in flight per SM.
+    const int reg = rowq_reg_mode();
+    if (vec && K % 256 == 0 && K <= 16384 && reinterpret_cast<uintptr_t>(q) % 16 == 0 &&
+        (reg == 2 || (reg == 1 && GROUP)) && (!SEG || src.seg_len >= 256))
+      return launch_rowq_reg<T, false, GROUP, SEG>(src, M, K, nullptr, nullptr, q, s, st);
     if (vec && K % 256 == 0 && K <= 16384 && reinterpret_cast<uintptr_t>(q) % 16 == 0 && (GROUP || K > 4096))
       return K <= 4096 ? launch_rowq_warp<T, GROUP, false, SEG>(src, M, K, nullptr, nullptr, q, s, st)
                        : launch_rowq_cta<T, GROUP, SEG>(src, M, K, q, s, st);
@@ -347,16 +384,17 @@ struct GemmEpi {
   int64_t block_stride = 0;
 };
 
-// Pair tiles (256 x 256 over a cluster of two CTAs, see gemm.cuh): the default for wide GEMMs of at
-// least 512 rows without a GELU epilogue, where they measured 1-4 % faster on a B200 than the
-// one-CTA tile (config 1: 41.5 vs 42.0 us; FLUX qkv 104.3 vs 108.2; linear2 155.4 vs 161.4) with
-// bit-identical results; with the GELU epilogue they were not faster (168.1 vs 166.9). Environment
-// DC_GEMM_PAIR = "0" turns them off, "1" uses them wherever M > 128.
+// Pair tiles (256 x 256 over a cluster of two CTAs, see gemm.cuh): the default for GEMMs of at
+// least 512 rows, where with 256-byte k-blocks they measured faster on a B200 than the one-CTA
+// tile with bit-identical results (config 1: 40.0 vs 41.8 us; FLUX qkv 100.0 vs 108.1; linear2
+// 145.2 vs 161.7; the GELU up-projection 156.9 vs 166.4). Environment DC_GEMM_PAIR = "0" turns
+// them off, "1" uses them wherever M > 128.
 bool use_pair_gemm(int64_t M, int gelu) {
+  (void)gelu;
   const char* env = getenv("DC_GEMM_PAIR");
   if (env != nullptr && strcmp(env, "0") == 0) return false;
   if (env != nullptr && strcmp(env, "1") == 0) return M > dc::kGemmBM;
-  return gelu == 0 && M >= 512;
+  return M >= 512;
 }
 
 // Largest number of two-CTA clusters of `kernel` resident at once on the current device.
@@ -388,22 +426,27 @@ template <int BN, int OUT, bool HAS_BIAS, int GELU, bool GATED, bool PAIR = fals
 int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* sw,
                 const void* bias, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K, const GemmEpi& epi,
                 cudaStream_t st) {
-  constexpr int STAGES = PAIR ? 6 : (BN == 256 ? 4 : 6);
+  // Pair and 128-wide tiles stage 256-byte k-blocks (two swizzle atoms) in 3 stages of 64 KB; the
+  // one-CTA 256-wide tile 128-byte k-blocks in 4 stages of 48 KB. Measured on a B200: the 256-byte
+  // k-blocks took config 1 from 41.1 to 40.0 us, FLUX's qkv from 104.3 to 100.0 us and linear2
+  // from 155.4 to 145.2 us (pair tiles).
+  constexpr int KATOMS = (PAIR || BN == 128) ? 2 : 1;
+  constexpr int STAGES = KATOMS == 2 ? 3 : 4;
   constexpr int kTileM = PAIR ? 2 * dc::kGemmBM : dc::kGemmBM;
   constexpr int kBoxB = PAIR ? BN / 2 : BN;          // B rows one CTA loads per k-block
-  using S = dc::GemmSmem<kBoxB, STAGES>;
+  using S = dc::GemmSmem<kBoxB, STAGES, KATOMS>;
   CUtensorMap ta, tb;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
     const uint64_t strides[1] = {static_cast<uint64_t>(ldq)};
-    const uint32_t box[2] = {dc::kGemmBK, dc::kGemmBM};
+    const uint32_t box[2] = {dc::kGemmAtom, dc::kGemmBM};
     int r = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (r) return r;
   }
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
     const uint64_t strides[1] = {static_cast<uint64_t>(ldw)};
-    const uint32_t box[2] = {dc::kGemmBK, static_cast<uint32_t>(kBoxB)};
+    const uint32_t box[2] = {dc::kGemmAtom, static_cast<uint32_t>(kBoxB)};
     int r = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (r) return r;
   }
@@ -412,7 +455,7 @@ int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, cons
   p.tiles_m = static_cast<int>((M + kTileM - 1) / kTileM);
   p.tiles_n = static_cast<int>((N + BN - 1) / BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
-  p.num_kb = static_cast<int>((K + dc::kGemmBK - 1) / dc::kGemmBK);
+  p.num_kb = static_cast<int>((K + S::kBK - 1) / S::kBK);
   p.sx = sx; p.sw = sw; p.bias = bias; p.out = out; p.ldo = ldo;
   p.gate = epi.gate; p.residual = epi.residual; p.ldr = epi.ldr;
   p.col_block = epi.col_block; p.block_stride = epi.block_stride;
@@ -423,7 +466,7 @@ int launch_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, cons
               epi.block_stride % row_elems == 0;
   p.res_vec = epi.residual != nullptr && reinterpret_cast<uintptr_t>(epi.residual) % 16 == 0 &&
               epi.ldr % 8 == 0;
-  auto kernel = dc::gemm_w8a8_kernel<BN, STAGES, OUT, HAS_BIAS, GELU, GATED, PAIR>;
+  auto kernel = dc::gemm_w8a8_kernel<BN, STAGES, OUT, HAS_BIAS, GELU, GATED, PAIR, KATOMS>;
   int r = set_smem(kernel, S::kDynamic);
   if (r) return r;
   if constexpr (PAIR) {

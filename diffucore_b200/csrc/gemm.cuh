@@ -37,7 +37,7 @@ namespace dc {
 enum GemmOut : int { kOutBF16 = 0, kOutF16 = 1, kOutI32 = 2 };
 
 constexpr int kGemmBM = 128;
-constexpr int kGemmBK = 128;            // bytes = int8 elements per k-block (one 128B swizzle row)
+constexpr int kGemmAtom = 128;          // bytes = int8 elements of K per 128B swizzle row (one TMA box)
 constexpr int kGemmEpiWarps = 8;        // two warps per TMEM lane quarter, each half of the columns
 constexpr int kGemmThreads = 64 + 32 * kGemmEpiWarps;
 
@@ -58,10 +58,14 @@ struct GemmParams {
   int res_vec;           // 16-byte residual loads allowed: residual 16-byte aligned, ldr rows of 16 B
 };
 
-template <int BN, int STAGES>
+// A k-block is KATOMS swizzle atoms of 128 bytes of K: A then B, each atom [rows][128 B].
+template <int BN, int STAGES, int KATOMS>
 struct GemmSmem {
-  static constexpr int kA = kGemmBM * kGemmBK;      // 16 KB
-  static constexpr int kB = BN * kGemmBK;           // 16 / 32 KB
+  static constexpr int kBK = KATOMS * kGemmAtom;    // int8 elements of K per k-block
+  static constexpr int kAtomA = kGemmBM * kGemmAtom;
+  static constexpr int kAtomB = BN * kGemmAtom;
+  static constexpr int kA = KATOMS * kAtomA;
+  static constexpr int kB = KATOMS * kAtomB;
   static constexpr int kStage = kA + kB;
   static constexpr int kBytes = STAGES * kStage;
   static constexpr int kDynamic = kBytes + 1024;    // slack for 1024-byte alignment
@@ -110,11 +114,14 @@ __device__ __forceinline__ float gated_residual(uint32_t res_bits, float gate, f
   return out_round<OUT>(__fadd_rn(rv, out_round<OUT>(__fmul_rn(gate, y))));
 }
 
-template <int BN, int STAGES, int OUT, bool HAS_BIAS, int GELU, bool GATED = false, bool PAIR = false>
+// KATOMS: 128-byte atoms of K per pipeline stage. Two (256-byte k-blocks) halve the barrier round
+// trips between the TMA producer and the MMA thread per byte of K.
+template <int BN, int STAGES, int OUT, bool HAS_BIAS, int GELU, bool GATED = false, bool PAIR = false,
+          int KATOMS = 1>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                  const GemmParams p) {
-  using S = GemmSmem<PAIR ? BN / 2 : BN, STAGES>;  // B rows staged by this CTA
+  using S = GemmSmem<PAIR ? BN / 2 : BN, STAGES, KATOMS>;  // B rows staged by this CTA
   constexpr int kHalf = BN / 2;                 // columns per epilogue warp
   constexpr int kTileM = PAIR ? 2 * kGemmBM : kGemmBM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -174,12 +181,20 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
             // both CTAs' halves count on the even CTA's barrier, which expects both
             const uint32_t bar = cluster_addr(&full_bar[stage], 0);
             if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * S::kStage);
-            tma_load_2d_pair(sa, &tma_a, bar, kb * kGemmBK, tm * kTileM + static_cast<int>(rank) * kGemmBM);
-            tma_load_2d_pair(sb, &tma_b, bar, kb * kGemmBK, tn * BN + static_cast<int>(rank) * (BN / 2));
+#pragma unroll
+            for (int at = 0; at < KATOMS; ++at) {
+              const int kx = kb * S::kBK + at * kGemmAtom;
+              tma_load_2d_pair(sa + at * S::kAtomA, &tma_a, bar, kx, tm * kTileM + static_cast<int>(rank) * kGemmBM);
+              tma_load_2d_pair(sb + at * S::kAtomB, &tma_b, bar, kx, tn * BN + static_cast<int>(rank) * (BN / 2));
+            }
           } else {
             mbar_arrive_expect_tx(&full_bar[stage], S::kStage);
-            tma_load_2d(sa, &tma_a, &full_bar[stage], kb * kGemmBK, tm * kGemmBM);
-            tma_load_2d(sb, &tma_b, &full_bar[stage], kb * kGemmBK, tn * BN);
+#pragma unroll
+            for (int at = 0; at < KATOMS; ++at) {
+              const int kx = kb * S::kBK + at * kGemmAtom;
+              tma_load_2d(sa + at * S::kAtomA, &tma_a, &full_bar[stage], kx, tm * kGemmBM);
+              tma_load_2d(sb + at * S::kAtomB, &tma_b, &full_bar[stage], kx, tn * BN);
+            }
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -212,9 +227,10 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
           const uint32_t sa = smem_u32(smem + stage * S::kStage);
           const uint32_t sb = sa + S::kA;
 #pragma unroll
-          for (int k = 0; k < kGemmBK / 32; ++k) {
-            const uint64_t ad = smem_desc(sa + k * 32, 16, 1024);
-            const uint64_t bd = smem_desc(sb + k * 32, 16, 1024);
+          for (int k = 0; k < S::kBK / 32; ++k) {
+            const int at = k / 4, off = (k % 4) * 32;      // atom, then 32-byte step inside its rows
+            const uint64_t ad = smem_desc(sa + at * S::kAtomA + off, 16, 1024);
+            const uint64_t bd = smem_desc(sb + at * S::kAtomB + off, 16, 1024);
             if constexpr (PAIR) mma_i8_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
             else mma_i8_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }

@@ -93,8 +93,8 @@ __device__ __forceinline__ float gelu_dtype(float h, int mode) {
 // The four-term sums of the 256-wide ConvRot butterfly, in the order the reference's Triton
 // `_hadamard_rows` (src/diffucore/models/_int8.py:364-372) computes them for rows of 1024 and more
 // elements (measured on a B200 from that function's own output, bit for bit): the stages over the
-// base-4 digits d3 (stride 64) and d1 (stride 4) add pairs (x0 + x1) + (x2 + x3), the stage over d2
-// (stride 16) adds (x0 + x2) + (x1 + x3), the stage over d0 (stride 1) adds in sequence
+// base-4 digits d3 (stride 64) and d2 (stride 16) add (x0 + x2) + (x1 + x3), the stage over d1
+// (stride 4) adds pairs (x0 + x1) + (x2 + x3), the stage over d0 (stride 1) adds in sequence
 // ((x0 + x1) + x2) + x3.
 __device__ __forceinline__ float quad_sum(float a0, float a1, float a2, float a3) {
   return __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
@@ -122,9 +122,9 @@ __device__ __forceinline__ float hstage_lanes(float x, int m_lo, int m_hi, int f
 // e = lane * 8 + j. Digits: d0 = j & 3, d1 = ((lane & 1) << 1) | (j >> 2), d2 = (lane >> 1) & 3,
 // d3 = lane >> 3. Stage order d3, d2, d1, d0 (most significant first).
 __device__ __forceinline__ void hadamard256_warp(float (&x)[8]) {
-  // d3: lane bits 3 and 4.
+  // d3: lane bits 3 and 4, pairs (d, d + 2) first.
 #pragma unroll
-  for (int j = 0; j < 8; ++j) x[j] = hstage_lanes(x[j], 8, 16, 8);
+  for (int j = 0; j < 8; ++j) x[j] = hstage_lanes(x[j], 8, 16, 16);
   // d2: lane bits 1 and 2, pairs (d, d + 2) first.
 #pragma unroll
   for (int j = 0; j < 8; ++j) x[j] = hstage_lanes(x[j], 2, 4, 4);

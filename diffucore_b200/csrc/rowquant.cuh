@@ -18,6 +18,9 @@
 //   rowq_warp_kernel  one warp per row, K <= 4096 (K % 256 == 0); optionally LayerNorm + AdaLN
 //                     modulation first (one shift/scale vector for all rows)
 //   rowq_cta_kernel   one CTA (16 half-warps) per row, 4096 < K <= 16384 (K % 256 == 0)
+//   rowq_pair_kernel, rowq_cta_pair_kernel   the same, two groups per half-warp in packed fp32
+//   rowq_reg_kernel   one CTA per row with the row in registers (no staging), eight lanes per
+//                     group holding column pairs; K % 256 == 0, K <= 16384 (the default)
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -36,11 +39,14 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
 // Radix-4 stage over the outer index of x[4 a + b] (digit a), and over the inner index (digit b).
+// PAIRS02: the outer sum as (x0 + x2) + (x1 + x3) (the d3 stage), else (x0 + x1) + (x2 + x3) (d1).
+template <bool PAIRS02>
 __device__ __forceinline__ void r4_outer(float (&x)[16]) {
   float y[16];
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
-    const float s = quad_sum(x[b], x[4 + b], x[8 + b], x[12 + b]);
+    const float s = PAIRS02 ? quad_sum_02_13(x[b], x[4 + b], x[8 + b], x[12 + b])
+                            : quad_sum(x[b], x[4 + b], x[8 + b], x[12 + b]);
 #pragma unroll
     for (int a = 0; a < 4; ++a) y[4 * a + b] = __fsub_rn(s, __fmul_rn(2.0f, x[4 * (3 - a) + b]));
   }
@@ -67,7 +73,7 @@ constexpr int kRotScratch = 272;   // floats per half-warp: 256 + 16 so the two 
 // Rotate one group held in layout X by the 16 lanes of a half-warp (L = lane & 15); returns it in
 // layout Y (times 1/16). Both halves of the warp must call it together (it syncs the warp).
 __device__ __forceinline__ void rotate256_half(float (&x)[16], float* scr, int L) {
-  r4_outer(x);                      // d3
+  r4_outer<true>(x);                // d3
   r4_inner<false>(x);               // d2
 #pragma unroll
   for (int i = 0; i < 16; ++i) scr[16 * i + (L ^ i)] = x[i];       // e >> 4 == i, e & 15 == L
@@ -75,7 +81,7 @@ __device__ __forceinline__ void rotate256_half(float (&x)[16], float* scr, int L
 #pragma unroll
   for (int c = 0; c < 16; ++c) x[c] = scr[16 * L + (c ^ L)];
   __syncwarp();
-  r4_outer(x);                      // d1
+  r4_outer<false>(x);               // d1
   r4_inner<true>(x);                // d0
 #pragma unroll
   for (int c = 0; c < 16; ++c) x[c] = __fmul_rn(x[c], 0.0625f);
@@ -319,11 +325,13 @@ __device__ __forceinline__ float2 round_trip2(float2 v) {
 }
 
 // r4_outer / r4_inner on pairs (same summation order per lane).
+template <bool PAIRS02>
 __device__ __forceinline__ void r4_outer2(float2 (&x)[16]) {
   float2 y[16];
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
-    const float2 s = add2(add2(x[b], x[4 + b]), add2(x[8 + b], x[12 + b]));
+    const float2 s = PAIRS02 ? add2(add2(x[b], x[8 + b]), add2(x[4 + b], x[12 + b]))
+                             : add2(add2(x[b], x[4 + b]), add2(x[8 + b], x[12 + b]));
 #pragma unroll
     for (int a = 0; a < 4; ++a) y[4 * a + b] = sub_twice2(s, x[4 * (3 - a) + b]);
   }
@@ -348,7 +356,7 @@ constexpr int kRotScratch2 = 256;   // float2 per half-warp (64-bit accesses: on
 
 // rotate256_half on pairs: layout X in, layout Y (times 1/16) out; both halves call it together.
 __device__ __forceinline__ void rotate256_pair(float2 (&x)[16], float2* scr, int L) {
-  r4_outer2(x);                     // d3
+  r4_outer2<true>(x);               // d3
   r4_inner2<false>(x);              // d2
 #pragma unroll
   for (int i = 0; i < 16; ++i) scr[16 * i + (L ^ i)] = x[i];
@@ -356,7 +364,7 @@ __device__ __forceinline__ void rotate256_pair(float2 (&x)[16], float2* scr, int
 #pragma unroll
   for (int c = 0; c < 16; ++c) x[c] = scr[16 * L + (c ^ L)];
   __syncwarp();
-  r4_outer2(x);                     // d1
+  r4_outer2<false>(x);              // d1
   r4_inner2<true>(x);               // d0
 #pragma unroll
   for (int c = 0; c < 16; ++c) x[c] = mul2(x[c], make_float2(0.0625f, 0.0625f));
@@ -542,6 +550,232 @@ rowq_cta_pair_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q,
     cp_async_commit();
   }
   cp_async_wait<0>();
+}
+
+// ----------------------------------------------------------------------------- register rows
+// rowq_reg_kernel: one CTA per row at a time (persistent over rows, several CTAs per SM), the row
+// held in registers instead of staged in shared memory. A 256-column group is spread over 8 lanes:
+// lane l8 holds columns 16 i + 2 l8 and 16 i + 2 l8 + 1 of it (i = 4 a + b = 0..15) as one float2,
+// so each load is one 32-bit pair and each ConvRot step one packed fp32 operation on the two
+// columns: per column the operations, and their order, of rotate256_half. The transpose between
+// the d2 and d1 stages goes through a swizzled block of shared memory per group (word
+// 16 i + (c ^ i)); after it lane l8 holds the 16 values of block rows 2 l8 (.x) and 2 l8 + 1
+// (.y), i.e. 32 consecutive columns, which leave as two 16-byte code chunks. A warp holds four
+// groups; the CTA has ceil(K / 1024) warps. The next row's pairs are in flight while a row is
+// processed.
+// LNMOD: LayerNorm (mean, then variance of the deviations, over the row in registers; each lane's
+// 32 values summed in column-pair order, then across the warp by an xor tree, then over the warps
+// in order) and the AdaLN modulation, each step rounded to the row dtype as torch's 16-bit ops
+// round. ROT = false: no rotation stages (the transpose still gathers consecutive columns).
+
+constexpr int kRegBlk = 272;   // floats per group block: 256 + 16, so groups 2k and 2k + 1 use other banks
+
+template <typename T>
+__device__ __forceinline__ float2 unpack_pair(uint32_t w) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  else return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+// Codes of eight columns of two block rows (.x, .y): quant8's arithmetic, packed.
+__device__ __forceinline__ void quant8x2(const float2 (&v)[8], float scale, float inv, int full, uint2& ox, uint2& oy) {
+  if (full) {
+    float a[8], b[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { a[j] = v[j].x; b[j] = v[j].y; }
+    ox = quant8(a, scale, inv, 1);
+    oy = quant8(b, scale, inv, 1);
+    return;
+  }
+  uint32_t bx[8], by[8], dx = 0, dy = 0;
+  const float2 inv2 = make_float2(inv, inv), mg = make_float2(kRoundMagic, kRoundMagic);
+  const float2 nmg = make_float2(-kRoundMagic, -kRoundMagic), m1 = make_float2(-1.0f, -1.0f);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 y = __fmul2_rn(v[j], inv2);
+    const float2 t = __fadd2_rn(y, mg);
+    const float2 d = __ffma2_rn(__fadd2_rn(t, nmg), m1, y);      // y - (t - magic), one rounding
+    dx = max(dx, __float_as_uint(d.x) & 0x7FFFFFFFu);
+    dy = max(dy, __float_as_uint(d.y) & 0x7FFFFFFFu);
+    bx[j] = __float_as_uint(t.x);
+    by[j] = __float_as_uint(t.y);
+  }
+  if (dx > __float_as_uint(0.5f - 1e-4f)) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bx[j] = static_cast<uint32_t>(static_cast<uint8_t>(quant_code(v[j].x, scale)));
+  }
+  if (dy > __float_as_uint(0.5f - 1e-4f)) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) by[j] = static_cast<uint32_t>(static_cast<uint8_t>(quant_code(v[j].y, scale)));
+  }
+  ox = make_uint2(__byte_perm(__byte_perm(bx[0], bx[1], 0x0040), __byte_perm(bx[2], bx[3], 0x0040), 0x5410),
+                  __byte_perm(__byte_perm(bx[4], bx[5], 0x0040), __byte_perm(bx[6], bx[7], 0x0040), 0x5410));
+  oy = make_uint2(__byte_perm(__byte_perm(by[0], by[1], 0x0040), __byte_perm(by[2], by[3], 0x0040), 0x5410),
+                  __byte_perm(__byte_perm(by[4], by[5], 0x0040), __byte_perm(by[6], by[7], 0x0040), 0x5410));
+}
+
+template <typename T, bool LNMOD, bool ROT, bool SEG>
+__global__ void __launch_bounds__(512)
+rowq_reg_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift, const T* __restrict__ mscale,
+                int8_t* __restrict__ q, float* __restrict__ s) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  __shared__ float red[4][32];               // sum, deviations, amax (two rows)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int slot = threadIdx.x, nslots = blockDim.x;
+  const int g = slot >> 3, l8 = slot & 7;
+  const bool live = g < (K >> 8);
+  const int c0 = 256 * g + 2 * l8;            // this lane's first column; the others are c0 + 16 i
+  float* blk = reinterpret_cast<float*>(sm) + (warp * 4 + (lane >> 3)) * kRegBlk;
+  float2* modv = reinterpret_cast<float2*>(sm + static_cast<size_t>(nw) * 4 * kRegBlk * sizeof(float));
+  float2* shv = modv + 16 * nslots;
+
+  // Source of pair i of a row: base0 + row * ld0 + 16 i for i < i1, base1 + row * ld1 + 16 (i - i1)
+  // after (an all-to-all receive buffer's segment boundary crosses a group at most once).
+  const T* base0 = static_cast<const T*>(src.x) + c0;
+  const T* base1 = base0;
+  int64_t ld0 = src.ldx, ld1 = src.ldx;
+  int i1 = 16;
+  if (SEG && live) {
+    if (c0 >= src.k1) {
+      base0 = static_cast<const T*>(src.x2) + (c0 - src.k1);
+      ld0 = ld1 = src.ldx2;
+      base1 = base0;
+    } else {
+      const int seg = c0 / src.seg_len;
+      base0 = static_cast<const T*>(src.x) + seg * src.seg_stride + (c0 - seg * src.seg_len);
+      const int cb = (seg + 1) * src.seg_len;        // first column of the next segment
+      i1 = min(16, (cb - c0 + 15) / 16);
+      if (i1 < 16) {
+        const int cn = c0 + 16 * i1;                  // column of pair i1 (>= cb)
+        if (cn >= src.k1) {
+          base1 = static_cast<const T*>(src.x2) + (cn - src.k1);
+          ld1 = src.ldx2;
+        } else {
+          base1 = static_cast<const T*>(src.x) + (seg + 1) * src.seg_stride + (cn - cb);
+        }
+      }
+    }
+  }
+
+  if (LNMOD) {
+    // this lane's (1 + scale) rounded to the row dtype, and shift, staged once
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+      if (live) {
+        const float2 sc = unpack_pair<T>(*reinterpret_cast<const uint32_t*>(mscale + c0 + 16 * i));
+        a = make_float2(Vec8<T>::round_trip(__fadd_rn(1.0f, sc.x)), Vec8<T>::round_trip(__fadd_rn(1.0f, sc.y)));
+        b = unpack_pair<T>(*reinterpret_cast<const uint32_t*>(shift + c0 + 16 * i));
+      }
+      modv[i * nslots + slot] = a;
+      shv[i * nslots + slot] = b;
+    }
+  }
+
+  uint32_t raw[16];
+  auto load_row = [&](int64_t row) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const T* p = i < i1 ? base0 + row * ld0 + 16 * i : base1 + row * ld1 + 16 * (i - i1);
+      raw[i] = live ? __ldg(reinterpret_cast<const unsigned int*>(p)) : 0u;
+    }
+  };
+  const int64_t stride = gridDim.x;
+  int64_t row = blockIdx.x;
+  if (row < M) load_row(row);
+  const float inv_k = 1.0f / static_cast<float>(K);
+  int par = 0;
+  for (; row < M; row += stride, par ^= 1) {
+    float2 x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = unpack_pair<T>(raw[i]);
+    if (row + stride < M) load_row(row + stride);
+
+    if (LNMOD) {
+      float2 a2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) a2 = __fadd2_rn(a2, x[i]);
+      float sum = warp_sum_f(__fadd_rn(a2.x, a2.y));
+      if (lane == 0) red[0][warp] = sum;
+      __syncthreads();
+      sum = red[0][0];
+      for (int w = 1; w < nw; ++w) sum = __fadd_rn(sum, red[0][w]);
+      const float mean = __fmul_rn(sum, inv_k);
+      const float2 nm = make_float2(-mean, -mean);
+      float2 v2 = make_float2(0.f, 0.f);
+      if (live) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 d = __fadd2_rn(x[i], nm);
+          v2 = __ffma2_rn(d, d, v2);
+        }
+      }
+      float var = warp_sum_f(__fadd_rn(v2.x, v2.y));
+      if (lane == 0) red[1][warp] = var;
+      __syncthreads();
+      var = red[1][0];
+      for (int w = 1; w < nw; ++w) var = __fadd_rn(var, red[1][w]);
+      const float rstd = rsqrtf(__fadd_rn(__fmul_rn(var, inv_k), 1e-6f));
+      const float2 rs = make_float2(rstd, rstd);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 n = round_trip2<T>(__fmul2_rn(__fadd2_rn(x[i], nm), rs));
+        const float2 y = round_trip2<T>(__fmul2_rn(modv[i * nslots + slot], n));
+        const float2 z = round_trip2<T>(__fadd2_rn(y, shv[i * nslots + slot]));
+        x[i] = live ? z : make_float2(0.f, 0.f);
+      }
+    }
+
+    if (ROT) {
+      r4_outer2<true>(x);               // d3
+      r4_inner2<false>(x);              // d2
+    }
+    // transpose: block word 16 i + (col ^ i); the pair (2 l8, 2 l8 + 1) of row i lands on one
+    // aligned word pair, in swapped order when i is odd
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float2 v = (i & 1) ? make_float2(x[i].y, x[i].x) : x[i];
+      *reinterpret_cast<float2*>(blk + 16 * i + 2 * (l8 ^ (i >> 1))) = v;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 16; c += 2) {
+      const int k = (c >> 1) ^ l8;
+      const float2 r0 = *reinterpret_cast<const float2*>(blk + 32 * l8 + 2 * k);        // row 2 l8: (c, c + 1)
+      const float2 r1 = *reinterpret_cast<const float2*>(blk + 32 * l8 + 16 + 2 * k);   // row 2 l8 + 1: (c + 1, c)
+      x[c] = make_float2(r0.x, r1.y);
+      x[c + 1] = make_float2(r0.y, r1.x);
+    }
+    __syncwarp();
+    if (ROT) {
+      r4_outer2<false>(x);              // d1
+      r4_inner2<true>(x);               // d0
+#pragma unroll
+      for (int c = 0; c < 16; ++c) x[c] = __fmul2_rn(x[c], make_float2(0.0625f, 0.0625f));
+    }
+
+    float am4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int c = 0; c < 16; ++c) am4[c & 3] = fmaxf(am4[c & 3], fmaxf(fabsf(x[c].x), fabsf(x[c].y)));
+    float am = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    if (lane == 0) red[2 + par][warp] = am;
+    __syncthreads();
+    am = red[2 + par][0];
+    for (int w = 1; w < nw; ++w) am = fmaxf(am, red[2 + par][w]);
+    const float scale = row_scale(am, src.full_div);
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (live) {
+      int8_t* qr = q + row * static_cast<int64_t>(K) + 256 * g + 32 * l8;
+      uint2 ax, ay, bx, by;
+      quant8x2(*reinterpret_cast<const float2(*)[8]>(&x[0]), scale, inv, src.full_div, ax, ay);
+      quant8x2(*reinterpret_cast<const float2(*)[8]>(&x[8]), scale, inv, src.full_div, bx, by);
+      *reinterpret_cast<uint4*>(qr) = make_uint4(ax.x, ax.y, bx.x, bx.y);
+      *reinterpret_cast<uint4*>(qr + 16) = make_uint4(ay.x, ay.y, by.x, by.y);
+    }
+    if (threadIdx.x == 0) s[row] = scale;
+  }
 }
 
 }  // namespace dc

@@ -8,7 +8,11 @@ TEST INFRASTRUCTURE ONLY (nothing in ``diffucore_b200`` loads any of it).
   exposes the prep kernels' outputs.
 * :func:`stage_python` copies the reference's ``src/diffucore/models/_int8.py`` unchanged (its
   Triton ``_rot_quant_kernel`` / ``_rescale_kernel`` and torch-op GPU path, ``_int8.py:299-323``,
-  ``:399-417``) so that it can be imported on the GPU box, where the reference checkout is absent.
+  ``:399-417``) so that it can be imported on the GPU box, where the reference checkout is absent;
+  and, unchanged, the model modules the drop-in test runs (``flux_dit.py``, ``anima_dit.py`` and the
+  modules they import) as a package ``diffucore.models`` under ``oracle/_ref/refpkg`` (its two
+  ``__init__.py`` are written empty there, since the reference's own import its whole pipeline
+  stack, which the test does not use).
 
 Output goes to ``oracle/_ref/`` only (git-ignored; it travels to the GPU box with the snapshot).
 
@@ -30,6 +34,8 @@ HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
 NAME = "dc_ref_attn_sm100"
 INT8_STAGED = OUT / "ref_int8.py"
+REF_PKG = OUT / "refpkg"
+REF_MODELS = ("_int8.py", "_attention.py", "_fused.py", "_norm.py", "flux_dit.py", "anima_dit.py", "llm_adapter.py")
 
 
 def default_root() -> Path | None:
@@ -56,12 +62,20 @@ def build(reference_root: str | Path) -> Path:
 
 
 def stage_python(reference_root: str | Path) -> Path:
-    """Copy the reference's ``_int8.py`` (unchanged) to ``oracle/_ref/ref_int8.py``."""
-    src = Path(reference_root) / "src" / "diffucore" / "models" / "_int8.py"
+    """Copy the reference's ``_int8.py`` (unchanged) to ``oracle/_ref/ref_int8.py``, and the model
+    modules of ``REF_MODELS`` (unchanged) to ``oracle/_ref/refpkg/diffucore/models/``."""
+    models = Path(reference_root) / "src" / "diffucore" / "models"
+    src = models / "_int8.py"
     if not src.exists():
         raise FileNotFoundError(f"no _int8.py at {src}")
     OUT.mkdir(exist_ok=True)
     shutil.copyfile(src, INT8_STAGED)
+    pkg = REF_PKG / "diffucore" / "models"
+    pkg.mkdir(parents=True, exist_ok=True)
+    (REF_PKG / "diffucore" / "__init__.py").write_text("")
+    (pkg / "__init__.py").write_text("")
+    for name in REF_MODELS:
+        shutil.copyfile(models / name, pkg / name)
     return INT8_STAGED
 
 
@@ -71,6 +85,10 @@ def available() -> bool:
 
 def int8_available() -> bool:
     return INT8_STAGED.exists()
+
+
+def models_available() -> bool:
+    return all((REF_PKG / "diffucore" / "models" / name).exists() for name in REF_MODELS)
 
 
 def load():

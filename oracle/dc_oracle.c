@@ -130,7 +130,7 @@ static float gelu_dtype(float h, int mode, int dtype) {
  * 4^d. Stages d3, d2, d1, d0 (_int8.py:364-372: reshape to [., 4, 4, 4, 4], then per axis
  * sum - 2 * flip, then x 0.0625). The four-term sums follow the order the reference's Triton
  * `_hadamard_rows` uses for rows of 1024 and more elements, identified from that function's own
- * output on a B200: d3 and d1 add (x0 + x1) + (x2 + x3), d2 adds (x0 + x2) + (x1 + x3), d0 adds
+ * output on a B200: d3 and d2 add (x0 + x2) + (x1 + x3), d1 adds (x0 + x1) + (x2 + x3), d0 adds
  * ((x0 + x1) + x2) + x3. */
 void or_hadamard256(float* x) {
   float y[256];
@@ -141,7 +141,7 @@ void or_hadamard256(float* x) {
       const int base = e - d * stride;
       const float x0 = x[base], x1 = x[base + stride], x2 = x[base + 2 * stride], x3 = x[base + 3 * stride];
       float s;
-      if (stage == 2) s = (x0 + x2) + (x1 + x3);
+      if (stage >= 2) s = (x0 + x2) + (x1 + x3);
       else if (stage == 0) s = ((x0 + x1) + x2) + x3;
       else s = (x0 + x1) + (x2 + x3);
       y[e] = s - 2.0f * x[base + (3 - d) * stride];

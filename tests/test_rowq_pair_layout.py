@@ -30,10 +30,14 @@ def _sub_twice(s, x):
     return (s + (F(-2.0) * x).astype(F)).astype(F)
 
 
-def _r4_outer(x):                     # x: [16, lanes]
+def _r4_outer(x, pairs02):            # x: [16, lanes]
+    """Sum over the outer digit as (x0 + x2) + (x1 + x3) (the d3 stage) or (x0 + x1) + (x2 + x3) (d1)."""
     y = np.empty_like(x)
     for b in range(4):
-        s = ((x[b] + x[4 + b]).astype(F) + (x[8 + b] + x[12 + b]).astype(F)).astype(F)
+        if pairs02:
+            s = ((x[b] + x[8 + b]).astype(F) + (x[4 + b] + x[12 + b]).astype(F)).astype(F)
+        else:
+            s = ((x[b] + x[4 + b]).astype(F) + (x[8 + b] + x[12 + b]).astype(F)).astype(F)
         for a in range(4):
             y[4 * a + b] = _sub_twice(s, x[4 * (3 - a) + b])
     return y
@@ -54,7 +58,7 @@ def _r4_inner(x, seq):
 
 def _rotate_half_warp(x):
     """rotate256_pair for one slot (.x or .y) of the 16 lanes: x [16 values, 16 lanes]."""
-    x = _r4_inner(_r4_outer(x), False)
+    x = _r4_inner(_r4_outer(x, True), False)
     scr = np.zeros(256, dtype=F)
     for L in range(16):
         for i in range(16):
@@ -63,7 +67,7 @@ def _rotate_half_warp(x):
     for L in range(16):
         for c in range(16):
             y[c, L] = scr[16 * L + (c ^ L)]
-    y = _r4_inner(_r4_outer(y), True)
+    y = _r4_inner(_r4_outer(y, False), True)
     return (y * F(0.0625)).astype(F)
 
 
