@@ -165,14 +165,14 @@ int rowq_reg_mode() {
   return atoi(env);
 }
 
-template <typename T, bool LNMOD, bool ROT, bool SEG>
-int launch_rowq_reg(const dc::RowSrc& src, int64_t M, int64_t K, const void* shift, const void* scale, int8_t* q,
-                    float* s, cudaStream_t st) {
+template <typename T, bool LNMOD, bool ROT, bool SEG, int ORD>
+int launch_rowq_reg_ord(const dc::RowSrc& src, int64_t M, int64_t K, const void* shift, const void* scale, int8_t* q,
+                        float* s, cudaStream_t st) {
   const int nw = static_cast<int>((K / 256 + 3) / 4);
   const int threads = 32 * nw;
   const size_t smem = static_cast<size_t>(nw) * 4 * dc::kRegBlk * sizeof(float) +
                       (LNMOD ? static_cast<size_t>(2) * 16 * threads * sizeof(float2) : 0);
-  auto kernel = dc::rowq_reg_kernel<T, LNMOD, ROT, SEG>;
+  auto kernel = dc::rowq_reg_kernel<T, LNMOD, ROT, SEG, ORD>;
   if (int r = set_smem(kernel, static_cast<int>(smem))) return r;
   int per_sm = 0;
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
@@ -183,6 +183,20 @@ int launch_rowq_reg(const dc::RowSrc& src, int64_t M, int64_t K, const void* shi
                                       static_cast<const T*>(scale), q, s);
   DC_CHECK_LAUNCH("quant_rows launch");
   return DC_OK;
+}
+
+// One kernel per summation order class of the rotation (compile-time stage orders).
+template <typename T, bool LNMOD, bool ROT, bool SEG>
+int launch_rowq_reg(const dc::RowSrc& src, int64_t M, int64_t K, const void* shift, const void* scale, int8_t* q,
+                    float* s, cudaStream_t st) {
+  if constexpr (!ROT) return launch_rowq_reg_ord<T, LNMOD, false, SEG, 0>(src, M, K, shift, scale, q, s, st);
+  switch (src.rot_order) {
+    case dc::kRotOrder256: return launch_rowq_reg_ord<T, LNMOD, ROT, SEG, dc::kRotOrder256>(src, M, K, shift, scale, q, s, st);
+    case dc::kRotOrder512: return launch_rowq_reg_ord<T, LNMOD, ROT, SEG, dc::kRotOrder512>(src, M, K, shift, scale, q, s, st);
+    case dc::kRotOrder1024: return launch_rowq_reg_ord<T, LNMOD, ROT, SEG, dc::kRotOrder1024>(src, M, K, shift, scale, q, s, st);
+    case dc::kRotOrderWide: return launch_rowq_reg_ord<T, LNMOD, ROT, SEG, dc::kRotOrderWide>(src, M, K, shift, scale, q, s, st);
+    default: return fail("quant_rows: unknown rotation order %d", src.rot_order);
+  }
 }
 
 template <typename T, bool GROUP, bool LNMOD, bool SEG>
@@ -332,6 +346,7 @@ int launch_quant(const void* x, int64_t M, int64_t K, int64_t ldx, int group, in
                  cudaStream_t st) {
   dc::RowSrc src = dc::plain_rows(x, ldx);
   src.full_div = quant_full_div();
+  src.rot_order = dc::rot_order_for_width(K);
   const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(q) % 8 == 0) && K <= 16384;
   if (group != 0 && !vec) return fail("rotated quantization needs K %% 256 == 0, ldx %% 8 == 0, 16-byte aligned rows");
@@ -942,6 +957,7 @@ int dc_quant_rows_seg(const void* x, int x_dtype, int64_t M, int64_t K, int64_t 
   dc::RowSrc src;
   src.x = x; src.ldx = ldx; src.seg_len = static_cast<int>(seg_len); src.seg_stride = seg_stride;
   src.k1 = static_cast<int>(k1); src.x2 = x2; src.ldx2 = ldx2; src.full_div = quant_full_div();
+  src.rot_order = dc::rot_order_for_width(K);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (x_dtype == DC_DTYPE_BF16)
     return group ? launch_quant_t<__nv_bfloat16, true, 0, true>(src, M, K, q, s, true, st)
@@ -971,6 +987,7 @@ int dc_ln_mod_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld
       (x_dtype == DC_DTYPE_BF16 || x_dtype == DC_DTYPE_F16)) {
     dc::RowSrc src = dc::plain_rows(x, ldx);
     src.full_div = quant_full_div();
+    src.rot_order = dc::rot_order_for_width(K);
     if (x_dtype == DC_DTYPE_BF16)
       return group ? launch_rowq_warp<__nv_bfloat16, true, true, false>(src, M, K, shift, scale, q, s, st)
                    : launch_rowq_warp<__nv_bfloat16, false, true, false>(src, M, K, shift, scale, q, s, st);

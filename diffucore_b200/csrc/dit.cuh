@@ -96,7 +96,7 @@ ln_mod_quant_kernel(const T* __restrict__ x, int64_t M, int K, int64_t ldx, cons
         }
       }
       // the 32 lanes at one i hold one 256-wide group; lanes past the row end hold zeros
-      if (GROUP) hadamard256_warp(v[i]);
+      if (GROUP) hadamard256_warp(v[i], rot_order_for_width(K));
 #pragma unroll
       for (int j = 0; j < 8; ++j) am4[j & 3] = fmaxf(am4[j & 3], fabsf(v[i][j]));
     }

@@ -135,6 +135,8 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
   __shared__ __align__(16) float col_sw[kGemmEpiWarps][kHalf];    // per-warp staging of sw / bias
   __shared__ __align__(16) float col_bias[kGemmEpiWarps][kHalf];
   __shared__ __align__(16) float col_gate[GATED ? kGemmEpiWarps : 1][GATED ? kHalf : 4];
+  // per epilogue warp: one 32-row x 32-column 16-bit block, 16-byte units swizzled (epi_unit)
+  __shared__ __align__(16) uint4 epi_tile[OUT == kOutI32 ? 1 : kGemmEpiWarps][OUT == kOutI32 ? 1 : 128];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
 
@@ -284,20 +286,85 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       const float sxr = (OUT != kOutI32 && row_ok) ? p.sx[row] : 0.0f;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + half * kHalf;
       // output tile origin: with column blocks the tile lies inside one block (col_block % BN == 0)
-      int64_t out_off = static_cast<int64_t>(row) * p.ldo;
+      int64_t blk_off = 0;
       int col_base = 0;                                   // first column of the tile's block
       if (p.col_block > 0) {
         const int64_t blk = static_cast<int64_t>(tn * BN) / p.col_block;
-        out_off += blk * p.block_stride;
+        blk_off = blk * p.block_stride;
         col_base = static_cast<int>(blk * p.col_block);
       }
+      const int64_t out_off = static_cast<int64_t>(row) * p.ldo + blk_off;
+      const int row0w = row - lane;                       // this warp's first row
 #pragma unroll 1
       for (int c = 0; c < kHalf; c += 32) {
         uint32_t r[32];
         tmem_ld32(taddr + c, r);
         tmem_wait_ld();
         const int col0 = ncol0 + c;
-        if (!row_ok || col0 >= p.N) continue;
+        if (col0 >= p.N) continue;                        // warp-uniform
+        if (OUT != kOutI32 && col0 + 32 <= p.N && p.out_vec && (!GATED || p.res_vec)) {
+          // Whole 32-column chunk (warp-uniform): the warp moves its 32 x 32 block through shared
+          // memory so that each 16-byte global access instruction covers 8 rows' full 64-byte
+          // segments (lane l: row 8 it + l / 4, 16 bytes l % 4) instead of one 16-byte piece of
+          // each of 32 rows. Unit (row rr, 16 bytes k) sits at rr * 4 + (k ^ (rr / 2 % 4)): both
+          // the row-wise and the column-wise accesses then spread over all banks.
+          uint4* tile = epi_tile[ew];
+          auto unit = [](int rr, int k) { return rr * 4 + (k ^ ((rr >> 1) & 3)); };
+          uint32_t res[16];
+          if (GATED) {
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+              const int rr = 8 * it + (lane >> 2), k = lane & 3;
+              const int grow = row0w + rr;
+              uint4 v = make_uint4(0, 0, 0, 0);
+              if (grow < p.M)
+                v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.residual) +
+                                                    static_cast<int64_t>(grow) * p.ldr + col0 + 8 * k);
+              tile[unit(rr, k)] = v;
+            }
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint4 u = tile[unit(lane, k)];
+              res[4 * k] = u.x; res[4 * k + 1] = u.y; res[4 * k + 2] = u.z; res[4 * k + 3] = u.w;
+            }
+            __syncwarp();
+          }
+          uint32_t w[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 s4 = *reinterpret_cast<const float4*>(my_sw + c + j);
+            float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (HAS_BIAS) b4 = *reinterpret_cast<const float4*>(my_bias + c + j);
+            float y0 = epi_value<OUT, HAS_BIAS, GELU>(r[j], sxr, s4.x, b4.x);
+            float y1 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 1], sxr, s4.y, b4.y);
+            float y2 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 2], sxr, s4.z, b4.z);
+            float y3 = epi_value<OUT, HAS_BIAS, GELU>(r[j + 3], sxr, s4.w, b4.w);
+            if (GATED) {
+              const float4 g4 = *reinterpret_cast<const float4*>(my_gate + c + j);
+              y0 = gated_residual<OUT>(res[j / 2] & 0xFFFFu, g4.x, y0);
+              y1 = gated_residual<OUT>(res[j / 2] >> 16, g4.y, y1);
+              y2 = gated_residual<OUT>(res[j / 2 + 1] & 0xFFFFu, g4.z, y2);
+              y3 = gated_residual<OUT>(res[j / 2 + 1] >> 16, g4.w, y3);
+            }
+            w[j / 2] = OUT == kOutBF16 ? pack_bf16x2(y0, y1) : pack_f16x2(y0, y1);
+            w[j / 2 + 1] = OUT == kOutBF16 ? pack_bf16x2(y2, y3) : pack_f16x2(y2, y3);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) tile[unit(lane, k)] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int rr = 8 * it + (lane >> 2), k = lane & 3;
+            const int grow = row0w + rr;
+            if (grow < p.M)
+              *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(grow) * p.ldo +
+                                        blk_off + (col0 - col_base) + 8 * k) = tile[unit(rr, k)];
+          }
+          __syncwarp();
+          continue;
+        }
+        if (!row_ok) continue;
         if (OUT == kOutI32) {
           int32_t* dst = reinterpret_cast<int32_t*>(p.out) + out_off + (col0 - col_base);
           if (col0 + 32 <= p.N && p.out_vec) {

@@ -90,20 +90,50 @@ __device__ __forceinline__ float gelu_dtype(float h, int mode) {
   return h;
 }
 
-// The four-term sums of the 256-wide ConvRot butterfly, in the order the reference's Triton
-// `_hadamard_rows` (src/diffucore/models/_int8.py:364-372) computes them for rows of 1024 and more
-// elements (measured on a B200 from that function's own output, bit for bit): the stages over the
-// base-4 digits d3 (stride 64) and d2 (stride 16) add (x0 + x2) + (x1 + x3), the stage over d1
-// (stride 4) adds pairs (x0 + x1) + (x2 + x3), the stage over d0 (stride 1) adds in sequence
-// ((x0 + x1) + x2) + x3.
-__device__ __forceinline__ float quad_sum(float a0, float a1, float a2, float a3) {
+// The four-term sums of the 256-wide ConvRot butterfly. The reference's Triton `_hadamard_rows`
+// (src/diffucore/models/_int8.py:364-372) sums each radix-4 stage (digit d3 of stride 64, d2 of 16,
+// d1 of 4, d0 of 1) in an order its register layout decides, and that layout depends on the
+// kernel's block width BLOCK = the next power of two >= K (with 4 warps up to BLOCK 2048, 8 above:
+// elements a thread holds in a row are summed in sequence, elements in other lanes by butterfly
+// shuffles, high lane bit first). Inferred on a B200 from `_rot_quant_kernel`'s own scales over
+// 34816-262144 rows per width (the only order per width that matches every row):
+//   BLOCK 256:      d3 (x0 + x2) + (x1 + x3), d2 and d1 the same, d0 (x0 + x1) + (x2 + x3)
+//   BLOCK 512:      d3 (x0 + x1) + (x2 + x3), d2 and d1 (x0 + x2) + (x1 + x3), d0 ((x0 + x1) + x2) + x3
+//   BLOCK 1024:     d3 and d2 (x0 + x2) + (x1 + x3), d1 (x0 + x1) + (x2 + x3), d0 in sequence
+//   BLOCK >= 2048:  d3 and d2 (x0 + x2) + (x1 + x3), d1 and d0 in sequence
+// An order is packed two bits per stage (stage s = digit d_s at bits 2 s).
+constexpr int kSumP0123 = 0;       // (x0 + x1) + (x2 + x3)
+constexpr int kSumP0213 = 1;       // (x0 + x2) + (x1 + x3)
+constexpr int kSumS0123 = 2;       // ((x0 + x1) + x2) + x3
+
+__host__ __device__ constexpr int rot_pack(int d3, int d2, int d1, int d0) {
+  return d0 | (d1 << 2) | (d2 << 4) | (d3 << 6);
+}
+__host__ __device__ constexpr int rot_stage(int packed, int stage) { return (packed >> (2 * stage)) & 3; }
+
+constexpr int kRotOrder256 = rot_pack(kSumP0213, kSumP0213, kSumP0213, kSumP0123);
+constexpr int kRotOrder512 = rot_pack(kSumP0123, kSumP0213, kSumP0213, kSumS0123);
+constexpr int kRotOrder1024 = rot_pack(kSumP0213, kSumP0213, kSumP0123, kSumS0123);
+constexpr int kRotOrderWide = rot_pack(kSumP0213, kSumP0213, kSumS0123, kSumS0123);   // BLOCK >= 2048
+
+__host__ __device__ inline int rot_order_for_width(int64_t K) {
+  int64_t block = 256;
+  while (block < K) block <<= 1;
+  if (block <= 256) return kRotOrder256;
+  if (block == 512) return kRotOrder512;
+  if (block == 1024) return kRotOrder1024;
+  return kRotOrderWide;
+}
+
+__device__ __forceinline__ float quad_sum_ord(float a0, float a1, float a2, float a3, int ord) {
+  if (ord == kSumP0213) return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
+  if (ord == kSumS0123) return __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
   return __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
 }
-__device__ __forceinline__ float quad_sum_02_13(float a0, float a1, float a2, float a3) {
-  return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
-}
-__device__ __forceinline__ float quad_sum_seq(float a0, float a1, float a2, float a3) {
-  return __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+__device__ __forceinline__ float2 quad_sum_ord2(float2 a0, float2 a1, float2 a2, float2 a3, int ord) {
+  if (ord == kSumP0213) return __fadd2_rn(__fadd2_rn(a0, a2), __fadd2_rn(a1, a3));
+  if (ord == kSumS0123) return __fadd2_rn(__fadd2_rn(__fadd2_rn(a0, a1), a2), a3);
+  return __fadd2_rn(__fadd2_rn(a0, a1), __fadd2_rn(a2, a3));
 }
 
 // One radix-4 stage across lanes: the digit lives in lane bits (xor masks m_lo, m_hi for its low
@@ -120,25 +150,29 @@ __device__ __forceinline__ float hstage_lanes(float x, int m_lo, int m_hi, int f
 
 // Rotate the 8 values a lane holds; 32 lanes of a warp hold one 256-wide group, element
 // e = lane * 8 + j. Digits: d0 = j & 3, d1 = ((lane & 1) << 1) | (j >> 2), d2 = (lane >> 1) & 3,
-// d3 = lane >> 3. Stage order d3, d2, d1, d0 (most significant first).
-__device__ __forceinline__ void hadamard256_warp(float (&x)[8]) {
-  // d3: lane bits 3 and 4, pairs (d, d + 2) first.
+// d3 = lane >> 3. Stage order d3, d2, d1, d0 (most significant first); `order` from
+// rot_order_for_width (its d3 and d2 sums are always one of the two pair forms).
+__device__ __forceinline__ void hadamard256_warp(float (&x)[8], int order) {
+  const int o3 = rot_stage(order, 3), o2 = rot_stage(order, 2), o1 = rot_stage(order, 1), o0 = rot_stage(order, 0);
+  // d3: lane bits 3 and 4.
 #pragma unroll
-  for (int j = 0; j < 8; ++j) x[j] = hstage_lanes(x[j], 8, 16, 16);
-  // d2: lane bits 1 and 2, pairs (d, d + 2) first.
+  for (int j = 0; j < 8; ++j) x[j] = hstage_lanes(x[j], 8, 16, o3 == kSumP0123 ? 8 : 16);
+  // d2: lane bits 1 and 2.
 #pragma unroll
-  for (int j = 0; j < 8; ++j) x[j] = hstage_lanes(x[j], 2, 4, 4);
-  // d1: low bit is j bit 2 (in-thread), high bit is lane bit 0.
+  for (int j = 0; j < 8; ++j) x[j] = hstage_lanes(x[j], 2, 4, o2 == kSumP0123 ? 2 : 4);
+  // d1: low bit is j bit 2 (in-thread), high bit is lane bit 0; x0, x1 in the even lane of a pair.
   {
+    const bool odd = (threadIdx.x & 1) != 0;
     float y[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float lo = (j < 4) ? __fadd_rn(x[j], x[j + 4]) : __fadd_rn(x[j - 4], x[j]);   // x[d1=2h] + x[d1=2h+1]
-      const float lo_other = __shfl_xor_sync(0xffffffffu, lo, 1);
-      const bool low_half = (threadIdx.x & 1) == 0;   // this lane holds d1 in {0, 1}
-      const float s = low_half ? __fadd_rn(lo, lo_other) : __fadd_rn(lo_other, lo);
-      const float f = __shfl_xor_sync(0xffffffffu, x[j ^ 4], 1);                      // x[3 - d1]
-      y[j] = __fsub_rn(s, __fmul_rn(2.0f, f));
+    for (int j = 0; j < 4; ++j) {
+      const float lo = x[j], hi = x[j + 4];
+      const float plo = __shfl_xor_sync(0xffffffffu, lo, 1), phi = __shfl_xor_sync(0xffffffffu, hi, 1);
+      const float x0 = odd ? plo : lo, x1 = odd ? phi : hi, x2 = odd ? lo : plo, x3 = odd ? hi : phi;
+      const float s = quad_sum_ord(x0, x1, x2, x3, o1);
+      // this lane holds digits 2 odd (j) and 2 odd + 1 (j + 4): x[3 - d] is x3 / x2, or x1 / x0
+      y[j] = __fsub_rn(s, __fmul_rn(2.0f, odd ? x1 : x3));
+      y[j + 4] = __fsub_rn(s, __fmul_rn(2.0f, odd ? x0 : x2));
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[j] = y[j];
@@ -148,7 +182,7 @@ __device__ __forceinline__ void hadamard256_warp(float (&x)[8]) {
     float y[8];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const float s = quad_sum_seq(x[4 * h], x[4 * h + 1], x[4 * h + 2], x[4 * h + 3]);
+      const float s = quad_sum_ord(x[4 * h], x[4 * h + 1], x[4 * h + 2], x[4 * h + 3], o0);
 #pragma unroll
       for (int d = 0; d < 4; ++d) y[4 * h + d] = __fsub_rn(s, __fmul_rn(2.0f, x[4 * h + (3 - d)]));
     }
@@ -171,11 +205,13 @@ struct RowSrc {
   const void* x2;
   int64_t ldx2;
   int full_div;       // 1: the quantizer divides with div.full.f32 (see row_scale)
+  int rot_order;      // ConvRot summation order for the row width (rot_order_for_width)
 };
 
 __host__ __device__ inline RowSrc plain_rows(const void* x, int64_t ldx) {
   RowSrc r;
   r.x = x; r.ldx = ldx; r.seg_len = 0; r.seg_stride = 0; r.k1 = 0; r.x2 = nullptr; r.ldx2 = 0; r.full_div = 0;
+  r.rot_order = 0;
   return r;
 }
 
@@ -403,7 +439,7 @@ quant_rows_warp_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ 
           for (int j = 0; j < 8; ++j) v[fi][j] = gelu_dtype<T>(v[fi][j], GELU);
         }
         // the 32 lanes at one i hold one 256-wide group (vectors 32 i .. 32 i + 31)
-        if (GROUP) hadamard256_warp(v[fi]);
+        if (GROUP) hadamard256_warp(v[fi], src.rot_order);
 #pragma unroll
         for (int j = 0; j < 8; ++j) am[j] = fmaxf(am[j], fabsf(v[fi][j]));
       }
@@ -466,7 +502,7 @@ quant_rows_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, fl
       }
       // A 256-group is 32 consecutive vectors = the 32 lanes of one warp at one i. Groups
       // past the row end hold zeros and are discarded; every lane joins the shuffles.
-      if (GROUP) hadamard256_warp(v[i]);
+      if (GROUP) hadamard256_warp(v[i], src.rot_order);
 #pragma unroll
       for (int j = 0; j < 8; ++j) am4[j & 3] = fmaxf(am4[j & 3], fabsf(v[i][j]));
     }

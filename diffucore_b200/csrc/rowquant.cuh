@@ -11,9 +11,9 @@
 //   the stores of X and the loads of Y hit 32 distinct banks);
 //   layout Y: lane L holds e = 16 L + c (c = 4 d1 + d0): stages d1, d0 in registers, then x 1/16.
 // Each stage computes S, the sum of the four x[d], and y = S - 2 x[3 - d], with the sums in the
-// order of the reference's Triton butterfly (quad_sum, quad_sum_02_13, quad_sum_seq in quant.cuh),
-// which the warp-shuffle butterfly of quant.cuh and the CPU oracle use too, so codes and scales are
-// bit-identical to it. Without rotation the same kernels read layout Y directly.
+// order the reference's Triton butterfly uses at the row's width (rot_order_for_width in
+// quant.cuh), which the warp-shuffle butterfly of quant.cuh and the CPU oracle use too, so codes
+// and scales are bit-identical to it. Without rotation the same kernels read layout Y directly.
 //
 //   rowq_warp_kernel  one warp per row, K <= 4096 (K % 256 == 0); optionally LayerNorm + AdaLN
 //                     modulation first (one shift/scale vector for all rows)
@@ -38,29 +38,24 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
-// Radix-4 stage over the outer index of x[4 a + b] (digit a), and over the inner index (digit b).
-// PAIRS02: the outer sum as (x0 + x2) + (x1 + x3) (the d3 stage), else (x0 + x1) + (x2 + x3) (d1).
-template <bool PAIRS02>
-__device__ __forceinline__ void r4_outer(float (&x)[16]) {
+// Radix-4 stage over the outer index of x[4 a + b] (digit a), and over the inner index (digit b),
+// the four-term sums in order `ord` (kSumP0123, kSumP0213, kSumS0123).
+__device__ __forceinline__ void r4_outer(float (&x)[16], int ord) {
   float y[16];
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
-    const float s = PAIRS02 ? quad_sum_02_13(x[b], x[4 + b], x[8 + b], x[12 + b])
-                            : quad_sum(x[b], x[4 + b], x[8 + b], x[12 + b]);
+    const float s = quad_sum_ord(x[b], x[4 + b], x[8 + b], x[12 + b], ord);
 #pragma unroll
     for (int a = 0; a < 4; ++a) y[4 * a + b] = __fsub_rn(s, __fmul_rn(2.0f, x[4 * (3 - a) + b]));
   }
 #pragma unroll
   for (int i = 0; i < 16; ++i) x[i] = y[i];
 }
-// SEQ: the four terms added in sequence (the d0 stage), else as (x0 + x2) + (x1 + x3) (the d2 stage).
-template <bool SEQ>
-__device__ __forceinline__ void r4_inner(float (&x)[16]) {
+__device__ __forceinline__ void r4_inner(float (&x)[16], int ord) {
   float y[16];
 #pragma unroll
   for (int a = 0; a < 4; ++a) {
-    const float s = SEQ ? quad_sum_seq(x[4 * a], x[4 * a + 1], x[4 * a + 2], x[4 * a + 3])
-                        : quad_sum_02_13(x[4 * a], x[4 * a + 1], x[4 * a + 2], x[4 * a + 3]);
+    const float s = quad_sum_ord(x[4 * a], x[4 * a + 1], x[4 * a + 2], x[4 * a + 3], ord);
 #pragma unroll
     for (int b = 0; b < 4; ++b) y[4 * a + b] = __fsub_rn(s, __fmul_rn(2.0f, x[4 * a + 3 - b]));
   }
@@ -72,17 +67,18 @@ constexpr int kRotScratch = 272;   // floats per half-warp: 256 + 16 so the two 
 
 // Rotate one group held in layout X by the 16 lanes of a half-warp (L = lane & 15); returns it in
 // layout Y (times 1/16). Both halves of the warp must call it together (it syncs the warp).
-__device__ __forceinline__ void rotate256_half(float (&x)[16], float* scr, int L) {
-  r4_outer<true>(x);                // d3
-  r4_inner<false>(x);               // d2
+// `order`: the stages' summation orders (rot_order_for_width).
+__device__ __forceinline__ void rotate256_half(float (&x)[16], float* scr, int L, int order) {
+  r4_outer(x, rot_stage(order, 3)); // d3
+  r4_inner(x, rot_stage(order, 2)); // d2
 #pragma unroll
   for (int i = 0; i < 16; ++i) scr[16 * i + (L ^ i)] = x[i];       // e >> 4 == i, e & 15 == L
   __syncwarp();
 #pragma unroll
   for (int c = 0; c < 16; ++c) x[c] = scr[16 * L + (c ^ L)];
   __syncwarp();
-  r4_outer<false>(x);               // d1
-  r4_inner<true>(x);                // d0
+  r4_outer(x, rot_stage(order, 1)); // d1
+  r4_inner(x, rot_stage(order, 0)); // d0
 #pragma unroll
   for (int c = 0; c < 16; ++c) x[c] = __fmul_rn(x[c], 0.0625f);
 }
@@ -210,7 +206,7 @@ rowq_warp_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift
 #pragma unroll
         for (int i = 0; i < 16; ++i) xv[i] = 0.0f;
       }
-      if (GROUP && 2 * it < ng) rotate256_half(xv, scr, L);     // warp-uniform condition
+      if (GROUP && 2 * it < ng) rotate256_half(xv, scr, L, src.rot_order);     // warp-uniform condition
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         vals[it][c] = xv[c];
@@ -271,7 +267,7 @@ rowq_cta_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, floa
 #pragma unroll
         for (int i = 0; i < 16; ++i) xv[i] = 0.0f;
       }
-      if (GROUP && 16 * it + 2 * warp < ng) rotate256_half(xv, scr, L);   // warp-uniform
+      if (GROUP && 16 * it + 2 * warp < ng) rotate256_half(xv, scr, L, src.rot_order);   // warp-uniform
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         vals[it][c] = xv[c];
@@ -325,26 +321,22 @@ __device__ __forceinline__ float2 round_trip2(float2 v) {
 }
 
 // r4_outer / r4_inner on pairs (same summation order per lane).
-template <bool PAIRS02>
-__device__ __forceinline__ void r4_outer2(float2 (&x)[16]) {
+__device__ __forceinline__ void r4_outer2(float2 (&x)[16], int ord) {
   float2 y[16];
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
-    const float2 s = PAIRS02 ? add2(add2(x[b], x[8 + b]), add2(x[4 + b], x[12 + b]))
-                             : add2(add2(x[b], x[4 + b]), add2(x[8 + b], x[12 + b]));
+    const float2 s = quad_sum_ord2(x[b], x[4 + b], x[8 + b], x[12 + b], ord);
 #pragma unroll
     for (int a = 0; a < 4; ++a) y[4 * a + b] = sub_twice2(s, x[4 * (3 - a) + b]);
   }
 #pragma unroll
   for (int i = 0; i < 16; ++i) x[i] = y[i];
 }
-template <bool SEQ>
-__device__ __forceinline__ void r4_inner2(float2 (&x)[16]) {
+__device__ __forceinline__ void r4_inner2(float2 (&x)[16], int ord) {
   float2 y[16];
 #pragma unroll
   for (int a = 0; a < 4; ++a) {
-    const float2 s = SEQ ? add2(add2(add2(x[4 * a], x[4 * a + 1]), x[4 * a + 2]), x[4 * a + 3])
-                         : add2(add2(x[4 * a], x[4 * a + 2]), add2(x[4 * a + 1], x[4 * a + 3]));
+    const float2 s = quad_sum_ord2(x[4 * a], x[4 * a + 1], x[4 * a + 2], x[4 * a + 3], ord);
 #pragma unroll
     for (int b = 0; b < 4; ++b) y[4 * a + b] = sub_twice2(s, x[4 * a + 3 - b]);
   }
@@ -355,17 +347,17 @@ __device__ __forceinline__ void r4_inner2(float2 (&x)[16]) {
 constexpr int kRotScratch2 = 256;   // float2 per half-warp (64-bit accesses: one half-warp per phase)
 
 // rotate256_half on pairs: layout X in, layout Y (times 1/16) out; both halves call it together.
-__device__ __forceinline__ void rotate256_pair(float2 (&x)[16], float2* scr, int L) {
-  r4_outer2<true>(x);               // d3
-  r4_inner2<false>(x);              // d2
+__device__ __forceinline__ void rotate256_pair(float2 (&x)[16], float2* scr, int L, int order) {
+  r4_outer2(x, rot_stage(order, 3)); // d3
+  r4_inner2(x, rot_stage(order, 2)); // d2
 #pragma unroll
   for (int i = 0; i < 16; ++i) scr[16 * i + (L ^ i)] = x[i];
   __syncwarp();
 #pragma unroll
   for (int c = 0; c < 16; ++c) x[c] = scr[16 * L + (c ^ L)];
   __syncwarp();
-  r4_outer2<false>(x);              // d1
-  r4_inner2<true>(x);               // d0
+  r4_outer2(x, rot_stage(order, 1)); // d1
+  r4_inner2(x, rot_stage(order, 0)); // d0
 #pragma unroll
   for (int c = 0; c < 16; ++c) x[c] = mul2(x[c], make_float2(0.0625f, 0.0625f));
 }
@@ -452,7 +444,7 @@ rowq_pair_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift
           xv[i] = make_float2(la ? z.x : 0.0f, lb ? z.y : 0.0f);
         }
       }
-      if (4 * j < ng) rotate256_pair(xv, scr, L);        // warp-uniform condition
+      if (4 * j < ng) rotate256_pair(xv, scr, L, src.rot_order);        // warp-uniform condition
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         vals[j][c] = xv[c];
@@ -517,7 +509,7 @@ rowq_cta_pair_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q,
       for (int i = 0; i < 16; ++i)
         xv[i] = make_float2(la ? ld_elem(r + 256 * ga + 16 * i + L) : 0.0f,
                             lb ? ld_elem(r + 256 * gb + 16 * i + L) : 0.0f);
-      if (32 * j + 2 * warp < ng) rotate256_pair(xv, scr, L);     // warp-uniform condition
+      if (32 * j + 2 * warp < ng) rotate256_pair(xv, scr, L, src.rot_order);     // warp-uniform condition
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         vals[j][c] = xv[c];
@@ -567,6 +559,8 @@ rowq_cta_pair_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q,
 // 32 values summed in column-pair order, then across the warp by an xor tree, then over the warps
 // in order) and the AdaLN modulation, each step rounded to the row dtype as torch's 16-bit ops
 // round. ROT = false: no rotation stages (the transpose still gathers consecutive columns).
+// ORD: the ConvRot summation order (one of the kRotOrder* of quant.cuh, the one src.rot_order
+// names), a compile-time constant so that each stage compiles to its one order.
 
 constexpr int kRegBlk = 272;   // floats per group block: 256 + 16, so groups 2k and 2k + 1 use other banks
 
@@ -614,7 +608,7 @@ __device__ __forceinline__ void quant8x2(const float2 (&v)[8], float scale, floa
                   __byte_perm(__byte_perm(by[4], by[5], 0x0040), __byte_perm(by[6], by[7], 0x0040), 0x5410));
 }
 
-template <typename T, bool LNMOD, bool ROT, bool SEG>
+template <typename T, bool LNMOD, bool ROT, bool SEG, int ORD>
 __global__ void __launch_bounds__(512)
 rowq_reg_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift, const T* __restrict__ mscale,
                 int8_t* __restrict__ q, float* __restrict__ s) {
@@ -727,8 +721,8 @@ rowq_reg_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift,
     }
 
     if (ROT) {
-      r4_outer2<true>(x);               // d3
-      r4_inner2<false>(x);              // d2
+      r4_outer2(x, rot_stage(ORD, 3));  // d3
+      r4_inner2(x, rot_stage(ORD, 2));  // d2
     }
     // transpose: block word 16 i + (col ^ i); the pair (2 l8, 2 l8 + 1) of row i lands on one
     // aligned word pair, in swapped order when i is odd
@@ -748,8 +742,8 @@ rowq_reg_kernel(const RowSrc src, int64_t M, int K, const T* __restrict__ shift,
     }
     __syncwarp();
     if (ROT) {
-      r4_outer2<false>(x);              // d1
-      r4_inner2<true>(x);               // d0
+      r4_outer2(x, rot_stage(ORD, 1));  // d1
+      r4_inner2(x, rot_stage(ORD, 0));  // d0
 #pragma unroll
       for (int c = 0; c < 16; ++c) x[c] = __fmul2_rn(x[c], make_float2(0.0625f, 0.0625f));
     }

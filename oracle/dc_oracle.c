@@ -126,23 +126,42 @@ static float gelu_dtype(float h, int mode, int dtype) {
   return h;
 }
 
-/* One 256-wide group in place; digit d of index e (base 4, d3 most significant) has stride
- * 4^d. Stages d3, d2, d1, d0 (_int8.py:364-372: reshape to [., 4, 4, 4, 4], then per axis
- * sum - 2 * flip, then x 0.0625). The four-term sums follow the order the reference's Triton
- * `_hadamard_rows` uses for rows of 1024 and more elements, identified from that function's own
- * output on a B200: d3 and d2 add (x0 + x2) + (x1 + x3), d1 adds (x0 + x1) + (x2 + x3), d0 adds
- * ((x0 + x1) + x2) + x3. */
-void or_hadamard256(float* x) {
+/* The four-term sums of each stage follow the order the reference's Triton `_hadamard_rows`
+ * uses, which its register layout decides from the kernel's block width BLOCK = the next power
+ * of two >= the row width (inferred on a B200 from `_rot_quant_kernel`'s own scales):
+ *   BLOCK 256:     d3, d2, d1 (x0 + x2) + (x1 + x3); d0 (x0 + x1) + (x2 + x3)
+ *   BLOCK 512:     d3 (x0 + x1) + (x2 + x3); d2, d1 (x0 + x2) + (x1 + x3); d0 ((x0 + x1) + x2) + x3
+ *   BLOCK 1024:    d3, d2 (x0 + x2) + (x1 + x3); d1 (x0 + x1) + (x2 + x3); d0 in sequence
+ *   BLOCK >= 2048: d3, d2 (x0 + x2) + (x1 + x3); d1, d0 in sequence */
+enum { SUM_P0123 = 0, SUM_P0213 = 1, SUM_S0123 = 2 };
+
+static int stage_order(int64_t width, int stage) {
+  int64_t block = 256;
+  while (block < width) block <<= 1;
+  static const int table[4][4] = {   /* [block class][stage d0..d3] */
+      {SUM_P0123, SUM_P0213, SUM_P0213, SUM_P0213},
+      {SUM_S0123, SUM_P0213, SUM_P0213, SUM_P0123},
+      {SUM_S0123, SUM_P0123, SUM_P0213, SUM_P0213},
+      {SUM_S0123, SUM_S0123, SUM_P0213, SUM_P0213}};
+  const int cls = block <= 256 ? 0 : block == 512 ? 1 : block == 1024 ? 2 : 3;
+  return table[cls][stage];
+}
+
+/* One 256-wide group in place, of a row `width` elements wide; digit d of index e (base 4, d3
+ * most significant) has stride 4^d. Stages d3, d2, d1, d0 (_int8.py:364-372: reshape to
+ * [., 4, 4, 4, 4], then per axis sum - 2 * flip, then x 0.0625). */
+void or_hadamard256(float* x, int64_t width) {
   float y[256];
   for (int stage = 3; stage >= 0; --stage) {
     const int stride = 1 << (2 * stage);
+    const int ord = stage_order(width, stage);
     for (int e = 0; e < 256; ++e) {
       const int d = (e / stride) & 3;
       const int base = e - d * stride;
       const float x0 = x[base], x1 = x[base + stride], x2 = x[base + 2 * stride], x3 = x[base + 3 * stride];
       float s;
-      if (stage >= 2) s = (x0 + x2) + (x1 + x3);
-      else if (stage == 0) s = ((x0 + x1) + x2) + x3;
+      if (ord == SUM_P0213) s = (x0 + x2) + (x1 + x3);
+      else if (ord == SUM_S0123) s = ((x0 + x1) + x2) + x3;
       else s = (x0 + x1) + (x2 + x3);
       y[e] = s - 2.0f * x[base + (3 - d) * stride];
     }
@@ -166,7 +185,7 @@ void or_quant_rows(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx, 
     float* row = (float*)malloc(sizeof(float) * (size_t)K);
     for (int64_t k = 0; k < K; ++k) row[k] = gelu_dtype(load_elem(x, dtype, m * ldx + k), gelu, dtype);
     if (group == 256)
-      for (int64_t g = 0; g + 256 <= K; g += 256) or_hadamard256(row + g);
+      for (int64_t g = 0; g + 256 <= K; g += 256) or_hadamard256(row + g, K);
     float amax = 0.0f;
     for (int64_t k = 0; k < K; ++k) amax = fmaxf(amax, fabsf(row[k]));
     float scale = amax / 127.0f;

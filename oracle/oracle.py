@@ -103,10 +103,11 @@ def quant_rows(x: np.ndarray, dtype: str, group: int = 0, gelu: int = 0):
     return q, s
 
 
-def hadamard256(x: np.ndarray) -> np.ndarray:
-    """The library's butterfly rotation of one 256-wide fp32 group."""
+def hadamard256(x: np.ndarray, width: int = 3072) -> np.ndarray:
+    """The library's butterfly rotation of one 256-wide fp32 group of a row ``width`` elements wide
+    (the width selects the summation order of the reference's Triton butterfly)."""
     y = np.array(x, dtype=np.float32, copy=True)
-    _load().or_hadamard256(_p(y))
+    _load().or_hadamard256(_p(y), ctypes.c_int64(width))
     return y
 
 

@@ -73,11 +73,16 @@ def triton_division():
 @pytest.mark.parametrize("M,K,group,dtype", [
     (4096, 3072, 0, torch.bfloat16), (4608, 3072, 256, torch.bfloat16), (4608, 15360, 256, torch.bfloat16),
     (4096, 12288, 256, torch.bfloat16), (512, 3072, 256, torch.float16), (300, 640, 0, torch.float16),
-    (7, 256, 256, torch.bfloat16), (33, 1000, 0, torch.bfloat16)])
+    (7, 256, 256, torch.bfloat16), (33, 1000, 0, torch.bfloat16),
+    # one width of each block-size class of the Triton kernel (its butterfly order depends on it)
+    (16384, 256, 256, torch.bfloat16), (16384, 512, 256, torch.bfloat16), (16384, 768, 256, torch.bfloat16),
+    (8192, 1024, 256, torch.float16), (8192, 1280, 256, torch.bfloat16), (4096, 2048, 256, torch.bfloat16),
+    (2048, 5120, 256, torch.bfloat16), (1024, 16384, 256, torch.bfloat16)])
 def test_triton_division_equals_reference_triton_quantizer(ref_int8, triton_division, M, K, group, dtype):
     """With the "triton" division the native quantizer gives the reference's Triton
     `_rot_quant_kernel` (src/diffucore/models/_int8.py:399-406) codes and scales bit for bit, with and
-    without the 256-wide ConvRot rotation, at the golden shapes and FLUX's row widths."""
+    without the 256-wide ConvRot rotation, at the golden shapes, FLUX's row widths and one width of
+    every block-size class of the Triton kernel."""
     from diffucore_b200 import _int8
     g = torch.Generator(device="cuda").manual_seed(M + K)
     x = (torch.randn(M, K, generator=g, device="cuda") * 2).to(dtype)

@@ -30,35 +30,54 @@ def _sub_twice(s, x):
     return (s + (F(-2.0) * x).astype(F)).astype(F)
 
 
-def _r4_outer(x, pairs02):            # x: [16, lanes]
-    """Sum over the outer digit as (x0 + x2) + (x1 + x3) (the d3 stage) or (x0 + x1) + (x2 + x3) (d1)."""
+P0123, P0213, S0123 = 0, 1, 2
+
+
+def _orders(K):
+    """Summation order per stage (d3, d2, d1, d0) of the reference's Triton butterfly for a row of
+    K elements (its block width is the next power of two >= K)."""
+    block = 256
+    while block < K:
+        block *= 2
+    if block <= 256:
+        return P0213, P0213, P0213, P0123
+    if block == 512:
+        return P0123, P0213, P0213, S0123
+    if block == 1024:
+        return P0213, P0213, P0123, S0123
+    return P0213, P0213, S0123, S0123
+
+
+def _quad(x0, x1, x2, x3, ord_):
+    if ord_ == P0213:
+        return ((x0 + x2).astype(F) + (x1 + x3).astype(F)).astype(F)
+    if ord_ == S0123:
+        return (((x0 + x1).astype(F) + x2).astype(F) + x3).astype(F)
+    return ((x0 + x1).astype(F) + (x2 + x3).astype(F)).astype(F)
+
+
+def _r4_outer(x, ord_):               # x: [16, lanes]
     y = np.empty_like(x)
     for b in range(4):
-        if pairs02:
-            s = ((x[b] + x[8 + b]).astype(F) + (x[4 + b] + x[12 + b]).astype(F)).astype(F)
-        else:
-            s = ((x[b] + x[4 + b]).astype(F) + (x[8 + b] + x[12 + b]).astype(F)).astype(F)
+        s = _quad(x[b], x[4 + b], x[8 + b], x[12 + b], ord_)
         for a in range(4):
             y[4 * a + b] = _sub_twice(s, x[4 * (3 - a) + b])
     return y
 
 
-def _r4_inner(x, seq):
-    """Sum over the inner digit in sequence (the d0 stage) or as (x0 + x2) + (x1 + x3) (the d2 stage)."""
+def _r4_inner(x, ord_):
     y = np.empty_like(x)
     for a in range(4):
-        if seq:
-            s = (((x[4 * a] + x[4 * a + 1]).astype(F) + x[4 * a + 2]).astype(F) + x[4 * a + 3]).astype(F)
-        else:
-            s = ((x[4 * a] + x[4 * a + 2]).astype(F) + (x[4 * a + 1] + x[4 * a + 3]).astype(F)).astype(F)
+        s = _quad(x[4 * a], x[4 * a + 1], x[4 * a + 2], x[4 * a + 3], ord_)
         for b in range(4):
             y[4 * a + b] = _sub_twice(s, x[4 * a + 3 - b])
     return y
 
 
-def _rotate_half_warp(x):
-    """rotate256_pair for one slot (.x or .y) of the 16 lanes: x [16 values, 16 lanes]."""
-    x = _r4_inner(_r4_outer(x, True), False)
+def _rotate_half_warp(x, K):
+    """rotate256_pair for one slot (.x or .y) of the 16 lanes of a row K wide: x [16 values, 16 lanes]."""
+    o3, o2, o1, o0 = _orders(K)
+    x = _r4_inner(_r4_outer(x, o3), o2)
     scr = np.zeros(256, dtype=F)
     for L in range(16):
         for i in range(16):
@@ -67,7 +86,7 @@ def _rotate_half_warp(x):
     for L in range(16):
         for c in range(16):
             y[c, L] = scr[16 * L + (c ^ L)]
-    y = _r4_inner(_r4_outer(y, False), True)
+    y = _r4_inner(_r4_outer(y, o1), o0)
     return (y * F(0.0625)).astype(F)
 
 
@@ -95,7 +114,7 @@ def _model_row(row, mod_a, mod_sh, mean, rstd, lnmod):
                         x[i, L] = v
                 slots.append((g, live, x))
             if 4 * j < ng:
-                slots = [(g, live, _rotate_half_warp(x)) for g, live, x in slots]
+                slots = [(g, live, _rotate_half_warp(x, K)) for g, live, x in slots]
             for g, live, x in slots:
                 if live:
                     vals[g] = x                            # layout Y: lane L holds 16 L + c
@@ -154,7 +173,7 @@ def _model_row_cta(row):
                         x[i, L] = row[256 * g + 16 * i + L]
                 assert 32 * j + 2 * warp < ng          # the warp-uniform rotate condition holds
                 assert g not in vals
-                vals[g] = _rotate_half_warp(x)
+                vals[g] = _rotate_half_warp(x, K)
     assert sorted(vals) == list(range(ng))
     amax = max(float(np.abs(v).max()) for v in vals.values())
     scale = np.float32(max(F(amax) / F(127.0), F(1e-30)))
