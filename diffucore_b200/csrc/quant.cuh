@@ -125,6 +125,10 @@ __host__ __device__ inline int rot_order_for_width(int64_t K) {
   return kRotOrderWide;
 }
 
+// s - 2 x with one rounding. 2 x is exact, so this equals the reference's `sum - 2 * flip`
+// computed as a product and a difference (no contraction) bit for bit, in one instruction.
+__device__ __forceinline__ float sub_twice(float s, float x) { return __fmaf_rn(-2.0f, x, s); }
+
 __device__ __forceinline__ float quad_sum_ord(float a0, float a1, float a2, float a3, int ord) {
   if (ord == kSumP0213) return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
   if (ord == kSumS0123) return __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
@@ -145,7 +149,7 @@ __device__ __forceinline__ float hstage_lanes(float x, int m_lo, int m_hi, int f
   const float a = __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, first));
   const float s = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, second));
   const float f = __shfl_xor_sync(0xffffffffu, x, m_lo | m_hi);          // x[3 - d]
-  return __fsub_rn(s, __fmul_rn(2.0f, f));
+  return sub_twice(s, f);
 }
 
 // Rotate the 8 values a lane holds; 32 lanes of a warp hold one 256-wide group, element
@@ -171,8 +175,8 @@ __device__ __forceinline__ void hadamard256_warp(float (&x)[8], int order) {
       const float x0 = odd ? plo : lo, x1 = odd ? phi : hi, x2 = odd ? lo : plo, x3 = odd ? hi : phi;
       const float s = quad_sum_ord(x0, x1, x2, x3, o1);
       // this lane holds digits 2 odd (j) and 2 odd + 1 (j + 4): x[3 - d] is x3 / x2, or x1 / x0
-      y[j] = __fsub_rn(s, __fmul_rn(2.0f, odd ? x1 : x3));
-      y[j + 4] = __fsub_rn(s, __fmul_rn(2.0f, odd ? x0 : x2));
+      y[j] = sub_twice(s, odd ? x1 : x3);
+      y[j + 4] = sub_twice(s, odd ? x0 : x2);
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[j] = y[j];
@@ -184,7 +188,7 @@ __device__ __forceinline__ void hadamard256_warp(float (&x)[8], int order) {
     for (int h = 0; h < 2; ++h) {
       const float s = quad_sum_ord(x[4 * h], x[4 * h + 1], x[4 * h + 2], x[4 * h + 3], o0);
 #pragma unroll
-      for (int d = 0; d < 4; ++d) y[4 * h + d] = __fsub_rn(s, __fmul_rn(2.0f, x[4 * h + (3 - d)]));
+      for (int d = 0; d < 4; ++d) y[4 * h + d] = sub_twice(s, x[4 * h + (3 - d)]);
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[j] = __fmul_rn(y[j], 0.0625f);

@@ -46,7 +46,7 @@ __device__ __forceinline__ void r4_outer(float (&x)[16], int ord) {
   for (int b = 0; b < 4; ++b) {
     const float s = quad_sum_ord(x[b], x[4 + b], x[8 + b], x[12 + b], ord);
 #pragma unroll
-    for (int a = 0; a < 4; ++a) y[4 * a + b] = __fsub_rn(s, __fmul_rn(2.0f, x[4 * (3 - a) + b]));
+    for (int a = 0; a < 4; ++a) y[4 * a + b] = sub_twice(s, x[4 * (3 - a) + b]);
   }
 #pragma unroll
   for (int i = 0; i < 16; ++i) x[i] = y[i];
@@ -57,7 +57,7 @@ __device__ __forceinline__ void r4_inner(float (&x)[16], int ord) {
   for (int a = 0; a < 4; ++a) {
     const float s = quad_sum_ord(x[4 * a], x[4 * a + 1], x[4 * a + 2], x[4 * a + 3], ord);
 #pragma unroll
-    for (int b = 0; b < 4; ++b) y[4 * a + b] = __fsub_rn(s, __fmul_rn(2.0f, x[4 * a + 3 - b]));
+    for (int b = 0; b < 4; ++b) y[4 * a + b] = sub_twice(s, x[4 * a + 3 - b]);
   }
 #pragma unroll
   for (int i = 0; i < 16; ++i) x[i] = y[i];
@@ -311,8 +311,8 @@ rowq_cta_kernel(const RowSrc src, int64_t M, int K, int8_t* __restrict__ q, floa
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 
-// s - 2 x per lane: __fsub_rn(s, __fmul_rn(2, x)) == s + round(-2 x) (negation is exact).
-__device__ __forceinline__ float2 sub_twice2(float2 s, float2 x) { return add2(s, mul2(make_float2(-2.f, -2.f), x)); }
+// sub_twice per lane: one packed FMA (-2 x is exact).
+__device__ __forceinline__ float2 sub_twice2(float2 s, float2 x) { return __ffma2_rn(make_float2(-2.f, -2.f), x, s); }
 
 template <typename T>
 __device__ __forceinline__ float2 round_trip2(float2 v) {
