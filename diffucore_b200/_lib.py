@@ -46,6 +46,9 @@ _SIGNATURES = {
                                        ctypes.c_int, _c_p, _c_p, _c_p]),
     "dc_qk_norm_rope": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p,
                                        _c_p, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p]),
+    "dc_qk_norm_rope_q8": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p,
+                                          _c_p, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, ctypes.c_int,
+                                          _c_p]),
     "dc_rescale": (ctypes.c_int, [_c_p, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, ctypes.c_int, _c_i64, _c_i64,
                                   _c_p]),
     "dc_attn_workspace_size": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int,
@@ -56,6 +59,8 @@ _SIGNATURES = {
                                         _c_p, ctypes.c_size_t, _c_p]),
     "dc_attn_int8_prep": (ctypes.c_int, [_c_p, _c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                          _c_i64p, _c_i64p, ctypes.c_int, _c_p, ctypes.c_size_t, _c_p]),
+    "dc_attn_int8_prep_k": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64p,
+                                           ctypes.c_int, _c_p, ctypes.c_size_t, _c_p]),
     "dc_attn_int8_main": (ctypes.c_int, [_c_p, ctypes.c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64p,
                                          ctypes.c_float, ctypes.c_int, _c_p, _c_i64p, _c_p, ctypes.c_size_t, _c_p]),
     "dc_attn_split_partials_size": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int,

@@ -31,9 +31,10 @@ constexpr int kStatWin = 128;       // rows per K-sum window (the reference's FL
 
 // Per-(b, h, window) partial K column sums in the reference's fixed order
 // (int8_attn_sm80.cu:92-135): thread (rg, ch) adds rows r0+rg, r0+rg+16, ... of its 8 channels;
-// the 16 row-group partials are then added in order rg = 0..15.
+// the 16 row-group partials are then added in order rg = 0..15. Six CTAs per SM, so that the
+// windows x heads of a 4608-token, 24-head call run in one wave.
 template <typename T, int D>
-__global__ void __launch_bounds__(16 * (D / 8))
+__global__ void __launch_bounds__(16 * (D / 8), 6)
 k_stats_kernel(const T* __restrict__ k, float* __restrict__ kpart, int L, int H, int64_t sb, int64_t sl,
                int64_t sh) {
   constexpr int NCH = D / 8;
@@ -60,12 +61,20 @@ k_stats_kernel(const T* __restrict__ k, float* __restrict__ kpart, int L, int H,
   }
 }
 
-// ksum[bh, d] = sum over windows in order (int8_attn_sm80.cu:137-142).
+// ksum[bh, d] = sum over windows in order (int8_attn_sm80.cu:137-142); the partials are loaded
+// eight at a time ahead of the in-order adds.
 template <int D>
 __global__ void k_sum_kernel(const float* __restrict__ kpart, float* __restrict__ ksum, int nwin) {
   const float* src = kpart + static_cast<int64_t>(blockIdx.x) * nwin * D + threadIdx.x;
   float s = 0.f;
-  for (int w = 0; w < nwin; ++w) s = __fadd_rn(s, src[w * D]);
+  for (int w0 = 0; w0 < nwin; w0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = w0 + i < nwin ? src[(w0 + i) * D] : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (w0 + i < nwin) s = __fadd_rn(s, v[i]);
+  }
   ksum[blockIdx.x * D + threadIdx.x] = s;
 }
 
@@ -126,8 +135,8 @@ block_quant_kernel(const T* __restrict__ x, const float* __restrict__ ksum, int8
     uint32_t w0 = 0, w1 = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      w0 |= static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(__fmul_rn(vals[u][i], inv))))) << (8 * i);
-      w1 |= static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(__fmul_rn(vals[u][i + 4], inv))))) << (8 * i);
+      w0 |= code_byte(__fmul_rn(vals[u][i], inv)) << (8 * i);
+      w1 |= code_byte(__fmul_rn(vals[u][i + 4], inv)) << (8 * i);
     }
     int8_t* dst = codes + (static_cast<int64_t>(bh) * Lpad + blk * kAttnKBlk + r) * D + c * 8;
     *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
@@ -137,18 +146,19 @@ block_quant_kernel(const T* __restrict__ x, const float* __restrict__ ksum, int8
 // Per-token Q codes (int8_attn_sm80.cu:341-388): amax over the D channels of the row;
 // inv = amax > 0 ? 127 / amax : 0; code = rn(x * inv); row scale = amax / 127 (the softmax scale
 // is applied by the main kernel). NCH = D / 8 lanes per row; rows in [L, Lpad) are zero.
+// Grid (Lpad / (256 / NCH), H, B).
 template <typename T, int D>
 __global__ void __launch_bounds__(256)
 q_token_quant_kernel(const T* __restrict__ q, int8_t* __restrict__ codes, float* __restrict__ row_scales, int L,
-                     int H, int Lpad, int64_t total_rows, int64_t sb, int64_t sl, int64_t sh) {
+                     int H, int Lpad, int64_t sb, int64_t sl, int64_t sh) {
   constexpr int NCH = D / 8;
   constexpr int ROWS_PER_CTA = 256 / NCH;
   const int sub = threadIdx.x / NCH, c = threadIdx.x % NCH;
-  const int64_t grow = static_cast<int64_t>(blockIdx.x) * ROWS_PER_CTA + sub;   // (bh, row) flattened
-  const bool live = grow < total_rows;
-  const int bh = live ? static_cast<int>(grow / Lpad) : 0;
-  const int row = live ? static_cast<int>(grow % Lpad) : 0;
-  const int b = bh / H, h = bh % H;
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int row = blockIdx.x * ROWS_PER_CTA + sub;
+  const int bh = b * H + h;
+  const int64_t grow = static_cast<int64_t>(bh) * Lpad + row;
+  const bool live = row < Lpad;
   float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (live && row < L) Vec8<T>::load(q + b * sb + row * sl + h * sh + c * 8, f);
   float amax = 0.f;
@@ -160,8 +170,8 @@ q_token_quant_kernel(const T* __restrict__ q, int8_t* __restrict__ codes, float*
   uint32_t w0 = 0, w1 = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    w0 |= static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(__fmul_rn(f[i], inv))))) << (8 * i);
-    w1 |= static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(__fmul_rn(f[i + 4], inv))))) << (8 * i);
+    w0 |= code_byte(__fmul_rn(f[i], inv)) << (8 * i);
+    w1 |= code_byte(__fmul_rn(f[i + 4], inv)) << (8 * i);
   }
   if (live) {
     *reinterpret_cast<uint2*>(codes + grow * D + c * 8) = make_uint2(w0, w1);

@@ -650,9 +650,10 @@ int check_strides(const void* ptr, const int64_t* s, const char* name) {
   return DC_OK;
 }
 
+// do_q = false: the Q codes and scales are already in the workspace (dc_qk_norm_rope_q8).
 template <typename T, int D>
 int attn_prep(const void* q, const void* k, int64_t B, int64_t H, int64_t Lq, int64_t Lk, const int64_t* qs,
-              const int64_t* ks, int mode, uint8_t* ws, const AttnLayout& a, cudaStream_t st) {
+              const int64_t* ks, int mode, uint8_t* ws, const AttnLayout& a, cudaStream_t st, bool do_q = true) {
   int8_t* q_codes = reinterpret_cast<int8_t*>(ws + a.q_codes);
   int8_t* k_codes = reinterpret_cast<int8_t*>(ws + a.k_codes);
   float* q_scale = reinterpret_cast<float*>(ws + a.q_scale);
@@ -668,16 +669,16 @@ int attn_prep(const void* q, const void* k, int64_t B, int64_t H, int64_t Lq, in
     dc::k_sum_kernel<D><<<static_cast<unsigned>(B * H), D, 0, st>>>(kpart, ksum, static_cast<int>(a.nwin));
     dc::block_quant_kernel<T, D><<<dim3(static_cast<unsigned>(a.Lk_pad / dc::kAttnKBlk), Hi, static_cast<unsigned>(B)), 256, 0, st>>>(
         kp, ksum, k_codes, k_scale, nullptr, static_cast<int>(Lk), Hi, static_cast<int>(a.Lk_pad), ks[0], ks[1], ks[2]);
-    const int64_t rows = B * H * a.Lq_pad;
     constexpr int rows_per_cta = 256 / (D / 8);
-    dc::q_token_quant_kernel<T, D><<<static_cast<unsigned>((rows + rows_per_cta - 1) / rows_per_cta), 256, 0, st>>>(
-        qp, q_codes, q_scale, static_cast<int>(Lq), Hi, static_cast<int>(a.Lq_pad), rows, qs[0], qs[1], qs[2]);
+    if (do_q) dc::q_token_quant_kernel<T, D><<<dim3(static_cast<unsigned>((a.Lq_pad + rows_per_cta - 1) / rows_per_cta), Hi,
+                                          static_cast<unsigned>(B)), 256, 0, st>>>(
+        qp, q_codes, q_scale, static_cast<int>(Lq), Hi, static_cast<int>(a.Lq_pad), qs[0], qs[1], qs[2]);
   } else {
     dc::block_quant_kernel<T, D><<<dim3(static_cast<unsigned>(a.Lk_pad / dc::kAttnKBlk), Hi, static_cast<unsigned>(B)), 256, 0, st>>>(
         kp, nullptr, k_codes, k_scale, nullptr, static_cast<int>(Lk), Hi, static_cast<int>(a.Lk_pad), ks[0], ks[1], ks[2]);
     // Q per 64-row block: only the per-row copy of the block scale is kept (the main kernel
     // reads one scale per query row in both modes).
-    dc::block_quant_kernel<T, D><<<dim3(static_cast<unsigned>(a.Lq_pad / dc::kAttnKBlk), Hi, static_cast<unsigned>(B)), 256, 0, st>>>(
+    if (do_q) dc::block_quant_kernel<T, D><<<dim3(static_cast<unsigned>(a.Lq_pad / dc::kAttnKBlk), Hi, static_cast<unsigned>(B)), 256, 0, st>>>(
         qp, nullptr, q_codes, nullptr, q_scale, static_cast<int>(Lq), Hi, static_cast<int>(a.Lq_pad), qs[0], qs[1],
         qs[2]);
   }
@@ -1005,10 +1006,19 @@ int dc_ln_mod_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ld
   }
 }
 
-int dc_qk_norm_rope(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64_t ld_row, int64_t q_off,
-                    int64_t k_off, const void* q_scale0, const void* k_scale0, const void* q_scale1,
-                    const void* k_scale1, int64_t split_row, const float* pe, int64_t pe_row0, void* stream) {
+static int qk_norm_rope_impl(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64_t ld_row, int64_t q_off,
+                             int64_t k_off, const void* q_scale0, const void* k_scale0, const void* q_scale1,
+                             const void* k_scale1, int64_t split_row, const float* pe, int64_t pe_row0,
+                             int8_t* q_codes, float* q_rscale, int64_t q_lpad, int write_q, void* stream) {
   if (L < 0 || H <= 0) return fail("qk_norm_rope: bad shape");
+  if (q_codes != nullptr) {
+    if (q_rscale == nullptr) return fail("qk_norm_rope: Q codes need their scale array");
+    if (q_lpad < L) return fail("qk_norm_rope: q_lpad=%lld below L=%lld", (long long)q_lpad, (long long)L);
+    if (reinterpret_cast<uintptr_t>(q_codes) % 4 || reinterpret_cast<uintptr_t>(q_rscale) % 4)
+      return fail("qk_norm_rope: Q codes and scales must be 4-byte aligned");
+  } else if (!write_q) {
+    return fail("qk_norm_rope: write_q = 0 needs the Q codes output");
+  }
   if (L == 0) return DC_OK;
   if (qkv == nullptr) return fail("qk_norm_rope: null qkv");
   if (D != 128) return fail("qk_norm_rope: head dim must be 128 (got %lld)", (long long)D);
@@ -1027,8 +1037,10 @@ int dc_qk_norm_rope(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64
   p.q_scale[0] = q_scale0; p.k_scale[0] = k_scale0;
   p.q_scale[1] = q_scale1 ? q_scale1 : q_scale0; p.k_scale[1] = k_scale1 ? k_scale1 : k_scale0;
   p.split_row = split_row; p.pe = pe; p.pe_row0 = pe_row0;
+  p.q_codes = q_codes; p.q_rscale = q_rscale; p.q_lpad = q_lpad; p.write_q = write_q;
+  const int64_t rows = q_codes != nullptr ? q_lpad : L;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
-  const int ctas = static_cast<int>(L < cap ? L : cap);
+  const int ctas = static_cast<int>(rows < cap ? rows : cap);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   constexpr int threads = 32 * dc::kRopeWarps;
   if (dtype == DC_DTYPE_BF16) dc::qk_norm_rope_kernel<__nv_bfloat16><<<ctas, threads, 0, st>>>(p);
@@ -1036,6 +1048,22 @@ int dc_qk_norm_rope(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64
   else return fail("qk_norm_rope: dtype must be fp16 or bf16");
   DC_CHECK_LAUNCH("qk_norm_rope launch");
   return DC_OK;
+}
+
+int dc_qk_norm_rope(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64_t ld_row, int64_t q_off,
+                    int64_t k_off, const void* q_scale0, const void* k_scale0, const void* q_scale1,
+                    const void* k_scale1, int64_t split_row, const float* pe, int64_t pe_row0, void* stream) {
+  return qk_norm_rope_impl(qkv, dtype, L, H, D, ld_row, q_off, k_off, q_scale0, k_scale0, q_scale1, k_scale1,
+                           split_row, pe, pe_row0, nullptr, nullptr, 0, 1, stream);
+}
+
+int dc_qk_norm_rope_q8(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64_t ld_row, int64_t q_off,
+                       int64_t k_off, const void* q_scale0, const void* k_scale0, const void* q_scale1,
+                       const void* k_scale1, int64_t split_row, const float* pe, int64_t pe_row0, int8_t* q_codes,
+                       float* q_rscale, int64_t q_lpad, int write_q, void* stream) {
+  if (q_codes == nullptr) return fail("qk_norm_rope_q8: null Q codes");
+  return qk_norm_rope_impl(qkv, dtype, L, H, D, ld_row, q_off, k_off, q_scale0, k_scale0, q_scale1, k_scale1,
+                           split_row, pe, pe_row0, q_codes, q_rscale, q_lpad, write_q, stream);
 }
 
 int dc_rescale(const int32_t* acc, int64_t lda, const float* sx, const float* sw, const void* bias, void* out,
@@ -1081,10 +1109,11 @@ int dc_attn_workspace_layout(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64
 static int attn_common(bool run_prep, bool run_main, const void* q, const void* k, const void* v, int dtype, int64_t B, int64_t H,
                        int64_t Lq, int64_t Lk, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
                        const int64_t* v_strides, float sm_scale, int mode, void* o, const int64_t* o_strides,
-                       void* workspace, size_t ws_bytes, void* stream) {
+                       void* workspace, size_t ws_bytes, void* stream, bool prep_q = true) {
   if (int r = check_attn_args(dtype, B, H, Lq, Lk, D, mode)) return r;
   if (run_prep) {
-    if (int r = check_strides(q, q_strides, "q")) return r;
+    if (prep_q)
+      if (int r = check_strides(q, q_strides, "q")) return r;
     if (int r = check_strides(k, k_strides, "k")) return r;
   }
   if (run_main) {
@@ -1101,15 +1130,15 @@ static int attn_common(bool run_prep, bool run_main, const void* q, const void* 
   int r = DC_OK;
   if (dtype == DC_DTYPE_BF16) {
     if (run_prep)
-      r = D == 128 ? attn_prep<__nv_bfloat16, 128>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st)
-                   : attn_prep<__nv_bfloat16, 64>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st);
+      r = D == 128 ? attn_prep<__nv_bfloat16, 128>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st, prep_q)
+                   : attn_prep<__nv_bfloat16, 64>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st, prep_q);
     if (r || !run_main) return r;
     return D == 128 ? attn_main<__nv_bfloat16, 128>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a, st)
                     : attn_main<__nv_bfloat16, 64>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a, st);
   }
   if (run_prep)
-    r = D == 128 ? attn_prep<__half, 128>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st)
-                 : attn_prep<__half, 64>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st);
+    r = D == 128 ? attn_prep<__half, 128>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st, prep_q)
+                 : attn_prep<__half, 64>(q, k, B, H, Lq, Lk, q_strides, k_strides, mode, ws, a, st, prep_q);
   if (r || !run_main) return r;
   return D == 128 ? attn_main<__half, 128>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a, st)
                   : attn_main<__half, 64>(v, B, H, Lq, Lk, v_strides, sm_scale, o, o_strides, ws, a, st);
@@ -1135,6 +1164,12 @@ int dc_attn_int8_prep(const void* q, const void* k, int dtype, int64_t B, int64_
                       size_t workspace_bytes, void* stream) {
   return attn_common(true, false, q, k, nullptr, dtype, B, H, Lq, Lk, D, q_strides, k_strides, nullptr, 1.0f, mode,
                      nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+int dc_attn_int8_prep_k(const void* k, int dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D,
+                        const int64_t* k_strides, int mode, void* workspace, size_t workspace_bytes, void* stream) {
+  return attn_common(true, false, nullptr, k, nullptr, dtype, B, H, Lq, Lk, D, nullptr, k_strides, nullptr, 1.0f, mode,
+                     nullptr, nullptr, workspace, workspace_bytes, stream, false);
 }
 
 int dc_attn_split_partials_size(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D, int nsplit, size_t* bytes) {

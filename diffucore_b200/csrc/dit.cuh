@@ -123,6 +123,14 @@ struct QkNormRopeParams {
   int64_t split_row;
   const float* pe;           // [L, 64, 2, 2] fp32: rows {cos, -sin}, {sin, cos} per rotary pair
   int64_t pe_row0;           // row r of qkv uses pe row pe_row0 + r
+  // Optional Q codes for the INT8 attention in the reference quant mode (one sequence): head h of
+  // row r gets codes q_codes[(h * q_lpad + r) * 128 ..] and scale q_rscale[h * q_lpad + r], with
+  // q_token_quant_kernel's arithmetic; rows [L, q_lpad) get zero codes and scales. write_q = 0
+  // leaves the normed, rotated q out of qkv (only the codes are needed then).
+  int8_t* q_codes = nullptr;
+  float* q_rscale = nullptr;
+  int64_t q_lpad = 0;
+  int write_q = 1;
 };
 
 // One CTA per row (grid-stride), 8 warps; warp w takes the row's (head, q|k) vectors w, w + 8, ...
@@ -168,6 +176,14 @@ __global__ void __launch_bounds__(32 * kRopeWarps)
 qk_norm_rope_kernel(const QkNormRopeParams p) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvec = static_cast<int>(2 * p.H);
+  if (p.q_codes != nullptr) {
+    // padding rows of the Q codes: zero, as the per-token quantizer leaves them
+    for (int64_t row = p.L + blockIdx.x; row < p.q_lpad; row += gridDim.x)
+      for (int h = warp; h < p.H; h += kRopeWarps) {
+        *reinterpret_cast<uint32_t*>(p.q_codes + (h * p.q_lpad + row) * 128 + lane * 4) = 0u;
+        if (lane == 0) p.q_rscale[h * p.q_lpad + row] = 0.0f;
+      }
+  }
   for (int64_t row = blockIdx.x; row < p.L; row += gridDim.x) {
     const float4* pe4 = reinterpret_cast<const float4*>(p.pe + (p.pe_row0 + row) * 256 + lane * 8);
     const float4 f0 = pe4[0], f1 = pe4[1];
@@ -187,7 +203,25 @@ qk_norm_rope_kernel(const QkNormRopeParams p) {
         const int v = v0 + b * kRopeWarps;
         if (v < nvec) {
           rms_rope4<T>(raw[b], (v & 1) ? ks : qs, f0, f1);
-          *reinterpret_cast<uint2*>(rbase + ((v & 1) ? p.k_off : p.q_off) + (v >> 1) * 128) = raw[b];
+          const bool is_q = (v & 1) == 0;
+          if (!is_q || p.write_q)
+            *reinterpret_cast<uint2*>(rbase + ((v & 1) ? p.k_off : p.q_off) + (v >> 1) * 128) = raw[b];
+          if (is_q && p.q_codes != nullptr) {
+            // the per-token Q codes of this head (q_token_quant_kernel's arithmetic on the
+            // rounded values just stored): amax over the 128 channels, codes rn(x * 127 / amax)
+            float f[8];
+            Vec8<T>::from_raw(make_uint4(raw[b].x, raw[b].y, 0u, 0u), f);
+            float amax = fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float inv = amax > 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+            uint32_t w = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w |= code_byte(__fmul_rn(f[i], inv)) << (8 * i);
+            const int64_t qrow = static_cast<int64_t>(v >> 1) * p.q_lpad + row;
+            *reinterpret_cast<uint32_t*>(p.q_codes + qrow * 128 + lane * 4) = w;
+            if (lane == 0) p.q_rscale[qrow] = __fdiv_rn(amax, 127.f);
+          }
         }
       }
     }

@@ -263,6 +263,12 @@ __device__ __forceinline__ int8_t quant_code(float x, float scale, int full = 0)
 // is bit-identical to quant_code on every element.
 constexpr float kRoundMagic = 12582912.0f;      // 1.5 * 2^23
 
+// Low byte of rn(y) for |y| <= 127.5 (a code): y + 1.5 * 2^23 rounds y to an integer with ties to
+// even, exactly as __float2int_rn, on the FMA pipe instead of the conversion unit.
+__device__ __forceinline__ uint32_t code_byte(float y) {
+  return __float_as_uint(__fadd_rn(y, kRoundMagic)) & 0xFFu;
+}
+
 __device__ __forceinline__ uint2 quant8(const float (&v)[8], float scale, float inv_scale, int full = 0) {
   uint32_t b[8];
   if (full) {

@@ -329,6 +329,12 @@ class LinearW:
 class CudaOps:
     """The sm_100a kernels behind the runner's steps."""
 
+    fuses_q8 = True      # qk_norm_rope can write the attention's Q codes (q8_workspace)
+
+    def exchange(self, out, inp, pg):
+        import torch.distributed as dist
+        dist.all_to_all_single(out, inp, group=pg)
+
     def ln_mod_quant(self, x, shift, scale, group, q, s):
         kernels.ln_mod_quant(x, shift, scale, group, q, s)
 
@@ -343,16 +349,17 @@ class CudaOps:
         kernels.gemm_w8a8_into(q, lin.weight, sx, lin.scale, lin.bias, out, ldo=ldo, gelu=gelu, gate=gate,
                                residual=residual, col_block=col_block, block_stride=block_stride)
 
-    def qk_norm_rope(self, qkv, q0, k0, q1, k1, split_row, pe):
-        kernels.qk_norm_rope(qkv, q0, k0, pe, q1, k1, split_row)
+    def qk_norm_rope(self, qkv, q0, k0, q1, k1, split_row, pe, q8_workspace=None):
+        kernels.qk_norm_rope(qkv, q0, k0, pe, q1, k1, split_row, q8_workspace=q8_workspace,
+                             write_q=q8_workspace is None)
 
-    def attention(self, q, k, v, out, sm_scale, backend, mode, workspace):
+    def attention(self, q, k, v, out, sm_scale, backend, mode, workspace, q_ready=False):
         if backend == "sdpa":
             o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
                                                scale=sm_scale)
             out.copy_(o.transpose(1, 2))
         else:
-            kernels.attn_int8(q, k, v, sm_scale, mode, workspace=workspace, out=out)
+            kernels.attn_int8(q, k, v, sm_scale, mode, workspace=workspace, out=out, q_ready=q_ready)
 
 
 class TimedOps:
@@ -550,10 +557,20 @@ class FluxRunner:
     def _codes(self, rows: int, K: int, row0: int = 0) -> torch.Tensor:
         return self.codes[: self.Lr * K].view(self.Lr, K)[row0: row0 + rows]
 
+    def _fuse_q8(self, blk) -> bool:
+        """Whether the norm + RoPE pass emits the Q codes: INT8 attention in the reference quant
+        mode on ops that support it (environment DC_FLUX_Q8=0 turns it off)."""
+        return (getattr(self.ops, "fuses_q8", False) and blk.attn_backend == "int8_turing"
+                and self.attn_mode == _lib.MODE_REF and self.workspace is not None
+                and os.environ.get("DC_FLUX_Q8", "1") != "0")
+
     def _exchange(self, out: torch.Tensor, inp: torch.Tensor, async_op: bool = False):
         """All-to-all of ``inp`` into ``out``; with ``async_op`` the collective's handle (the caller
-        waits on it before reading ``out`` or writing ``inp``)."""
+        waits on it before reading ``out`` or writing ``inp``). Blocking exchanges go through the
+        ops object when it has an ``exchange`` (so a timing wrapper sees them)."""
         import torch.distributed as dist
+        if not async_op and hasattr(self.ops, "exchange"):
+            return self.ops.exchange(out, inp, self.pg)
         return dist.all_to_all_single(out, inp, group=self.pg, async_op=async_op)
 
     def _qkv_views(self):
@@ -574,8 +591,14 @@ class FluxRunner:
         if self.P > 1 and not exchanged:
             self._exchange(self.recv, self.send)
         r4, q, k, v = self._qkv_views()
-        self.ops.qk_norm_rope(r4, q0, k0, q1, k1, split_row, self.pe)
-        self.ops.attention(q, k, v, out4, self.sm_scale, blk.attn_backend, self.attn_mode, self.workspace)
+        if self._fuse_q8(blk):
+            # the norm + RoPE pass writes the attention's Q codes; q itself is not written back
+            self.ops.qk_norm_rope(r4, q0, k0, q1, k1, split_row, self.pe, q8_workspace=self.workspace)
+            self.ops.attention(q, k, v, out4, self.sm_scale, blk.attn_backend, self.attn_mode, self.workspace,
+                               q_ready=True)
+        else:
+            self.ops.qk_norm_rope(r4, q0, k0, q1, k1, split_row, self.pe)
+            self.ops.attention(q, k, v, out4, self.sm_scale, blk.attn_backend, self.attn_mode, self.workspace)
         if self.P > 1:
             self._exchange(self.O_recv, self.O)
 

@@ -185,10 +185,14 @@ def quant_rows_seg(recv: torch.Tensor, x2: torch.Tensor | None, group: int, q: t
 
 def qk_norm_rope(qkv: torch.Tensor, q_scale0: torch.Tensor, k_scale0: torch.Tensor, pe: torch.Tensor,
                  q_scale1: torch.Tensor | None = None, k_scale1: torch.Tensor | None = None,
-                 split_row: int | None = None) -> None:
+                 split_row: int | None = None, q8_workspace: torch.Tensor | None = None,
+                 write_q: bool = True) -> None:
     """In place on ``qkv`` [L, 3, H, 128] (row-strided): RMSNorm of q and k per head with their
     scales, then RoPE with ``pe`` [L, 64, 2, 2] fp32. Rows below ``split_row`` use the ``*0``
-    scales, the rest the ``*1`` scales."""
+    scales, the rest the ``*1`` scales. With ``q8_workspace`` (an attention workspace for
+    (1, H, L, L, 128) in the reference quant mode) the Q codes and scales go straight into it
+    (``dc_qk_norm_rope_q8``); :func:`attn_int8` with ``q_ready=True`` then quantizes only K, and
+    ``write_q=False`` leaves q in ``qkv`` untouched."""
     _require_cuda(qkv, pe)
     L, three, H, D = qkv.shape
     if three != 3 or qkv.stride(3) != 1 or qkv.stride(2) != D or qkv.stride(1) != H * D:
@@ -201,9 +205,20 @@ def qk_norm_rope(qkv: torch.Tensor, q_scale0: torch.Tensor, k_scale0: torch.Tens
     if pe.dtype != torch.float32 or not pe.is_contiguous() or pe.numel() < L * D * 2:
         raise ValueError(f"qk_norm_rope: pe must be a contiguous fp32 table of at least [{L}, {D // 2}, 2, 2]")
     lib = _lib.load()
-    _lib.check(lib.dc_qk_norm_rope(_ptr(qkv), _DTYPE[qkv.dtype], L, H, D, qkv.stride(0), 0, H * D, _ptr(q_scale0),
-                                   _ptr(k_scale0), _ptr(q_scale1), _ptr(k_scale1), int(split_row), _ptr(pe), 0,
-                                   _stream(qkv)))
+    if q8_workspace is None:
+        _lib.check(lib.dc_qk_norm_rope(_ptr(qkv), _DTYPE[qkv.dtype], L, H, D, qkv.stride(0), 0, H * D,
+                                       _ptr(q_scale0), _ptr(k_scale0), _ptr(q_scale1), _ptr(k_scale1),
+                                       int(split_row), _ptr(pe), 0, _stream(qkv)))
+        return
+    lay = attn_workspace_layout(1, H, L, L, D, _lib.MODE_REF)
+    if q8_workspace.numel() < lay["total"] or q8_workspace.dtype != torch.uint8:
+        raise ValueError(f"qk_norm_rope: q8_workspace needs {lay['total']} bytes (uint8)")
+    base = q8_workspace.data_ptr()
+    _lib.check(lib.dc_qk_norm_rope_q8(_ptr(qkv), _DTYPE[qkv.dtype], L, H, D, qkv.stride(0), 0, H * D,
+                                      _ptr(q_scale0), _ptr(k_scale0), _ptr(q_scale1), _ptr(k_scale1),
+                                      int(split_row), _ptr(pe), 0, ctypes.c_void_p(base + lay["q_codes"]),
+                                      ctypes.c_void_p(base + lay["q_scale"]), lay["Lq_pad"], int(bool(write_q)),
+                                      _stream(qkv)))
 
 
 def attn_workspace_layout(B: int, H: int, Lq: int, Lk: int, D: int, mode: int) -> dict:
@@ -233,29 +248,42 @@ def _check_attn_inputs(q, k, v):
 
 def attn_int8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float,
               mode: int = _lib.MODE_REF, workspace: torch.Tensor | None = None,
-              out: torch.Tensor | None = None) -> torch.Tensor:
+              out: torch.Tensor | None = None, q_ready: bool = False) -> torch.Tensor:
     """INT8 attention over ``(B, L, H, D)`` q/k/v (any strides with stride(-1) == 1 and the
     others multiples of 8) -> contiguous ``(B, Lq, H, D)`` in the input dtype. Shapes whose grid
     fills the GPU poorly (few heads over long sequences, a sequence-parallel rank's share) run
     :func:`attn_int8_split` with the key-range count :func:`choose_attn_split` picks; the
-    environment variable ``DC_ATTN_SPLIT=0`` turns that routing off."""
+    environment variable ``DC_ATTN_SPLIT=0`` turns that routing off. ``q_ready``: ``workspace``
+    already holds the Q codes and scales (:func:`qk_norm_rope` with ``q8_workspace``), so only K
+    is quantized here and ``q`` is not read."""
     B, Lq, Lk, H, D = _check_attn_inputs(q, k, v)
+    if q_ready and workspace is None:
+        raise ValueError("attn_int8: q_ready needs the workspace that holds the Q codes")
     if os.environ.get("DC_ATTN_SPLIT", "auto") != "0":
         nsplit = choose_attn_split(B, H, Lq, Lk, _sm_count(q.device), D=D)
         if nsplit > 1:
-            return attn_int8_split(q, k, v, sm_scale, nsplit, mode, workspace=workspace, out=out)
+            return attn_int8_split(q, k, v, sm_scale, nsplit, mode, workspace=workspace, out=out, q_ready=q_ready)
     lib = _lib.load()
     nbytes = ctypes.c_size_t(0)
     _lib.check(lib.dc_attn_workspace_size(B, H, Lq, Lk, D, int(mode), ctypes.byref(nbytes)))
     if workspace is None or workspace.numel() < nbytes.value:
+        if q_ready:
+            raise ValueError(f"attn_int8: workspace below the {nbytes.value} bytes this shape needs")
         workspace = torch.empty(nbytes.value, device=q.device, dtype=torch.uint8)
     if out is None:
         out = torch.empty(B, Lq, H, D, device=q.device, dtype=q.dtype)
     with torch.cuda.device(q.device):
-        _lib.check(lib.dc_attn_int8_fwd(_ptr(q), _ptr(k), _ptr(v), _DTYPE[q.dtype], B, H, Lq, Lk, D,
-                                        _blhd_strides(q), _blhd_strides(k), _blhd_strides(v),
-                                        float(sm_scale), int(mode), _ptr(out), _blhd_strides(out),
-                                        _ptr(workspace), workspace.numel(), _stream(q)))
+        if q_ready:
+            _lib.check(lib.dc_attn_int8_prep_k(_ptr(k), _DTYPE[k.dtype], B, H, Lq, Lk, D, _blhd_strides(k), int(mode),
+                                               _ptr(workspace), workspace.numel(), _stream(k)))
+            _lib.check(lib.dc_attn_int8_main(_ptr(v), _DTYPE[v.dtype], B, H, Lq, Lk, D, _blhd_strides(v),
+                                             float(sm_scale), int(mode), _ptr(out), _blhd_strides(out),
+                                             _ptr(workspace), workspace.numel(), _stream(v)))
+        else:
+            _lib.check(lib.dc_attn_int8_fwd(_ptr(q), _ptr(k), _ptr(v), _DTYPE[q.dtype], B, H, Lq, Lk, D,
+                                            _blhd_strides(q), _blhd_strides(k), _blhd_strides(v),
+                                            float(sm_scale), int(mode), _ptr(out), _blhd_strides(out),
+                                            _ptr(workspace), workspace.numel(), _stream(q)))
     return out
 
 
@@ -306,7 +334,8 @@ def attn_split_partials_bytes(B: int, H: int, Lq: int, Lk: int, D: int, nsplit: 
 
 def attn_int8_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float, nsplit: int,
                     mode: int = _lib.MODE_REF, workspace: torch.Tensor | None = None,
-                    partials: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+                    partials: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                    q_ready: bool = False) -> torch.Tensor:
     """:func:`attn_int8` with the keys divided into ``nsplit`` ranges (one CTA per 256 query rows and
     key range, then a merge of the ranges): the same result to rounding, for grids of few heads."""
     B, Lq, Lk, H, D = _check_attn_inputs(q, k, v)
@@ -314,6 +343,8 @@ def attn_int8_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale:
     nbytes = ctypes.c_size_t(0)
     _lib.check(lib.dc_attn_workspace_size(B, H, Lq, Lk, D, int(mode), ctypes.byref(nbytes)))
     if workspace is None or workspace.numel() < nbytes.value:
+        if q_ready:
+            raise ValueError(f"attn_int8_split: workspace below the {nbytes.value} bytes this shape needs")
         workspace = torch.empty(nbytes.value, device=q.device, dtype=torch.uint8)
     pbytes = attn_split_partials_bytes(B, H, Lq, Lk, D, nsplit)
     if partials is None or partials.numel() < pbytes:
@@ -321,9 +352,13 @@ def attn_int8_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale:
     if out is None:
         out = torch.empty(B, Lq, H, D, device=q.device, dtype=q.dtype)
     with torch.cuda.device(q.device):
-        _lib.check(lib.dc_attn_int8_prep(_ptr(q), _ptr(k), _DTYPE[q.dtype], B, H, Lq, Lk, D, _blhd_strides(q),
-                                         _blhd_strides(k), int(mode), _ptr(workspace), workspace.numel(),
-                                         _stream(q)))
+        if q_ready:
+            _lib.check(lib.dc_attn_int8_prep_k(_ptr(k), _DTYPE[k.dtype], B, H, Lq, Lk, D, _blhd_strides(k), int(mode),
+                                               _ptr(workspace), workspace.numel(), _stream(k)))
+        else:
+            _lib.check(lib.dc_attn_int8_prep(_ptr(q), _ptr(k), _DTYPE[q.dtype], B, H, Lq, Lk, D, _blhd_strides(q),
+                                             _blhd_strides(k), int(mode), _ptr(workspace), workspace.numel(),
+                                             _stream(q)))
         _lib.check(lib.dc_attn_int8_main_split(_ptr(v), _DTYPE[v.dtype], B, H, Lq, Lk, D, _blhd_strides(v),
                                                float(sm_scale), int(mode), _ptr(out), _blhd_strides(out),
                                                _ptr(workspace), workspace.numel(), int(nsplit), _ptr(partials),

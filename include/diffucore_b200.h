@@ -139,6 +139,19 @@ int dc_qk_norm_rope(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64
                     int64_t k_off, const void* q_scale0, const void* k_scale0, const void* q_scale1,
                     const void* k_scale1, int64_t split_row, const float* pe, int64_t pe_row0, void* stream);
 
+/* dc_qk_norm_rope that also emits the INT8 attention's Q codes and per-token scales (reference
+ * quant mode) for one sequence (batch 1), straight into an attention workspace: head h of row r
+ * gets codes q_codes[(h * q_lpad + r) * D ..] and scale q_rscale[h * q_lpad + r], bit for bit the
+ * per-token quantization of dc_attn_int8_prep (int8_attn_sm80.cu:341-388) on the rounded q; rows
+ * [L, q_lpad) get zeros. Pass the workspace's Q codes / Q scale addresses and its padded length
+ * (dc_attn_workspace_layout), then run dc_attn_int8_prep_k and dc_attn_int8_main. write_q = 0
+ * leaves q in qkv as it was (only the codes are produced). Fuses the reference's `QKNorm` +
+ * `apply_rope` (flux_dit.py:129-151, :179-184) with the attention's Q quantization. */
+int dc_qk_norm_rope_q8(void* qkv, int dtype, int64_t L, int64_t H, int64_t D, int64_t ld_row, int64_t q_off,
+                       int64_t k_off, const void* q_scale0, const void* k_scale0, const void* q_scale1,
+                       const void* k_scale1, int64_t split_row, const float* pe, int64_t pe_row0, int8_t* q_codes,
+                       float* q_rscale, int64_t q_lpad, int write_q, void* stream);
+
 /* out[M, N] = dtype(float(acc) * (sx[m] * sw[n])) (+ bias in dtype), acc int32 [M, N] with row
  * stride lda: the epilogue of dc_gemm_w8a8 as a separate pass, for an int32 result already in
  * hand. Replaces `rescale` (src/diffucore/models/_int8.py:313-323) and its Triton
@@ -178,6 +191,12 @@ int dc_attn_int8_fwd(const void* q, const void* k, const void* v, int dtype, int
 int dc_attn_int8_prep(const void* q, const void* k, int dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk,
                       int64_t D, const int64_t* q_strides, const int64_t* k_strides, int mode, void* workspace,
                       size_t workspace_bytes, void* stream);
+
+/* The K half of dc_attn_int8_prep (K codes, K scales and, in mode REF, ksum), for callers whose
+ * Q codes are already in the workspace (dc_qk_norm_rope_q8). Replaces the reference's K prep
+ * kernels (int8_attn_sm80.cu:38-142). */
+int dc_attn_int8_prep_k(const void* k, int dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D,
+                        const int64_t* k_strides, int mode, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Only the attention stage of dc_attn_int8_fwd, over a workspace that dc_attn_int8_prep (same
  * B, H, Lq, Lk, D, mode) already filled: lets a caller quantize Q/K once (or elsewhere, e.g. before

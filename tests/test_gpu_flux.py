@@ -232,3 +232,86 @@ def test_flux_backbone_batch_equals_per_sample():
     for b in range(2):
         one = model(img[b:b + 1], iid, txt[b:b + 1], tid, t[b:b + 1], y[b:b + 1])
         assert torch.equal(both[b:b + 1], one)
+
+
+# ─── QK norm + RoPE emitting the attention's Q codes (dc_qk_norm_rope_q8) ───────────────
+
+def _qkv_case(L, H, seed):
+    g = torch.Generator().manual_seed(seed)
+    qkv = (torch.randn(L, 3, H, 128, generator=g) * 2).to(torch.bfloat16).to(DEV)
+    sc = [(1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16).to(DEV) for _ in range(4)]
+    ids = torch.cat([torch.zeros(min(L, 64), 3), flux.img_ids(16, 16, 2)[0]])[:L]
+    if ids.shape[0] < L:
+        ids = torch.cat([ids, torch.zeros(L - ids.shape[0], 3)])
+    pe = flux.rope_table(ids.to(DEV), (16, 56, 56), 10_000)
+    return qkv, sc, pe
+
+
+@pytest.mark.parametrize("L,H", [(300, 3), (1000, 4), (4608, 2)])
+def test_qk_norm_rope_q_codes_equal_the_prep_codes(L, H):
+    """The Q codes and scales written by the norm + RoPE pass equal the attention prep's per-token
+    codes of the normed q bit for bit (padding rows zero), q is left as it was, k is normed."""
+    qkv, sc, pe = _qkv_case(L, H, L + H)
+    split = min(64, L)
+    want_qkv = qkv.clone()
+    kernels.qk_norm_rope(want_qkv, sc[0], sc[1], pe, sc[2], sc[3], split)
+    want = kernels.attn_int8_prep(want_qkv[:, 0].unsqueeze(0), want_qkv[:, 1].unsqueeze(0), _lib.MODE_REF)
+    lay = kernels.attn_workspace_layout(1, H, L, L, 128, _lib.MODE_REF)
+    ws = torch.full((lay["total"],), 0x5A, device=DEV, dtype=torch.uint8)     # stale bytes
+    got_qkv = qkv.clone()
+    kernels.qk_norm_rope(got_qkv, sc[0], sc[1], pe, sc[2], sc[3], split, q8_workspace=ws, write_q=False)
+    torch.cuda.synchronize()
+    Lp = lay["Lq_pad"]
+    codes = ws[lay["q_codes"]: lay["q_codes"] + H * Lp * 128].view(torch.int8).view(H, Lp, 128)
+    scales = ws[lay["q_scale"]: lay["q_scale"] + H * Lp * 4].view(torch.float32).view(H, Lp)
+    assert torch.equal(codes[:, :L], want["q_codes"][0]) and torch.equal(scales[:, :L], want["q_scale"][0])
+    assert not codes[:, L:].any() and not scales[:, L:].any()
+    assert torch.equal(got_qkv[:, 0], qkv[:, 0])                 # q not written back
+    assert torch.equal(got_qkv[:, 1:], want_qkv[:, 1:])          # k normed, v untouched
+
+
+@pytest.mark.parametrize("L,H", [(300, 3), (4608, 3)])
+def test_attention_with_fused_q_codes_equals_unfused(L, H):
+    """Norm + RoPE with Q codes, then the attention with K-only prep, gives the unfused path's
+    output bit for bit (plain and key-range-split routing)."""
+    qkv, sc, pe = _qkv_case(L, H, 7 * L + H)
+    ref_qkv = qkv.clone()
+    kernels.qk_norm_rope(ref_qkv, sc[0], sc[1], pe, sc[2], sc[3], min(64, L))
+    q, k, v = (ref_qkv[:, i].unsqueeze(0) for i in range(3))
+    lay = kernels.attn_workspace_layout(1, H, L, L, 128, _lib.MODE_REF)
+    for split in ("0", "auto"):
+        import os
+        prev = os.environ.get("DC_ATTN_SPLIT")
+        os.environ["DC_ATTN_SPLIT"] = split
+        try:
+            want = kernels.attn_int8(q, k, v, 128 ** -0.5, _lib.MODE_REF)
+            got_qkv = qkv.clone()
+            ws = torch.empty(lay["total"], device=DEV, dtype=torch.uint8)
+            kernels.qk_norm_rope(got_qkv, sc[0], sc[1], pe, sc[2], sc[3], min(64, L), q8_workspace=ws,
+                                 write_q=False)
+            gq, gk, gv = (got_qkv[:, i].unsqueeze(0) for i in range(3))
+            got = kernels.attn_int8(gq, gk, gv, 128 ** -0.5, _lib.MODE_REF, workspace=ws, q_ready=True)
+        finally:
+            if prev is None:
+                os.environ.pop("DC_ATTN_SPLIT", None)
+            else:
+                os.environ["DC_ATTN_SPLIT"] = prev
+        torch.cuda.synchronize()
+        assert _lib.device_error() == 0
+        assert torch.equal(got, want), split
+
+
+def test_flux_runner_fused_q_codes_bit_identical(monkeypatch):
+    """The runner's fused Q-code path (default) against DC_FLUX_Q8=0 on the tiny fixture model."""
+    fx = _fixture()
+    outs = []
+    for env in ("0", "1"):
+        monkeypatch.setenv("DC_FLUX_Q8", env)
+        runner = _tiny_runner(256, "int8_turing")
+        runner.set_positions(torch.from_numpy(fx["img_ids"]), torch.from_numpy(fx["txt_ids"]))
+        img = bits_to_torch(fx["img"], torch.bfloat16)[0].to(DEV)
+        txt = bits_to_torch(fx["txt"], torch.bfloat16)[0].to(DEV)
+        y = bits_to_torch(fx["y"], torch.bfloat16).to(DEV)
+        outs.append(runner.forward(img, txt, torch.full((1,), 0.7, dtype=torch.bfloat16, device=DEV), y).clone())
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
