@@ -436,6 +436,12 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
         issue_s(0, 0); mma_commit(&s_ready[0]);
         issue_s(1, 0); mma_commit(&s_ready[1]);
       }
+      // In the loop, descriptors are stage 0's plus st * kStage in the start-address field, both
+      // waits on the stages (this tile's V, the next tile's K, loaded stages ahead) come first, and the
+      // MMA thread then only waits on P between its MMA groups.
+      const uint64_t qd0 = smem_desc_sw(sq_addr, 16, SM::kQKAtom, SM::kQKSwizzle);
+      const uint64_t kd0 = smem_desc_sw(smem_u32(sstage), 16, SM::kQKAtom, SM::kQKSwizzle);
+      const uint64_t vd0 = smem_desc_sw(smem_u32(sstage + SM::kKTile), SM::kVHalf, 1024, 2);
       for (int j = 0; j < n && ok; ++j) {
         const int st = j % kAttnStages;
         const uint32_t ph = (j / kAttnStages) & 1;
@@ -443,19 +449,40 @@ attn_int8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constan
         const uint32_t ph1 = ((j + 1) / kAttnStages) & 1;
         const bool more = j + 1 < n;
         if (!mbar_wait(&v_full[st], ph, abort)) { ok = false; break; }
-        for (int i = 0; i < 2 && ok; ++i) {
+        if (more && !mbar_wait(&k_full[st1], ph1, abort)) { ok = false; break; }
+        const uint64_t vd = vd0 + static_cast<uint64_t>(st * (SM::kStage >> 4));
+        const uint64_t kd = kd0 + static_cast<uint64_t>(st1 * (SM::kStage >> 4));
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+#pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            if (!mbar_wait(&p_ready[i][hh], j & 1, abort)) { ok = false; break; }
-            tc_fence_after();
-            issue_pv(i, hh, st, j > 0 || hh > 0);
-            mma_commit(&pv_done[i][hh]);
+            if (ok) ok = mbar_wait(&p_ready[i][hh], j & 1, abort);
+            if (ok) {
+              tc_fence_after();
+              // O_i += P_i[:, 64 keys of half hh] . V[those keys, :] (see issue_pv)
+              uint64_t bd = vd + static_cast<uint64_t>((hh * 64 * 128) >> 4);
+              const uint32_t d = tmem + kOCol + i * D;
+              uint32_t a = tmem + i * 128 + hh * 64;
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                mma_f16_ts(d, a, bd, idesc_o, (j > 0 || hh > 0 || kk > 0) ? 1u : 0u);
+                bd += 2048 >> 4;
+                a += 8;
+              }
+              mma_commit(&pv_done[i][hh]);
+            }
           }
-          if (!ok) break;
-          if (i == 1) mma_commit(&kv_empty[st]);
-          if (more) {
-            if (i == 0 && !mbar_wait(&k_full[st1], ph1, abort)) { ok = false; break; }
-            tc_fence_after();
-            issue_s(i, st1);
+          if (ok && i == 1) mma_commit(&kv_empty[st]);
+          if (ok && more) {
+            uint64_t ad = qd0 + static_cast<uint64_t>((i * SM::kQTile) >> 4);
+            uint64_t bd = kd;
+            const uint32_t d = tmem + i * 128;
+#pragma unroll
+            for (int kk = 0; kk < D / 32; ++kk) {
+              mma_i8_ss(d, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+              ad += 32 >> 4;
+              bd += 32 >> 4;
+            }
             mma_commit(&s_ready[i]);
           }
         }
