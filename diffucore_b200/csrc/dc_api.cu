@@ -1038,9 +1038,13 @@ static int qk_norm_rope_impl(void* qkv, int dtype, int64_t L, int64_t H, int64_t
   p.q_scale[1] = q_scale1 ? q_scale1 : q_scale0; p.k_scale[1] = k_scale1 ? k_scale1 : k_scale0;
   p.split_row = split_row; p.pe = pe; p.pe_row0 = pe_row0;
   p.q_codes = q_codes; p.q_rscale = q_rscale; p.q_lpad = q_lpad; p.write_q = write_q;
-  const int64_t rows = q_codes != nullptr ? q_lpad : L;
+  if (L * 2 * H >= (int64_t(1) << 31)) return fail("qk_norm_rope: L * 2H must stay below 2^31");
+  // one warp per (row, vector); the Q-code padding rows need CTAs too
+  const int64_t warps = L * 2 * H;
+  int64_t want = (warps + dc::kRopeWarps - 1) / dc::kRopeWarps;
+  if (q_codes != nullptr && q_lpad - L > want) want = q_lpad - L;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
-  const int ctas = static_cast<int>(rows < cap ? rows : cap);
+  const int ctas = static_cast<int>(want < cap ? want : cap);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   constexpr int threads = 32 * dc::kRopeWarps;
   if (dtype == DC_DTYPE_BF16) dc::qk_norm_rope_kernel<__nv_bfloat16><<<ctas, threads, 0, st>>>(p);

@@ -133,9 +133,8 @@ struct QkNormRopeParams {
   int write_q = 1;
 };
 
-// One CTA per row (grid-stride), 8 warps; warp w takes the row's (head, q|k) vectors w, w + 8, ...
-// (lane holds elements 4 lane .. 4 lane + 3 = rotary pairs 2 lane, 2 lane + 1). The row's RoPE
-// entries are loaded once per warp and all of a warp's vectors are loaded before any is computed.
+// One warp per (row, head, q|k) vector (lane holds elements 4 lane .. 4 lane + 3 = rotary pairs
+// 2 lane, 2 lane + 1); a warp loads its kRopeBatch vectors before computing any.
 template <typename T>
 __device__ __forceinline__ void rms_rope4(uint2& raw, const T* scl, float4 f0, float4 f1) {
   const uint2 sraw = *reinterpret_cast<const uint2*>(scl);
@@ -169,7 +168,7 @@ __device__ __forceinline__ void rms_rope4(uint2& raw, const T* scl, float4 f0, f
 }
 
 constexpr int kRopeWarps = 8;
-constexpr int kRopeBatch = 6;     // vectors per warp loaded together (2 H / 8 for H = 24)
+constexpr int kRopeBatch = 6;     // vectors per warp loaded together
 
 template <typename T>
 __global__ void __launch_bounds__(32 * kRopeWarps)
@@ -184,45 +183,51 @@ qk_norm_rope_kernel(const QkNormRopeParams p) {
         if (lane == 0) p.q_rscale[h * p.q_lpad + row] = 0.0f;
       }
   }
-  for (int64_t row = blockIdx.x; row < p.L; row += gridDim.x) {
-    const float4* pe4 = reinterpret_cast<const float4*>(p.pe + (p.pe_row0 + row) * 256 + lane * 8);
-    const float4 f0 = pe4[0], f1 = pe4[1];
-    const bool first = row < p.split_row;
-    const T* qs = static_cast<const T*>(first ? p.q_scale[0] : p.q_scale[1]) + lane * 4;
-    const T* ks = static_cast<const T*>(first ? p.k_scale[0] : p.k_scale[1]) + lane * 4;
-    T* rbase = static_cast<T*>(p.qkv) + row * p.ld_row + lane * 4;
-    for (int v0 = warp; v0 < nvec; v0 += kRopeWarps * kRopeBatch) {
-      uint2 raw[kRopeBatch];
+  // (row, vector) items, item = row * nvec + v, dealt to the warps of the grid in turn: few heads
+  // per row (a sequence-parallel split leaves 3 of 24) fill the warps as well as many do.
+  const uint32_t n_items = static_cast<uint32_t>(p.L) * static_cast<uint32_t>(nvec);   // < 2^31 (host)
+  const uint32_t nw = gridDim.x * kRopeWarps;
+  for (uint32_t i0 = blockIdx.x * kRopeWarps + warp; i0 < n_items; i0 += nw * kRopeBatch) {
+    uint2 raw[kRopeBatch];
+    uint32_t rows[kRopeBatch];
+    int vs[kRopeBatch];
 #pragma unroll
-      for (int b = 0; b < kRopeBatch; ++b) {
-        const int v = v0 + b * kRopeWarps;
-        if (v < nvec) raw[b] = *reinterpret_cast<const uint2*>(rbase + ((v & 1) ? p.k_off : p.q_off) + (v >> 1) * 128);
-      }
+    for (int b = 0; b < kRopeBatch; ++b) {
+      const uint32_t item = i0 + b * nw;
+      rows[b] = item / static_cast<uint32_t>(nvec);
+      vs[b] = static_cast<int>(item - rows[b] * static_cast<uint32_t>(nvec));
+      if (item < n_items)
+        raw[b] = *reinterpret_cast<const uint2*>(static_cast<const T*>(p.qkv) + rows[b] * p.ld_row + lane * 4 +
+                                                 ((vs[b] & 1) ? p.k_off : p.q_off) + (vs[b] >> 1) * 128);
+    }
 #pragma unroll
-      for (int b = 0; b < kRopeBatch; ++b) {
-        const int v = v0 + b * kRopeWarps;
-        if (v < nvec) {
-          rms_rope4<T>(raw[b], (v & 1) ? ks : qs, f0, f1);
-          const bool is_q = (v & 1) == 0;
-          if (!is_q || p.write_q)
-            *reinterpret_cast<uint2*>(rbase + ((v & 1) ? p.k_off : p.q_off) + (v >> 1) * 128) = raw[b];
-          if (is_q && p.q_codes != nullptr) {
-            // the per-token Q codes of this head (q_token_quant_kernel's arithmetic on the
-            // rounded values just stored): amax over the 128 channels, codes rn(x * 127 / amax)
-            float f[8];
-            Vec8<T>::from_raw(make_uint4(raw[b].x, raw[b].y, 0u, 0u), f);
-            float amax = fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
+    for (int b = 0; b < kRopeBatch; ++b) {
+      if (i0 + b * nw >= n_items) break;             // warp-uniform; later items are further out
+      const int64_t row = rows[b];
+      const int v = vs[b];
+      const float4* pe4 = reinterpret_cast<const float4*>(p.pe + (p.pe_row0 + row) * 256 + lane * 8);
+      const bool first = row < p.split_row;
+      const bool is_q = (v & 1) == 0;
+      const T* scl = static_cast<const T*>(is_q ? (first ? p.q_scale[0] : p.q_scale[1])
+                                                : (first ? p.k_scale[0] : p.k_scale[1])) + lane * 4;
+      rms_rope4<T>(raw[b], scl, pe4[0], pe4[1]);
+      T* dst = static_cast<T*>(p.qkv) + row * p.ld_row + lane * 4 + (is_q ? p.q_off : p.k_off) + (v >> 1) * 128;
+      if (!is_q || p.write_q) *reinterpret_cast<uint2*>(dst) = raw[b];
+      if (is_q && p.q_codes != nullptr) {
+        // the per-token Q codes of this head (q_token_quant_kernel's arithmetic on the rounded
+        // values just stored): amax over the 128 channels, codes rn(x * 127 / amax)
+        float f[8];
+        Vec8<T>::from_raw(make_uint4(raw[b].x, raw[b].y, 0u, 0u), f);
+        float amax = fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            const float inv = amax > 0.f ? __fdiv_rn(127.f, amax) : 0.f;
-            uint32_t w = 0;
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float inv = amax > 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+        uint32_t w = 0;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) w |= code_byte(__fmul_rn(f[i], inv)) << (8 * i);
-            const int64_t qrow = static_cast<int64_t>(v >> 1) * p.q_lpad + row;
-            *reinterpret_cast<uint32_t*>(p.q_codes + qrow * 128 + lane * 4) = w;
-            if (lane == 0) p.q_rscale[qrow] = __fdiv_rn(amax, 127.f);
-          }
-        }
+        for (int i = 0; i < 4; ++i) w |= code_byte(__fmul_rn(f[i], inv)) << (8 * i);
+        const int64_t qrow = static_cast<int64_t>(v >> 1) * p.q_lpad + row;
+        *reinterpret_cast<uint32_t*>(p.q_codes + qrow * 128 + lane * 4) = w;
+        if (lane == 0) p.q_rscale[qrow] = __fdiv_rn(amax, 127.f);
       }
     }
   }
