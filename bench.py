@@ -1061,6 +1061,39 @@ def bench_flux_headline(args, world, rank, dev, peaks, sampler) -> dict:
     return head
 
 
+def bench_exchange(args, world: int, rank: int, dev) -> dict:
+    """The Ulysses exchange alone: NCCL ``all_to_all_single`` of bf16 rows at the FLUX sizes per rank
+    (q/k/v out: rows x 9216, attention output back: rows x 3072, rows = tokens / N at 1024^2 and
+    2048^2), CUDA events over ``steps`` calls after ``warmup``, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    if world < 2:
+        return {"skipped": "needs N > 1 ranks"}
+    out = {}
+    for side in (1024, 2048):
+        rows = (FLUX_TXT + (side // 16) ** 2) // world
+        for cols, what in ((9216, "qkv"), (3072, "attn_out")):
+            x = torch.randn(rows * cols, device=dev).to(torch.bfloat16)
+            y = torch.empty_like(x)
+            for _ in range(args.warmup):
+                dist.all_to_all_single(y, x)
+            torch.cuda.synchronize()
+            _barrier(world)
+            s, e = _events(2)
+            s.record()
+            for _ in range(args.steps):
+                dist.all_to_all_single(y, x)
+            e.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([s.elapsed_time(e) / args.steps], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sent = rows * cols * 2 * (world - 1) / world
+            out[f"{side}px_{what}_{rows}x{cols}"] = {"us": round(t.item() * 1e3, 1),
+                                                      "gbs_sent_per_rank": round(sent / (t.item() * 1e-3) / 1e9, 1)}
+            del x, y
+    return {"what": "NCCL all_to_all_single, bf16, Ulysses exchange sizes per rank", "n_gpus": world, **out}
+
+
 def bench_reference_gpu(args, dev) -> dict:
     """The reference's own GPU path for the two hot calls, timed on this GPU beside this library's:
     its W8A8 linear (Triton `_rot_quant_kernel` -> torch._int_mm (cuBLASLt) -> Triton
@@ -1445,11 +1478,11 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-extras", action="store_true", help="the headline FLUX step only")
     ap.add_argument("--only", default="all",
-                    choices=("all", "attention", "gemm", "flux", "glue", "sdxl", "variants", "rowq", "refgpu"),
+                    choices=("all", "attention", "gemm", "flux", "glue", "sdxl", "variants", "rowq", "refgpu", "exchange"),
                     help="attention: BASELINE config 2 alone; gemm / flux: the config-1 W8A8 linear / the FLUX DiT "
                          "at 1024^2 and 2048^2; glue: the FLUX glue kernels; sdxl: the UNet; variants: kernel "
                          "variants against the defaults; rowq: the row quantizers; refgpu: the reference's own GPU "
-                         "path against this library's")
+                         "path against this library's; exchange: the Ulysses all-to-alls alone (N > 1)")
     ap.add_argument("--clocks-csv-dir", default=None,
                     help="also write the raw nvidia-smi clock samples of the timed region to this folder")
     ap.add_argument("--op-breakdown", action="store_true",
@@ -1479,6 +1512,8 @@ def main() -> int:
     if args.only in ("glue", "sdxl", "variants", "rowq"):
         fn = {"glue": bench_glue, "sdxl": bench_sdxl, "variants": bench_variants, "rowq": bench_rowq}[args.only]
         return finish(fn(args, dev, peaks))
+    if args.only == "exchange":
+        return finish(bench_exchange(args, world, rank, dev))
     if args.only == "refgpu":
         return finish(bench_reference_gpu(args, dev))
     if args.only == "attention":
